@@ -1,0 +1,343 @@
+#!/usr/bin/env python
+"""Benchmark of the quantized decode GEMV (ZeroLlm QuantizedKernels.MatVecMulQ8_0 /
+ZeroTensor GgufDequantizer.GemvQ8_0) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: single Q8_0 linear 4096 x 4096 (out x in), x ~ N(0,1) fp32, W ~ N(0,0.02) quantized to Q8_0 in
+blocks of 32 with fp16 scales, y fp32 [4096].  One step = one GEMV over each of R = 16 distinct weight
+copies (286 MB in total, above the 126 MB L2, so every launch streams its weights from HBM).  At N > 1
+every rank runs the same workload on its own GPU (replicas: the GEMV has no cross-rank exchange), and
+`value` is the sum over ranks.
+
+Prints one JSON line (rank 0).  `value` is device-timed weight-stream throughput with everything resident;
+`e2e` is the same metric through the reference bridge entry zc_gemv_q8_0 with host (pinned) buffers, the
+weight and activation copies to the device and the result copy back inside the timed region.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "quant-matmul weight GB/s (% HBM peak); decode tokens/s at 1/2/4/8 B200"
+ROWS = COLS = 4096
+N_COPIES = 16
+QBYTES = ROWS * COLS + ROWS * (COLS // 32) * 2   # int8 values + fp16 scales streamed per launch
+ALGO_BYTES = QBYTES + COLS * 4 + ROWS * 4        # + x read + y written
+AOS_BYTES = ROWS * (COLS // 32) * 34             # the reference's packed weight bytes
+# Published CPU figure for this exact GEMV (ZeroTensor/README.md:198-203): 3.79 ms for the 17.8 MB weight.
+PUBLISHED_GBS = AOS_BYTES / 3.79e-3 / 1e9
+# dram__bytes_read.sum + dram__bytes_write.sum of one gemv_q8_0_kernel launch, from the ncu capture summarised
+# in profiles/gemv_q8_0_4096x4096.md (None until that capture exists).
+NCU_TRAFFIC_BYTES = None
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """Polls NVML (the data nvidia-smi prints) every 20 ms on a background thread."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting", 0x10: "sync_boost"}
+
+    def __init__(self, device_index: int):
+        self.samples, self.reasons, self.max_mhz, self.ok = [], set(), None, False
+        self._stop = threading.Event()
+        try:
+            import pynvml as N
+            N.nvmlInit()
+            h = None
+            try:
+                import torch
+                uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+                h = N.nvmlDeviceGetHandleByUUID(("GPU-" + uuid) if not uuid.startswith("GPU-") else uuid)
+            except Exception:
+                h = N.nvmlDeviceGetHandleByIndex(device_index)
+            self._N, self._h = N, h
+            self.max_mhz = N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.ok = False
+
+    def _run(self):
+        N, h = self._N, self._h
+        while not self._stop.is_set():
+            try:
+                self.samples.append(N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM))
+                r = N.nvmlDeviceGetCurrentClocksEventReasons(h)
+                for bit, name in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.02)
+
+    def __enter__(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.ok:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ----------------------------------------------------------------------------------------------------------
+# CPU legs (the oracle restates the reference's C# MatVecMulQ8_0; test infrastructure used only here)
+# ----------------------------------------------------------------------------------------------------------
+def _cpu_weights(n_copies, seed=1234):
+    import oracle as O
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal(COLS, dtype=np.float32)
+    ws = [O.quantize_q8_0(rng.standard_normal((ROWS, COLS), dtype=np.float32) * np.float32(0.02))
+          for _ in range(n_copies)]
+    return ws, x
+
+
+def cpu_baseline(seconds=10.0):
+    """Times the oracle's MatVecMulQ8_0 (AVX2 order, one row per task, all host threads) on a bounded sample."""
+    import oracle as O
+    ws, x = _cpu_weights(8)
+    y = np.empty(ROWS, np.float32)
+    O.matvec(8, ws[0], x, ROWS, COLS, threads=0)
+    calls, t0 = 0, time.perf_counter()
+    while True:
+        O.lib().orc_matvec_q8_0(ws[calls % 8].ctypes.data_as(O._u8p), x.ctypes.data_as(O._f32p),
+                                y.ctypes.data_as(O._f32p), ROWS, COLS, 0, 0)
+        calls += 1
+        el = time.perf_counter() - t0
+        if el >= seconds and calls >= 3:
+            break
+    gbs = calls * QBYTES / el / 1e9
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": O.lib().orc_num_threads(), "kind": "port",
+            "sample": f"{calls} calls of MatVecMulQ8_0 {ROWS}x{COLS} rotating 8 weight copies "
+                      f"({8 * AOS_BYTES / 1e6:.0f} MB) in {el:.1f} s"}
+
+
+def run_reference(args):
+    """`--impl reference`: the reference's CPU path (oracle restatement of the C#) on all host cores.
+    Each step is one MatVecMulQ8_0 call on the next of 8 rotating weight copies (143 MB, above the host LLC),
+    a bounded sample of the GPU arm's 16-copy step with the same per-byte metric."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import oracle as O
+    ws, x = _cpu_weights(8)
+    y = np.empty(ROWS, np.float32)
+
+    def step(i):
+        w = ws[i % 8]
+        O.lib().orc_matvec_q8_0(w.ctypes.data_as(O._u8p), x.ctypes.data_as(O._f32p), y.ctypes.data_as(O._f32p),
+                                ROWS, COLS, 0, 0)
+
+    for i in range(args.warmup):
+        step(i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        step(i)
+    el = time.perf_counter() - t0
+    gbs = args.steps * QBYTES / el / 1e9
+    cores = O.lib().orc_num_threads()
+    line = {"impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": round(gbs / PUBLISHED_GBS, 3),
+            "dtype": "int8xfp32", "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
+            "config": {"workload": f"q8_0_gemv_{ROWS}x{COLS}", "rows": ROWS, "cols": COLS, "weight_copies": 8,
+                       "parallelism": "host threads"},
+            "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+                             "sample": f"{args.steps} MatVecMulQ8_0 {ROWS}x{COLS} calls rotating 8 weight copies "
+                                       "(C++ restatement of the reference C#, AVX2 order, one row per task)"},
+            "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------------------------------------
+# GPU arm
+# ----------------------------------------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+
+    from zeroplatform_b200 import _lib
+    from zeroplatform_b200.ops import QuantizedWeight, quantize
+
+    L = _lib.lib()
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+    weights = []
+    for _ in range(N_COPIES):
+        w32 = torch.randn((ROWS, COLS), generator=gen, device=dev, dtype=torch.float32) * 0.02
+        weights.append(QuantizedWeight.upload(8, quantize(8, w32), ROWS, COLS, device=dev))
+        del w32
+    x = torch.randn(COLS, generator=gen, device=dev, dtype=torch.float32)
+    ys = torch.empty((N_COPIES, ROWS), device=dev, dtype=torch.float32)
+    stream = torch.cuda.Stream(device=dev)
+
+    def step():
+        for r, w in enumerate(weights):
+            rc = L.zcu_gemv_q8_0(w.qs.data_ptr(), w.d.data_ptr(), x.data_ptr(), ys[r].data_ptr(), ROWS, COLS, 0,
+                                 stream.cuda_stream)
+            if rc != 0:
+                raise RuntimeError(f"zcu_gemv_q8_0 failed: {rc}")
+
+    with torch.cuda.stream(stream):
+        step()  # sets kernel attributes outside capture
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    sampler = ClockSampler(local)
+    with sampler:
+        # warm-up: at least W steps and at least --min-warmup-s of load so the clock samples cover a busy GPU
+        t_w = time.perf_counter()
+        n_w = 0
+        while n_w < args.warmup or time.perf_counter() - t_w < args.min_warmup_s:
+            graph.replay()
+            n_w += 1
+            if n_w % 200 == 0:
+                stream.synchronize()
+        stream.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    launches = args.steps * N_COPIES
+    per_rank_gbs = launches * QBYTES / (ms * 1e-3) / 1e9
+    value = per_rank_gbs * world
+    launch_s = ms * 1e-3 / launches
+    achieved = ALGO_BYTES / launch_s / 1e9
+    peak, peak_kind = _peaks()
+
+    # End to end through the reference bridge entry (host buffers, copies inside the timed region).
+    e2e = None
+    try:
+        host_w = [torch.empty(AOS_BYTES, dtype=torch.uint8, pin_memory=True) for _ in range(N_COPIES)]
+        aos = torch.empty(AOS_BYTES, dtype=torch.uint8, device=dev)
+        for hw in host_w:
+            w32 = torch.randn((ROWS, COLS), generator=gen, device=dev, dtype=torch.float32) * 0.02
+            aos.copy_(quantize(8, w32).reshape(-1))
+            hw.copy_(aos)
+        hx = torch.empty(COLS, dtype=torch.float32, pin_memory=True)
+        hx.copy_(x)
+        hy = torch.empty(ROWS, dtype=torch.float32, pin_memory=True)
+        e2e_steps = max(2, min(args.steps, 10))
+
+        def e2e_step():
+            for hw in host_w:
+                rc = L.zc_gemv_q8_0(hw.data_ptr(), hx.data_ptr(), hy.data_ptr(), ROWS, COLS)
+                if rc != 0:
+                    raise RuntimeError(f"zc_gemv_q8_0 failed: {rc}")
+
+        for _ in range(2):
+            e2e_step()
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            e2e_step()
+        el = time.perf_counter() - t0
+        if world > 1:
+            t = torch.tensor([el], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            el = float(t.item())
+        e2e = {"value": round(e2e_steps * N_COPIES * QBYTES * world / el / 1e9, 3), "unit": "GB/s",
+               "h2d_bytes_per_step": N_COPIES * (AOS_BYTES + COLS * 4),
+               "d2h_bytes_per_step": N_COPIES * ROWS * 4,
+               "api": "zc_gemv_q8_0 (ZeroTensorNativeBridge ABI, pinned host buffers)",
+               "steps": e2e_steps}
+        del host_w
+    except Exception as ex:  # keep the device-timed line even if the e2e leg fails
+        e2e = {"value": None, "unit": "GB/s", "error": str(ex)[:200]}
+
+    cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu) else None
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+                "warmup": max(args.warmup, n_w), "ms_per_step": round(ms_per_step, 6), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": round(value / PUBLISHED_GBS, 2), "dtype": "int8xfp32",
+                "data": "synthetic (seeded N(0,0.02) weights quantized on device, N(0,1) activations)",
+                "config": {"workload": f"q8_0_gemv_{ROWS}x{COLS}", "rows": ROWS, "cols": COLS,
+                           "weight_copies": N_COPIES, "l2": "inputs larger than L2: 16 rotating weight copies, 286 MB",
+                           "parallelism": f"replicas x{world}", "graph": "one CUDA graph of 16 GEMV launches per step"},
+                "pct_hbm_peak": round(100.0 * per_rank_gbs / peak, 1),
+                "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                             "frac": round(achieved / peak, 3), "peak_source": peak_kind,
+                             "traffic": NCU_TRAFFIC_BYTES, "algorithmic_bytes_per_launch": ALGO_BYTES,
+                             "kernel": "gemv_q8_0_kernel", "launch_us": round(launch_s * 1e6, 3)},
+                "e2e": e2e, "gpu_launches": launches,
+                "clocks": sampler.summary(), "cpu_baseline": cpu}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--min-warmup-s", type=float, default=1.0,
+                    help="keep warming up for at least this long (clock samples under load)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,93 @@
+/*
+ * zero_tensor_cuda.h -- device-pointer extension of the ZeroTensor native bridge (libzero_tensor.so).
+ *
+ * The reference ABI in zero_tensor.h takes host pointers, so every call would copy its weights over
+ * PCIe.  These entry points take DEVICE pointers and a CUDA stream (cudaStream_t passed as void*;
+ * NULL = the legacy default stream) and only enqueue work: nothing here synchronises the host.
+ * The caller owns every buffer, as in the reference (ZeroTensorNativeBridge.cs:340-348 pins caller
+ * memory and never receives library memory).  Device buffers are what ZeroTensor exposes as
+ * DeviceMemoryStorage<T> with DeviceType.Cuda (ZeroTensor/src/ZeroTensor.Core/Storage/
+ * DeviceMemoryStorage.cs:20-110, Storage/DeviceType.cs:16): DeviceHandle is the CUdeviceptr passed here.
+ * Return codes as in zero_tensor.h (0 = success).
+ *
+ * Device weight layout ("SoA"), produced once per weight by zcu_q8_0_repack / zcu_q4_0_repack from the
+ * reference's packed GGML blocks (BlockQ8_0.cs:10-17, BlockQ4_0.cs:10-17):
+ *   Q8_0: qs  int8 [n_rows][k_cols]           d fp16 bits [n_rows][k_cols/32]
+ *   Q4_0: qs  uint8[n_rows][k_cols/32][16]    d fp16 bits [n_rows][k_cols/32]
+ *         (byte j of a block = element j in the low nibble, element j+16 in the high nibble)
+ * Device pointers must be 16-byte aligned (cudaMalloc gives 256).
+ */
+#ifndef ZERO_TENSOR_CUDA_H
+#define ZERO_TENSOR_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifndef ZC_API
+#if defined(__GNUC__)
+#define ZC_API __attribute__((visibility("default")))
+#else
+#define ZC_API
+#endif
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* fp32 [n] (n a multiple of 32, 16-byte aligned) -> packed GGML blocks, bit-identical to
+ * LlmQuantizer.QuantizeToQ8_0 / QuantizeToQ4_0 (ZeroLlm/src/ZeroLlm.Core/Quantization/LlmQuantizer.cs:20-57,
+ * BlockQ8_0.Quantize BlockQ8_0.cs:43-71, BlockQ4_0.Quantize BlockQ4_0.cs:120-150). */
+ZC_API int32_t zcu_quantize_q8_0(const float* src, uint8_t* blocks, size_t n, void* stream);
+ZC_API int32_t zcu_quantize_q4_0(const float* src, uint8_t* blocks, size_t n, void* stream);
+
+/* AoS GGML blocks (device) -> SoA device layout. Replaces nothing in the reference: the managed code
+ * streams the AoS blocks straight from the mmap (GgufFormat.cs:206-244); on the GPU the one-time
+ * repack makes every row 16-byte aligned for 128-bit streaming loads. */
+ZC_API int32_t zcu_q8_0_repack(const uint8_t* aos, int8_t* qs, uint16_t* d, size_t n_rows, size_t k_cols, void* stream);
+ZC_API int32_t zcu_q4_0_repack(const uint8_t* aos, uint8_t* qs, uint16_t* d, size_t n_rows, size_t k_cols, void* stream);
+
+/* Decode GEMV on device buffers.  accumulate == 0: y = W x -- QuantizedKernels.MatVecMulQ8_0 /
+ * MatVecMulQ4_0 (ZeroLlm/src/ZeroLlm.Core/Quantization/QuantizedKernels.cs:190-267);
+ * accumulate != 0: y += W x -- MatVecAddQ8_0 / MatVecAddQ4_0 (:272-349).  x[k_cols], y[n_rows] fp32. */
+ZC_API int32_t zcu_gemv_q8_0(const int8_t* qs, const uint16_t* d, const float* x, float* y, size_t n_rows, size_t k_cols,
+                      int32_t accumulate, void* stream);
+ZC_API int32_t zcu_gemv_q4_0(const uint8_t* qs, const uint16_t* d, const float* x, float* y, size_t n_rows, size_t k_cols,
+                      int32_t accumulate, void* stream);
+
+/* Paged decode attention on device buffers -- GqaAttention.Forward (ZeroLlm/src/ZeroLlm.Core/Layers/
+ * GqaAttention.cs:29-130) and TensorOps.PagedAttention (TensorOps.Neural.cs:2372-2476) for `batch`
+ * sequences with one query token each.
+ *   q, out        [batch][hq][hd] fp32
+ *   k_pool/v_pool element (page p, slot t, kv head h, dim e) at p*page_stride + t*slot_stride +
+ *                 h*head_stride + e (elements); kv_dtype 0 = fp32, 1 = fp16
+ *   page_table    [batch][max_pages] int32 physical page ids; ids outside [0, num_pages) are skipped
+ *   ctx_len       [batch] int32 tokens attended per sequence (the reference's per-layer causal length
+ *                 is the caller's choice of ctx_len; ctx_len 0 yields zeros, GqaAttention.cs:38-42)
+ *   max_ctx       an upper bound of ctx_len (sizes the split-K grid; the kernel reads ctx_len itself)
+ * Long contexts are split across CTAs; the split partials live in a library-owned workspace per
+ * (device, stream), so concurrent calls on one stream are ordered and calls on different streams do
+ * not share it. */
+ZC_API int32_t zcu_paged_attention(const float* q, const void* k_pool, const void* v_pool, int32_t kv_dtype,
+                            const int32_t* page_table, const int32_t* ctx_len, float* out, int32_t batch, int32_t hq,
+                            int32_t hkv, int32_t hd, int32_t page_size, int32_t max_pages, int32_t num_pages,
+                            int64_t page_stride, int64_t slot_stride, int64_t head_stride, float scale,
+                            int32_t max_ctx, void* stream);
+
+/* RmsNorm.Forward (Layers/RmsNorm.cs:14-59) on `rows` rows of n elements. */
+ZC_API int32_t zcu_rmsnorm(const float* x, const float* w, float* out, int32_t rows, int32_t n, float eps, void* stream);
+/* SwiGLU.Forward (Layers/SwiGLU.cs:13-51). */
+ZC_API int32_t zcu_swiglu(const float* gate, const float* up, float* out, size_t n, void* stream);
+/* RoPE.ApplyInplace (Layers/RoPE.cs:131-163) on x [rows][heads][hd] at positions pos[row] (pos == NULL:
+ * pos0 + row), with cos/sin tables [max_pos][hd/2] as RoPE.EnsureCache builds them (:83-125). */
+ZC_API int32_t zcu_rope(float* x, int32_t rows, int32_t heads, int32_t hd, const int32_t* pos, int32_t pos0,
+                 const float* cos_t, const float* sin_t, int32_t max_pos, void* stream);
+/* LlmEngine.LookupTokenEmbedding for a Q8_0 table in SoA layout (Engine/LlmEngine.cs:317-345):
+ * out[i] = dequantized row tokens[i] (ids outside [0, vocab) read row 0). */
+ZC_API int32_t zcu_embed_q8_0(const int8_t* qs, const uint16_t* d, const int32_t* tokens, int32_t n_tokens, int32_t vocab,
+                       int32_t dim, float* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

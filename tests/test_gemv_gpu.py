@@ -1,0 +1,123 @@
+"""Decode GEMV parity: CUDA (libzero_tensor.so) vs the CPU oracle on identical seeded inputs.
+
+Tolerance: max|y - y_oracle| / max|y_oracle| <= 1e-5.  Both sides accumulate fp32 products of the same
+exactly-dequantized weights; only the summation order differs (the north-star bound is 1e-3).
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from tests.conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-5
+
+SHAPES = [(1, 32), (3, 64), (17, 96), (1023, 768), (2304, 768), (4096, 4096), (768, 2048), (4096, 11008),
+          (11008, 4096), (257, 14336), (33, 20480)]
+
+
+def _case(qtype, rows, cols, seed):
+    rng = np.random.default_rng(seed)
+    w = (rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(0.02))
+    x = rng.standard_normal(cols, dtype=np.float32)
+    blocks = O.quantize_q8_0(w) if qtype == 8 else O.quantize_q4_0(w)
+    return blocks, x, rng
+
+
+@pytest.mark.parametrize("qtype", [8, 4])
+@pytest.mark.parametrize("rows,cols", SHAPES)
+def test_device_gemv_matches_oracle(qtype, rows, cols):
+    from zeroplatform_b200.ops import QuantizedWeight
+    blocks, x, rng = _case(qtype, rows, cols, rows * 131 + cols + qtype)
+    ref = O.matvec(qtype, blocks, x, rows, cols)
+    qw = QuantizedWeight.upload(qtype, blocks, rows, cols)
+    xd = torch.from_numpy(x).cuda()
+    y = qw.gemv(xd)
+    torch.cuda.synchronize()
+    assert rel_err(y.cpu().numpy(), ref) <= TOL
+    # MatVecAdd: y += W x
+    y0 = rng.standard_normal(rows, dtype=np.float32)
+    yt = torch.from_numpy(y0.copy()).cuda()
+    qw.gemv(xd, yt, accumulate=True)
+    ref_acc = O.matvec(qtype, blocks, x, rows, cols, y=y0.copy())
+    assert rel_err(yt.cpu().numpy(), ref_acc) <= TOL
+
+
+def test_repack_is_a_pure_relayout():
+    from zeroplatform_b200.ops import QuantizedWeight
+    blocks, _, _ = _case(8, 64, 256, 1)
+    qw = QuantizedWeight.upload(8, blocks, 64, 256)
+    b = blocks.reshape(64, 8, 34)
+    assert np.array_equal(qw.qs.cpu().numpy().view(np.uint8).reshape(64, 8, 32), b[:, :, 2:])
+    assert np.array_equal(qw.d.cpu().numpy().view(np.uint8).reshape(64, 8, 2), b[:, :, :2])
+    b4, _, _ = _case(4, 64, 256, 2)
+    q4 = QuantizedWeight.upload(4, b4, 64, 256)
+    b4 = b4.reshape(64, 8, 18)
+    assert np.array_equal(q4.qs.cpu().numpy().reshape(64, 8, 16), b4[:, :, 2:])
+    assert np.array_equal(q4.d.cpu().numpy().view(np.uint8).reshape(64, 8, 2), b4[:, :, :2])
+
+
+# ---- the reference bridge ABI with host buffers (NeuralOperatorsTests.cs:584-628 goldens) ---------------
+def test_bridge_gemv_q8_0_golden_192():
+    from zeroplatform_b200.ops import TensorBlas
+    blk = np.zeros(34, np.uint8)
+    blk[1] = 0x40
+    blk[2:] = 3
+    y = TensorBlas.gemv_q8_0(np.ones(32, np.float32), blk, 1, 32)
+    assert abs(y[0] - 192.0) < 1e-4
+
+
+def test_bridge_gemv_q4_0_golden_48():
+    from zeroplatform_b200.ops import TensorBlas
+    blk = np.zeros(18, np.uint8)
+    blk[1] = 0x3C
+    blk[2:] = 0x9A
+    y = TensorBlas.gemv_q4_0(np.ones(32, np.float32), blk, 1, 32)
+    assert abs(y[0] - 48.0) < 1e-4
+
+
+@pytest.mark.parametrize("qtype", [8, 4])
+@pytest.mark.parametrize("rows,cols", [(4096, 4096), (300, 11008), (5, 64)])
+def test_bridge_gemv_matches_oracle(qtype, rows, cols):
+    from zeroplatform_b200.ops import TensorBlas
+    blocks, x, _ = _case(qtype, rows, cols, 99 + rows)
+    ref = O.matvec(qtype, blocks, x, rows, cols)
+    fn = TensorBlas.gemv_q8_0 if qtype == 8 else TensorBlas.gemv_q4_0
+    assert rel_err(fn(x, blocks, rows, cols), ref) <= TOL
+
+
+def test_bridge_rejects_bad_k():
+    from zeroplatform_b200 import _lib
+    from zeroplatform_b200.ops import _np_ptr
+    x = np.ones(48, np.float32)
+    y = np.zeros(1, np.float32)
+    w = np.zeros(64, np.uint8)
+    assert _lib.lib().zc_gemv_q8_0(_np_ptr(w), _np_ptr(x), _np_ptr(y), 1, 48) == -2
+
+
+def test_bridge_is_reentrant_across_threads():
+    """LlmEngine.PrefillPrompt calls the kernels from Parallel.For workers (LlmEngine.cs:208)."""
+    import concurrent.futures as cf
+    from zeroplatform_b200.ops import TensorBlas
+    cases = [_case(8, 512, 768, s) for s in range(8)]
+    refs = [O.matvec(8, b, x, 512, 768) for b, x, _ in cases]
+    with cf.ThreadPoolExecutor(8) as ex:
+        outs = list(ex.map(lambda c: TensorBlas.gemv_q8_0(c[1], c[0], 512, 768), cases))
+    for o, r in zip(outs, refs):
+        assert rel_err(o, r) <= TOL
+
+
+@pytest.mark.parametrize("qtype", [8, 4])
+@pytest.mark.parametrize("scale", [0.02, 1.0, 1e-6, 300.0])
+def test_device_quantizer_bit_exact(qtype, scale):
+    """zcu_quantize_q*_0 vs LlmQuantizer (oracle): identical bytes, including all-zero and outlier blocks."""
+    from zeroplatform_b200.ops import quantize
+    rng = np.random.default_rng(int(scale * 1000) + qtype)
+    w = (rng.standard_normal((96, 512)) * scale).astype(np.float32)
+    w[0, :32] = 0.0
+    w[1, 7] = 9 * scale
+    w[2, 40] = -9 * scale
+    ref = O.quantize_q8_0(w) if qtype == 8 else O.quantize_q4_0(w)
+    got = quantize(qtype, torch.from_numpy(w).cuda()).cpu().numpy()
+    assert np.array_equal(got, ref)

@@ -1,0 +1,78 @@
+"""ctypes binding of libzero_tensor.so (the in-tree CUDA library).
+
+Loading fails loudly when the library has not been built: there is no CPU or
+PyTorch fallback anywhere in this package.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libzero_tensor.so")
+_lib = None
+
+sz = C.c_size_t
+i32 = C.c_int32
+i64 = C.c_int64
+vp = C.c_void_p
+f32 = C.c_float
+
+# Every exported symbol with its C signature (include/zero_tensor.h, include/zero_tensor_cuda.h).
+SIGNATURES = {
+    # reference bridge ABI (host pointers)
+    "zc_version": (C.c_uint32, []),
+    "zc_is_simd_supported": (i32, []),
+    "zc_gemm_f32": (i32, [sz, sz, sz, f32, vp, C.c_ssize_t, C.c_ssize_t, vp, C.c_ssize_t, C.c_ssize_t, f32, vp,
+                          C.c_ssize_t, C.c_ssize_t, i32]),
+    "zc_flash_attention_f32": (i32, [sz, sz, sz, sz, sz, f32, i32, sz, sz, sz, vp, vp, vp, vp, vp]),
+    "zc_gemv_q4_0": (i32, [vp, vp, vp, sz, sz]),
+    "zc_gemv_q8_0": (i32, [vp, vp, vp, sz, sz]),
+    "zc_rmsnorm_f32": (i32, [sz, vp, vp, vp, f32]),
+    "zc_silu_f32": (i32, [sz, vp, vp]),
+    "zc_swiglu_f32": (i32, [sz, vp, vp, vp]),
+    "zc_rope_f32": (i32, [sz, sz, sz, sz, f32, vp]),
+    "zc_paged_attention_f32": (i32, [sz, sz, sz, sz, sz, f32, vp, vp, vp, vp, vp]),
+    "zc_dot_i8": (i32, [sz, vp, vp, vp]),
+    "zc_cuda_last_error": (C.c_char_p, []),
+    # device-pointer extension
+    "zcu_quantize_q8_0": (i32, [vp, vp, sz, vp]),
+    "zcu_quantize_q4_0": (i32, [vp, vp, sz, vp]),
+    "zcu_q8_0_repack": (i32, [vp, vp, vp, sz, sz, vp]),
+    "zcu_q4_0_repack": (i32, [vp, vp, vp, sz, sz, vp]),
+    "zcu_gemv_q8_0": (i32, [vp, vp, vp, vp, sz, sz, i32, vp]),
+    "zcu_gemv_q4_0": (i32, [vp, vp, vp, vp, sz, sz, i32, vp]),
+    "zcu_paged_attention": (i32, [vp, vp, vp, i32, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, i64, i64, i64,
+                                  f32, i32, vp]),
+    "zcu_rmsnorm": (i32, [vp, vp, vp, i32, i32, f32, vp]),
+    "zcu_swiglu": (i32, [vp, vp, vp, sz, vp]),
+    "zcu_rope": (i32, [vp, i32, i32, i32, vp, i32, vp, vp, i32, vp]),
+    "zcu_embed_q8_0": (i32, [vp, vp, vp, i32, i32, i32, vp, vp]),
+}
+
+
+class ZcError(RuntimeError):
+    pass
+
+
+def lib():
+    """Load libzero_tensor.so (raises when it is missing)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ZcError(f"{LIB_PATH} is not built; run `python -m zeroplatform_b200.build` "
+                      "(this package has no CPU fallback)")
+    L = C.CDLL(LIB_PATH)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def check(rc: int, what: str = "") -> None:
+    if rc != 0:
+        msg = lib().zc_cuda_last_error().decode(errors="replace")
+        raise ZcError(f"{what} failed with status {rc}: {msg}")

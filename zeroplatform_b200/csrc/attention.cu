@@ -1,0 +1,311 @@
+// attention.cu -- paged-KV decode attention (one query token per sequence).
+//
+// Restates GqaAttention.Forward (ZeroLlm/src/ZeroLlm.Core/Layers/GqaAttention.cs:29-130) over a
+// KvSequenceView (Memory/PagedKvCache.cs:10-42), and the ZeroTensor operator
+// TensorOps.PagedAttention (ZeroTensor/src/ZeroTensor.Core/TensorOps.Neural.cs:2372-2476):
+//   out[h] = sum_t softmax_t(q[h] . K[t, h/group] * scale) * V[t, h/group],  t < ctx_len.
+// ctx_len == 0 gives zeros (GqaAttention.cs:38-42).  The reference's per-layer causal length
+// (non-final layers exclude the current token) is the caller's ctx_len choice.
+//
+// Design: one CTA per (query-head tile, sequence, split).  A query-head tile holds GT query heads
+// that share one KV head, so every K/V row is read once for the whole GQA group.  Inside a CTA,
+// LPT = hd/8 lanes cooperate on one token (each lane owns 8 dims and issues one 16-byte load per
+// K or V row for fp16 pools), 4 token passes are kept in flight per warp, scores go through a
+// shuffle reduction over the LPT lanes, and each token group keeps an online-softmax state
+// (max, sum, accumulator) in the exp2 domain.  Token groups merge in shared memory.  Long
+// contexts are split across CTAs (flash-decoding); the last CTA of a (sequence, head tile) to
+// finish -- found with an atomic arrival counter, no waiting -- merges the split partials.
+// Roofline: HBM, bytes = 2 * ctx * hkv * hd * sizeof(kv) per sequence + q/out.
+
+#include <math.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace zc {
+
+namespace {
+
+constexpr int ATT_WARPS = 4;
+constexpr int ATT_THREADS = ATT_WARPS * 32;
+constexpr int ATT_UNROLL = 4;
+constexpr float LOG2E = 1.4426950408889634f;
+
+template <typename KV>
+__device__ __forceinline__ void load8(const KV* p, float (&f)[8]);
+
+template <>
+__device__ __forceinline__ void load8<__half>(const __half* p, float (&f)[8]) {
+  int4 r = ld_stream_v4(p);
+  const __half2* h = reinterpret_cast<const __half2*>(&r);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 v = __half22float2(h[i]);
+    f[2 * i] = v.x;
+    f[2 * i + 1] = v.y;
+  }
+}
+
+template <>
+__device__ __forceinline__ void load8<float>(const float* p, float (&f)[8]) {
+  int4 a = ld_stream_v4(p);
+  int4 b = ld_stream_v4(p + 4);
+  f[0] = __int_as_float(a.x);
+  f[1] = __int_as_float(a.y);
+  f[2] = __int_as_float(a.z);
+  f[3] = __int_as_float(a.w);
+  f[4] = __int_as_float(b.x);
+  f[5] = __int_as_float(b.y);
+  f[6] = __int_as_float(b.z);
+  f[7] = __int_as_float(b.w);
+}
+
+struct AttnDev {
+  const float* q;
+  const void* k_pool;
+  const void* v_pool;
+  const int32_t* page_table;
+  const int32_t* ctx_len;
+  float* out;
+  float* ws;
+  int* counters;
+  int hq, group, page_size, max_pages, num_pages;
+  long long page_stride, slot_stride, head_stride;
+  float scale_log2;
+};
+
+template <int HD, typename KV, int GT>
+__global__ void __launch_bounds__(ATT_THREADS) paged_attn_kernel(AttnDev a) {
+  constexpr int LPT = HD / 8;        // lanes per token
+  constexpr int TPW = 32 / LPT;      // tokens per warp pass
+  constexpr int NG = ATT_WARPS * TPW;  // token groups per CTA
+  __shared__ float sm_m[NG][GT];
+  __shared__ float sm_l[NG][GT];
+  __shared__ float sm_acc[NG][GT][HD];
+  __shared__ int s_last;
+
+  const int split = blockIdx.x, tile = blockIdx.y, b = blockIdx.z;
+  const int splits = gridDim.x, tiles = gridDim.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tg = lane / LPT, sub = lane % LPT;
+  const int qh0 = tile * GT;
+  const int kvh = qh0 / a.group;
+  const int ctx = max(0, a.ctx_len[b]);
+  const int P = a.page_size;
+  const int n_pages = (ctx + P - 1) / P;
+  const int pps = (n_pages + splits - 1) / splits;
+  const int t_begin = min(ctx, split * pps * P);
+  const int t_end = min(ctx, (split + 1) * pps * P);
+  const int32_t* pt = a.page_table + (size_t)b * a.max_pages;
+  const KV* kp = reinterpret_cast<const KV*>(a.k_pool);
+  const KV* vp = reinterpret_cast<const KV*>(a.v_pool);
+
+  float q[GT][8], m[GT], l[GT], acc[GT][8];
+#pragma unroll
+  for (int g = 0; g < GT; ++g) {
+    const float* qg = a.q + ((size_t)b * a.hq + qh0 + g) * HD + 8 * sub;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      q[g][e] = qg[e] * a.scale_log2;
+      acc[g][e] = 0.f;
+    }
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+  }
+
+  for (int t0 = t_begin + warp * TPW * ATT_UNROLL; t0 < t_end; t0 += ATT_WARPS * TPW * ATT_UNROLL) {
+    float kf[ATT_UNROLL][8], vf[ATT_UNROLL][8];
+    bool valid[ATT_UNROLL];
+#pragma unroll
+    for (int u = 0; u < ATT_UNROLL; ++u) {
+      const int t = t0 + u * TPW + tg;
+      const int lp = t / P;
+      int page = (t < t_end && lp < a.max_pages) ? pt[lp] : -1;
+      valid[u] = page >= 0 && page < a.num_pages;  // out-of-range page ids are never dereferenced
+      if (valid[u]) {
+        const long long off = page * a.page_stride + (long long)(t % P) * a.slot_stride +
+                              (long long)kvh * a.head_stride + 8 * sub;
+        load8<KV>(kp + off, kf[u]);
+        load8<KV>(vp + off, vf[u]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) kf[u][e] = vf[u][e] = 0.f;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < ATT_UNROLL; ++u) {
+#pragma unroll
+      for (int g = 0; g < GT; ++g) {
+        float s = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) s = fmaf(q[g][e], kf[u][e], s);
+#pragma unroll
+        for (int o = LPT / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (valid[u]) {
+          const float mn = fmaxf(m[g], s);
+          const float alpha = exp2f(m[g] - mn);
+          const float p = exp2f(s - mn);
+          l[g] = l[g] * alpha + p;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[g][e] = fmaf(p, vf[u][e], acc[g][e] * alpha);
+          m[g] = mn;
+        }
+      }
+    }
+  }
+
+  const int gi = warp * TPW + tg;
+#pragma unroll
+  for (int g = 0; g < GT; ++g) {
+    if (sub == 0) {
+      sm_m[gi][g] = m[g];
+      sm_l[gi][g] = l[g];
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) sm_acc[gi][g][8 * sub + e] = acc[g][e];
+  }
+  __syncthreads();
+
+  for (int it = threadIdx.x; it < GT * HD; it += ATT_THREADS) {
+    const int g = it / HD, e = it % HD;
+    float M = -INFINITY;
+    for (int i = 0; i < NG; ++i) M = fmaxf(M, sm_m[i][g]);
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+      for (int i = 0; i < NG; ++i) {
+        const float mi = sm_m[i][g];
+        if (mi == -INFINITY) continue;
+        const float w = exp2f(mi - M);
+        L = fmaf(sm_l[i][g], w, L);
+        O = fmaf(sm_acc[i][g][e], w, O);
+      }
+    }
+    const size_t head = (size_t)b * a.hq + qh0 + g;
+    if (splits == 1) {
+      a.out[head * HD + e] = L > 0.f ? O / L : 0.f;
+    } else {
+      float* ws = a.ws + (head * splits + split) * (HD + 2);
+      ws[e] = O;
+      if (e == 0) {
+        ws[HD] = M;
+        ws[HD + 1] = L;
+      }
+    }
+  }
+  if (splits == 1) return;
+
+  // Split-K merge by the last CTA of this (sequence, head tile) to arrive.
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int* ctr = a.counters + (size_t)b * tiles + tile;
+    s_last = (atomicAdd(ctr, 1) == splits - 1);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int it = threadIdx.x; it < GT * HD; it += ATT_THREADS) {
+    const int g = it / HD, e = it % HD;
+    const size_t head = (size_t)b * a.hq + qh0 + g;
+    const float* ws = a.ws + head * splits * (HD + 2);
+    float M = -INFINITY;
+    for (int s = 0; s < splits; ++s) M = fmaxf(M, __ldcg(ws + s * (HD + 2) + HD));
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+      for (int s = 0; s < splits; ++s) {
+        const float ms = __ldcg(ws + s * (HD + 2) + HD);
+        if (ms == -INFINITY) continue;
+        const float w = exp2f(ms - M);
+        L = fmaf(__ldcg(ws + s * (HD + 2) + HD + 1), w, L);
+        O = fmaf(__ldcg(ws + s * (HD + 2) + e), w, O);
+      }
+    }
+    a.out[head * HD + e] = L > 0.f ? O / L : 0.f;
+  }
+  if (threadIdx.x == 0) a.counters[(size_t)b * tiles + tile] = 0;  // ready for the next call
+}
+
+template <int HD, typename KV>
+int launch_hd(const AttnDev& d, int batch, int tiles_gt, int gt, int splits, cudaStream_t s) {
+  dim3 grid(splits, tiles_gt, batch);
+  switch (gt) {
+    case 1: paged_attn_kernel<HD, KV, 1><<<grid, ATT_THREADS, 0, s>>>(d); break;
+    case 2: paged_attn_kernel<HD, KV, 2><<<grid, ATT_THREADS, 0, s>>>(d); break;
+    case 4: paged_attn_kernel<HD, KV, 4><<<grid, ATT_THREADS, 0, s>>>(d); break;
+    case 8: paged_attn_kernel<HD, KV, 8><<<grid, ATT_THREADS, 0, s>>>(d); break;
+    default: return kUnsupported;
+  }
+  return cudaPeekAtLastError() == cudaSuccess ? kOk : kCudaError;
+}
+
+template <typename KV>
+int launch_kv(const AttnDev& d, int hd, int batch, int tiles_gt, int gt, int splits, cudaStream_t s) {
+  switch (hd) {
+    case 8: return launch_hd<8, KV>(d, batch, tiles_gt, gt, splits, s);
+    case 16: return launch_hd<16, KV>(d, batch, tiles_gt, gt, splits, s);
+    case 32: return launch_hd<32, KV>(d, batch, tiles_gt, gt, splits, s);
+    case 64: return launch_hd<64, KV>(d, batch, tiles_gt, gt, splits, s);
+    case 128: return launch_hd<128, KV>(d, batch, tiles_gt, gt, splits, s);
+    case 256: return launch_hd<256, KV>(d, batch, tiles_gt, gt, splits, s);
+    default: return kUnsupported;
+  }
+}
+
+}  // namespace
+
+size_t paged_attention_workspace_floats(int batch, int hq, int hd, int splits) {
+  return splits <= 1 ? 0 : (size_t)batch * hq * splits * (hd + 2);
+}
+
+int paged_attention_choose_splits(int batch, int hkv, int max_ctx, int page_size) {
+  if (max_ctx <= 0 || page_size <= 0) return 1;
+  const int n_pages = (max_ctx + page_size - 1) / page_size;
+  const int ctas = batch * hkv;
+  const int want = (2 * 148 + ctas - 1) / ctas;  // about two CTAs per SM
+  int splits = want < 1 ? 1 : want;
+  if (splits > n_pages) splits = n_pages;
+  if (splits > 64) splits = 64;
+  return splits < 1 ? 1 : splits;
+}
+
+int paged_attention(const PagedAttnArgs& a, cudaStream_t s) {
+  if (!a.q || !a.k_pool || !a.v_pool || !a.page_table || !a.ctx_len || !a.out) return kBadArgument;
+  if (a.batch <= 0 || a.hq <= 0 || a.hkv <= 0 || a.hq % a.hkv || a.page_size <= 0 || a.max_pages <= 0)
+    return kBadArgument;
+  const int elem = a.kv_half ? 2 : 4;
+  const long long vec = 16 / elem;  // elements per 16-byte load
+  if (a.page_stride % vec || a.slot_stride % vec || a.head_stride % vec) return kUnsupported;
+  if ((reinterpret_cast<uintptr_t>(a.k_pool) | reinterpret_cast<uintptr_t>(a.v_pool)) & 15) return kUnsupported;
+  const int group = a.hq / a.hkv;
+  int gt = 1;
+  for (int c : {8, 4, 2})
+    if (group % c == 0) {
+      gt = c;
+      break;
+    }
+  int splits = a.splits > 0 ? a.splits : paged_attention_choose_splits(a.batch, a.hkv, a.max_ctx, a.page_size);
+  if (splits > 1 && (!a.workspace || !a.counters)) splits = 1;
+  AttnDev d;
+  d.q = a.q;
+  d.k_pool = a.k_pool;
+  d.v_pool = a.v_pool;
+  d.page_table = a.page_table;
+  d.ctx_len = a.ctx_len;
+  d.out = a.out;
+  d.ws = a.workspace;
+  d.counters = a.counters;
+  d.hq = a.hq;
+  d.group = group;
+  d.page_size = a.page_size;
+  d.max_pages = a.max_pages;
+  d.num_pages = a.num_pages > 0 ? a.num_pages : 0x7fffffff;
+  d.page_stride = a.page_stride;
+  d.slot_stride = a.slot_stride;
+  d.head_stride = a.head_stride;
+  d.scale_log2 = a.scale * LOG2E;
+  const int tiles = a.hq / gt;
+  return a.kv_half ? launch_kv<__half>(d, a.hd, a.batch, tiles, gt, splits, s)
+                   : launch_kv<float>(d, a.hd, a.batch, tiles, gt, splits, s);
+}
+
+}  // namespace zc

@@ -1,0 +1,513 @@
+// capi.cu -- extern "C" entry points of libzero_tensor.so (declared in include/zero_tensor.h and
+// include/zero_tensor_cuda.h).
+//
+// Host-pointer entries (zc_*) follow the ZeroTensor native-bridge contract
+// (ZeroTensor/src/ZeroTensor.Core/Native/ZeroTensorNativeBridge.cs:93-389): synchronous, caller-owned
+// host buffers, 0 = handled.  Each host thread gets its own non-blocking CUDA stream and grow-only
+// device staging buffers per device, so concurrent callers (Parallel.For workers) never share state.
+// Device-pointer entries (zcu_*) only enqueue work on the caller's stream.
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <utility>
+#include <vector>
+
+#include "../../include/zero_tensor.h"
+#include "../../include/zero_tensor_cuda.h"
+#include "common.cuh"
+#include "kernels.h"
+
+namespace {
+
+using namespace zc;
+
+thread_local std::string t_last_error;
+
+int fail(int code, const char* what) {
+  t_last_error = what;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  char buf[256];
+  std::snprintf(buf, sizeof(buf), "%s: %s", what, cudaGetErrorString(e));
+  t_last_error = buf;
+  return kCudaError;
+}
+
+#define ZC_CUDA(call)                                   \
+  do {                                                  \
+    cudaError_t e_ = (call);                            \
+    if (e_ != cudaSuccess) return cuda_fail(e_, #call); \
+  } while (0)
+
+#define ZC_RC(call)                                              \
+  do {                                                           \
+    int rc_ = (call);                                            \
+    if (rc_ != kOk) {                                            \
+      if (t_last_error.empty()) t_last_error = #call " failed"; \
+      return rc_;                                                \
+    }                                                            \
+  } while (0)
+
+// Per-thread, per-device staging context for the host-pointer entries.  Contexts live until the process
+// exits (the driver releases their memory); freeing them from thread-exit destructors could run after
+// the CUDA runtime has been torn down.
+struct HostCtx {
+  int device = -1;
+  cudaStream_t stream = nullptr;
+  void* buf[8] = {};
+  size_t cap[8] = {};
+};
+thread_local std::vector<HostCtx*> t_ctx;
+
+int host_ctx(HostCtx** out) {
+  int dev = 0;
+  ZC_CUDA(cudaGetDevice(&dev));
+  for (HostCtx* c : t_ctx)
+    if (c->device == dev) {
+      *out = c;
+      return kOk;
+    }
+  HostCtx* c = new HostCtx();
+  c->device = dev;
+  ZC_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+  t_ctx.push_back(c);
+  *out = c;
+  return kOk;
+}
+
+int staging(HostCtx* c, int slot, size_t bytes, void** p) {
+  if (bytes == 0) bytes = 16;
+  if (c->cap[slot] < bytes) {
+    if (c->buf[slot]) {
+      ZC_CUDA(cudaStreamSynchronize(c->stream));
+      ZC_CUDA(cudaFree(c->buf[slot]));
+      c->buf[slot] = nullptr;
+      c->cap[slot] = 0;
+    }
+    size_t cap = std::max(bytes, c->cap[slot] * 2);
+    if (cudaMalloc(&c->buf[slot], cap) != cudaSuccess) {
+      cudaGetLastError();
+      return fail(kOutOfMemory, "device staging allocation failed");
+    }
+    c->cap[slot] = cap;
+  }
+  *p = c->buf[slot];
+  return kOk;
+}
+
+int finish(HostCtx* c) {
+  ZC_CUDA(cudaGetLastError());
+  ZC_CUDA(cudaStreamSynchronize(c->stream));
+  return kOk;
+}
+
+// Split-K workspace of the paged attention, one per (device, stream).  The arrival counters are zeroed
+// when allocated and every launch leaves them zeroed.
+struct AttnWs {
+  float* ws = nullptr;
+  size_t ws_floats = 0;
+  int* ctr = nullptr;
+  size_t ctr_n = 0;
+};
+std::mutex g_ws_mu;
+std::map<std::pair<int, cudaStream_t>, AttnWs> g_ws;
+
+int attn_workspace(cudaStream_t s, size_t floats, size_t counters, float** ws, int** ctr) {
+  int dev = 0;
+  ZC_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> g(g_ws_mu);
+  AttnWs& w = g_ws[{dev, s}];
+  if (w.ws_floats < floats) {
+    if (w.ws) {
+      ZC_CUDA(cudaStreamSynchronize(s));
+      ZC_CUDA(cudaFree(w.ws));
+      w.ws = nullptr;
+      w.ws_floats = 0;
+    }
+    if (cudaMalloc(&w.ws, floats * sizeof(float)) != cudaSuccess) {
+      cudaGetLastError();
+      return fail(kOutOfMemory, "attention workspace allocation failed");
+    }
+    w.ws_floats = floats;
+  }
+  if (w.ctr_n < counters) {
+    if (w.ctr) {
+      ZC_CUDA(cudaStreamSynchronize(s));
+      ZC_CUDA(cudaFree(w.ctr));
+      w.ctr = nullptr;
+      w.ctr_n = 0;
+    }
+    if (cudaMalloc(&w.ctr, counters * sizeof(int)) != cudaSuccess) {
+      cudaGetLastError();
+      return fail(kOutOfMemory, "attention counter allocation failed");
+    }
+    ZC_CUDA(cudaMemsetAsync(w.ctr, 0, counters * sizeof(int), s));
+    w.ctr_n = counters;
+  }
+  *ws = w.ws;
+  *ctr = w.ctr;
+  return kOk;
+}
+
+int attention_device(const PagedAttnArgs& in, cudaStream_t s) {
+  PagedAttnArgs a = in;
+  int splits = paged_attention_choose_splits(a.batch, a.hkv, a.max_ctx, a.page_size);
+  a.splits = splits;
+  a.workspace = nullptr;
+  a.counters = nullptr;
+  if (splits > 1) {
+    ZC_RC(attn_workspace(s, paged_attention_workspace_floats(a.batch, a.hq, a.hd, splits),
+                         (size_t)a.batch * a.hq, &a.workspace, &a.counters));
+  }
+  return paged_attention(a, s);
+}
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+int gemv_host(int qtype, const uint8_t* w, const float* x, float* y, size_t n, size_t k) {
+  if (!w || !x || !y) return fail(kBadArgument, "null pointer");
+  if (k == 0 || k % QK) return fail(kBadArgument, "k_cols must be a positive multiple of 32");
+  if (n == 0) return kOk;
+  if (n > 0x7fffffff || k > 0x7fffffff) return fail(kUnsupported, "dimension too large");
+  HostCtx* c = nullptr;
+  ZC_RC(host_ctx(&c));
+  const size_t nb = n * (k / QK);
+  const size_t aos_bytes = nb * (qtype == 8 ? Q8_BLOCK_BYTES : Q4_BLOCK_BYTES);
+  const size_t qs_bytes = qtype == 8 ? n * k : n * k / 2;
+  void *d_aos, *d_qs, *d_d, *d_x, *d_y;
+  ZC_RC(staging(c, 0, aos_bytes, &d_aos));
+  ZC_RC(staging(c, 1, qs_bytes, &d_qs));
+  ZC_RC(staging(c, 2, nb * 2, &d_d));
+  ZC_RC(staging(c, 3, k * sizeof(float), &d_x));
+  ZC_RC(staging(c, 4, n * sizeof(float), &d_y));
+  ZC_CUDA(cudaMemcpyAsync(d_aos, w, aos_bytes, cudaMemcpyHostToDevice, c->stream));
+  ZC_CUDA(cudaMemcpyAsync(d_x, x, k * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+  if (qtype == 8) {
+    ZC_RC(repack_q8_0((const uint8_t*)d_aos, (int8_t*)d_qs, (uint16_t*)d_d, n, k, c->stream));
+    ZC_RC(gemv_q8_0((const int8_t*)d_qs, (const uint16_t*)d_d, (const float*)d_x, (float*)d_y, (int)n, (int)k, 0,
+                    c->stream));
+  } else {
+    ZC_RC(repack_q4_0((const uint8_t*)d_aos, (uint8_t*)d_qs, (uint16_t*)d_d, n, k, c->stream));
+    ZC_RC(gemv_q4_0((const uint8_t*)d_qs, (const uint16_t*)d_d, (const float*)d_x, (float*)d_y, (int)n, (int)k, 0,
+                    c->stream));
+  }
+  ZC_CUDA(cudaMemcpyAsync(y, d_y, n * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+  return finish(c);
+}
+
+}  // namespace
+
+extern "C" {
+
+// ------------------------------------------------------------------------------------------
+// Reference bridge ABI (include/zero_tensor.h)
+// ------------------------------------------------------------------------------------------
+uint32_t zc_version(void) { return (0u << 16) | (1u << 8) | 0u; }
+
+int32_t zc_is_simd_supported(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+    cudaGetLastError();
+    return 0;
+  }
+  int dev = 0, major = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return major == 10 ? 1 : 0;
+}
+
+const char* zc_cuda_last_error(void) { return t_last_error.c_str(); }
+
+int32_t zc_gemv_q8_0(const uint8_t* w, const float* x, float* y, size_t n_rows, size_t k_cols) {
+  t_last_error.clear();
+  return gemv_host(8, w, x, y, n_rows, k_cols);
+}
+
+int32_t zc_gemv_q4_0(const uint8_t* w, const float* x, float* y, size_t n_rows, size_t k_cols) {
+  t_last_error.clear();
+  return gemv_host(4, w, x, y, n_rows, k_cols);
+}
+
+int32_t zc_gemm_f32(size_t m, size_t n, size_t k, float alpha, const float* a, intptr_t rsa, intptr_t csa,
+                    const float* b, intptr_t rsb, intptr_t csb, float beta, float* c, intptr_t rsc, intptr_t csc,
+                    int32_t parallel) {
+  (void)parallel;
+  t_last_error.clear();
+  if (!a || !b || !c) return fail(kBadArgument, "null pointer");
+  if (m == 0 || n == 0) return kOk;
+  if (m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff) return fail(kUnsupported, "dimension too large");
+  HostCtx* cx = nullptr;
+  ZC_RC(host_ctx(&cx));
+  // Pack the strided operands row-major on the host, run the GEMM, scatter C back.
+  std::vector<float> ha(m * k), hb(k * n), hc(m * n);
+  for (size_t i = 0; i < m; ++i)
+    for (size_t p = 0; p < k; ++p) ha[i * k + p] = a[(intptr_t)i * rsa + (intptr_t)p * csa];
+  for (size_t p = 0; p < k; ++p)
+    for (size_t j = 0; j < n; ++j) hb[p * n + j] = b[(intptr_t)p * rsb + (intptr_t)j * csb];
+  if (beta != 0.f)
+    for (size_t i = 0; i < m; ++i)
+      for (size_t j = 0; j < n; ++j) hc[i * n + j] = c[(intptr_t)i * rsc + (intptr_t)j * csc];
+  void *da, *db, *dc;
+  ZC_RC(staging(cx, 0, ha.size() * 4, &da));
+  ZC_RC(staging(cx, 1, hb.size() * 4, &db));
+  ZC_RC(staging(cx, 2, hc.size() * 4, &dc));
+  ZC_CUDA(cudaMemcpyAsync(da, ha.data(), ha.size() * 4, cudaMemcpyHostToDevice, cx->stream));
+  ZC_CUDA(cudaMemcpyAsync(db, hb.data(), hb.size() * 4, cudaMemcpyHostToDevice, cx->stream));
+  if (beta != 0.f) ZC_CUDA(cudaMemcpyAsync(dc, hc.data(), hc.size() * 4, cudaMemcpyHostToDevice, cx->stream));
+  ZC_RC(sgemm((int)m, (int)n, (int)k, alpha, (const float*)da, (const float*)db, beta, (float*)dc, cx->stream));
+  ZC_CUDA(cudaMemcpyAsync(hc.data(), dc, hc.size() * 4, cudaMemcpyDeviceToHost, cx->stream));
+  ZC_RC(finish(cx));
+  for (size_t i = 0; i < m; ++i)
+    for (size_t j = 0; j < n; ++j) c[(intptr_t)i * rsc + (intptr_t)j * csc] = hc[i * n + j];
+  return kOk;
+}
+
+int32_t zc_flash_attention_f32(size_t, size_t, size_t, size_t, size_t, float, int32_t, size_t, size_t, size_t,
+                               const float*, const float*, const float*, const float*, float*) {
+  t_last_error = "zc_flash_attention_f32: prefill attention is not provided by this library";
+  return kNotHandled;
+}
+
+int32_t zc_rmsnorm_f32(size_t n, const float* x, const float* w, float* dst, float eps) {
+  t_last_error.clear();
+  if (!x || !w || !dst) return fail(kBadArgument, "null pointer");
+  if (n == 0) return kOk;
+  if (n > 0x7fffffff) return fail(kUnsupported, "dimension too large");
+  HostCtx* c = nullptr;
+  ZC_RC(host_ctx(&c));
+  void *dx, *dw, *dy;
+  ZC_RC(staging(c, 0, n * 4, &dx));
+  ZC_RC(staging(c, 1, n * 4, &dw));
+  ZC_RC(staging(c, 2, n * 4, &dy));
+  ZC_CUDA(cudaMemcpyAsync(dx, x, n * 4, cudaMemcpyHostToDevice, c->stream));
+  ZC_CUDA(cudaMemcpyAsync(dw, w, n * 4, cudaMemcpyHostToDevice, c->stream));
+  ZC_RC(rmsnorm((const float*)dx, (const float*)dw, (float*)dy, 1, (int)n, eps, c->stream));
+  ZC_CUDA(cudaMemcpyAsync(dst, dy, n * 4, cudaMemcpyDeviceToHost, c->stream));
+  return finish(c);
+}
+
+static int32_t unary_host(size_t n, const float* a, const float* b, float* dst, int op) {
+  t_last_error.clear();
+  if (!a || !dst || (op == 1 && !b)) return fail(kBadArgument, "null pointer");
+  if (n == 0) return kOk;
+  HostCtx* c = nullptr;
+  ZC_RC(host_ctx(&c));
+  void *da, *db, *dy;
+  ZC_RC(staging(c, 0, n * 4, &da));
+  ZC_RC(staging(c, 1, n * 4, &db));
+  ZC_RC(staging(c, 2, n * 4, &dy));
+  ZC_CUDA(cudaMemcpyAsync(da, a, n * 4, cudaMemcpyHostToDevice, c->stream));
+  if (op == 1) {
+    ZC_CUDA(cudaMemcpyAsync(db, b, n * 4, cudaMemcpyHostToDevice, c->stream));
+    ZC_RC(swiglu((const float*)da, (const float*)db, (float*)dy, n, c->stream));
+  } else {
+    ZC_RC(silu((const float*)da, (float*)dy, n, c->stream));
+  }
+  ZC_CUDA(cudaMemcpyAsync(dst, dy, n * 4, cudaMemcpyDeviceToHost, c->stream));
+  return finish(c);
+}
+
+int32_t zc_silu_f32(size_t n, const float* src, float* dst) { return unary_host(n, src, nullptr, dst, 0); }
+
+int32_t zc_swiglu_f32(size_t n, const float* gate, const float* up, float* dst) {
+  return unary_host(n, gate, up, dst, 1);
+}
+
+int32_t zc_rope_f32(size_t num_heads, size_t seq_len, size_t head_dim, size_t pos_offset, float theta_base,
+                    float* x) {
+  t_last_error.clear();
+  if (!x) return fail(kBadArgument, "null pointer");
+  if (head_dim == 0 || (head_dim & 1)) return fail(kBadArgument, "head_dim must be even");
+  const size_t n = num_heads * seq_len * head_dim;
+  if (n == 0) return kOk;
+  HostCtx* c = nullptr;
+  ZC_RC(host_ctx(&c));
+  void* dx;
+  ZC_RC(staging(c, 0, n * 4, &dx));
+  ZC_CUDA(cudaMemcpyAsync(dx, x, n * 4, cudaMemcpyHostToDevice, c->stream));
+  ZC_RC(rope_tensorops((float*)dx, (int)num_heads, (int)seq_len, (int)head_dim, (int)pos_offset, theta_base,
+                       c->stream));
+  ZC_CUDA(cudaMemcpyAsync(x, dx, n * 4, cudaMemcpyDeviceToHost, c->stream));
+  return finish(c);
+}
+
+int32_t zc_paged_attention_f32(size_t hq, size_t hkv, size_t hd, size_t block_size, size_t ctx_len, float scale,
+                               const float* q, const float* k_cache, const float* v_cache, const int32_t* block_table,
+                               float* out) {
+  t_last_error.clear();
+  if (!q || !out) return fail(kBadArgument, "null pointer");
+  if (hq == 0 || hkv == 0 || hq % hkv || hd == 0 || block_size == 0) return fail(kBadArgument, "bad head geometry");
+  if (hq > 4096 || hd > 4096 || block_size > 65536 || ctx_len > (1u << 28))
+    return fail(kUnsupported, "dimension too large");
+  if (ctx_len > 0 && (!k_cache || !v_cache || !block_table)) return fail(kBadArgument, "null pointer");
+  HostCtx* c = nullptr;
+  ZC_RC(host_ctx(&c));
+  const size_t nlb = (ctx_len + block_size - 1) / block_size;
+  const size_t blk_floats = block_size * hkv * hd;
+  // Gather the referenced blocks into a compact device pool (logical order), so that only the pages
+  // the table names cross PCIe; the ABI does not carry the pool's extent.
+  int32_t max_id = -1;
+  for (size_t i = 0; i < nlb; ++i) {
+    if (block_table[i] < 0) return fail(kBadArgument, "negative block id");
+    max_id = std::max(max_id, block_table[i]);
+  }
+  void *dq, *dk, *dv, *dpt, *dctx, *dout;
+  ZC_RC(staging(c, 0, hq * hd * 4, &dq));
+  ZC_RC(staging(c, 1, std::max<size_t>(nlb, 1) * blk_floats * 4, &dk));
+  ZC_RC(staging(c, 2, std::max<size_t>(nlb, 1) * blk_floats * 4, &dv));
+  ZC_RC(staging(c, 3, std::max<size_t>(nlb, 1) * 4 + 4, &dpt));
+  ZC_RC(staging(c, 4, 16, &dctx));
+  ZC_RC(staging(c, 5, hq * hd * 4, &dout));
+  std::vector<int32_t> ident(std::max<size_t>(nlb, 1));
+  for (size_t i = 0; i < ident.size(); ++i) ident[i] = (int32_t)i;
+  const int32_t ctx32 = (int32_t)ctx_len;
+  ZC_CUDA(cudaMemcpyAsync(dq, q, hq * hd * 4, cudaMemcpyHostToDevice, c->stream));
+  for (size_t i = 0; i < nlb; ++i) {
+    const size_t src = (size_t)block_table[i] * blk_floats;
+    ZC_CUDA(cudaMemcpyAsync((float*)dk + i * blk_floats, k_cache + src, blk_floats * 4, cudaMemcpyHostToDevice,
+                            c->stream));
+    ZC_CUDA(cudaMemcpyAsync((float*)dv + i * blk_floats, v_cache + src, blk_floats * 4, cudaMemcpyHostToDevice,
+                            c->stream));
+  }
+  ZC_CUDA(cudaMemcpyAsync(dpt, ident.data(), ident.size() * 4, cudaMemcpyHostToDevice, c->stream));
+  ZC_CUDA(cudaMemcpyAsync(dctx, &ctx32, 4, cudaMemcpyHostToDevice, c->stream));
+  PagedAttnArgs a{};
+  a.q = (const float*)dq;
+  a.k_pool = dk;
+  a.v_pool = dv;
+  a.page_table = (const int32_t*)dpt;
+  a.ctx_len = (const int32_t*)dctx;
+  a.out = (float*)dout;
+  a.batch = 1;
+  a.hq = (int)hq;
+  a.hkv = (int)hkv;
+  a.hd = (int)hd;
+  a.page_size = (int)block_size;
+  a.max_pages = (int)std::max<size_t>(nlb, 1);
+  a.num_pages = (int)std::max<size_t>(nlb, 1);
+  a.page_stride = (long long)blk_floats;
+  a.slot_stride = (long long)(hkv * hd);
+  a.head_stride = (long long)hd;
+  a.scale = scale;
+  a.kv_half = 0;
+  a.max_ctx = (int)ctx_len;
+  int rc = attention_device(a, c->stream);
+  if (rc != kOk) {
+    if (t_last_error.empty()) t_last_error = "paged attention: unsupported head_dim or layout";
+    cudaStreamSynchronize(c->stream);
+    return rc;
+  }
+  ZC_CUDA(cudaMemcpyAsync(out, dout, hq * hd * 4, cudaMemcpyDeviceToHost, c->stream));
+  (void)max_id;
+  return finish(c);
+}
+
+int32_t zc_dot_i8(size_t n, const int8_t* a, const int8_t* b, int32_t* out) {
+  t_last_error.clear();
+  if (!a || !b || !out) return fail(kBadArgument, "null pointer");
+  HostCtx* c = nullptr;
+  ZC_RC(host_ctx(&c));
+  void *da, *db, *dr;
+  ZC_RC(staging(c, 0, n, &da));
+  ZC_RC(staging(c, 1, n, &db));
+  ZC_RC(staging(c, 2, 16, &dr));
+  if (n) {
+    ZC_CUDA(cudaMemcpyAsync(da, a, n, cudaMemcpyHostToDevice, c->stream));
+    ZC_CUDA(cudaMemcpyAsync(db, b, n, cudaMemcpyHostToDevice, c->stream));
+  }
+  ZC_RC(dot_i8((const int8_t*)da, (const int8_t*)db, n, (int32_t*)dr, c->stream));
+  ZC_CUDA(cudaMemcpyAsync(out, dr, 4, cudaMemcpyDeviceToHost, c->stream));
+  return finish(c);
+}
+
+// ------------------------------------------------------------------------------------------
+// Device-pointer extension (include/zero_tensor_cuda.h)
+// ------------------------------------------------------------------------------------------
+int32_t zcu_quantize_q8_0(const float* src, uint8_t* blocks, size_t n, void* stream) {
+  return quantize_q8_0(src, blocks, n, as_stream(stream));
+}
+
+int32_t zcu_quantize_q4_0(const float* src, uint8_t* blocks, size_t n, void* stream) {
+  return quantize_q4_0(src, blocks, n, as_stream(stream));
+}
+
+int32_t zcu_q8_0_repack(const uint8_t* aos, int8_t* qs, uint16_t* d, size_t n_rows, size_t k_cols, void* stream) {
+  return repack_q8_0(aos, qs, d, n_rows, k_cols, as_stream(stream));
+}
+
+int32_t zcu_q4_0_repack(const uint8_t* aos, uint8_t* qs, uint16_t* d, size_t n_rows, size_t k_cols, void* stream) {
+  return repack_q4_0(aos, qs, d, n_rows, k_cols, as_stream(stream));
+}
+
+int32_t zcu_gemv_q8_0(const int8_t* qs, const uint16_t* d, const float* x, float* y, size_t n_rows, size_t k_cols,
+                      int32_t accumulate, void* stream) {
+  if (n_rows > 0x7fffffff || k_cols > 0x7fffffff) return kUnsupported;
+  return gemv_q8_0(qs, d, x, y, (int)n_rows, (int)k_cols, accumulate, as_stream(stream));
+}
+
+int32_t zcu_gemv_q4_0(const uint8_t* qs, const uint16_t* d, const float* x, float* y, size_t n_rows, size_t k_cols,
+                      int32_t accumulate, void* stream) {
+  if (n_rows > 0x7fffffff || k_cols > 0x7fffffff) return kUnsupported;
+  return gemv_q4_0(qs, d, x, y, (int)n_rows, (int)k_cols, accumulate, as_stream(stream));
+}
+
+int32_t zcu_paged_attention(const float* q, const void* k_pool, const void* v_pool, int32_t kv_dtype,
+                            const int32_t* page_table, const int32_t* ctx_len, float* out, int32_t batch, int32_t hq,
+                            int32_t hkv, int32_t hd, int32_t page_size, int32_t max_pages, int32_t num_pages,
+                            int64_t page_stride, int64_t slot_stride, int64_t head_stride, float scale,
+                            int32_t max_ctx, void* stream) {
+  t_last_error.clear();
+  if (num_pages <= 0) return fail(kBadArgument, "num_pages must be positive");
+  PagedAttnArgs a{};
+  a.q = q;
+  a.k_pool = k_pool;
+  a.v_pool = v_pool;
+  a.page_table = page_table;
+  a.ctx_len = ctx_len;
+  a.out = out;
+  a.batch = batch;
+  a.hq = hq;
+  a.hkv = hkv;
+  a.hd = hd;
+  a.page_size = page_size;
+  a.max_pages = max_pages;
+  a.num_pages = num_pages;
+  a.page_stride = page_stride;
+  a.slot_stride = slot_stride;
+  a.head_stride = head_stride;
+  a.scale = scale;
+  a.kv_half = kv_dtype == 1;
+  a.max_ctx = max_ctx;
+  return attention_device(a, as_stream(stream));
+}
+
+int32_t zcu_rmsnorm(const float* x, const float* w, float* out, int32_t rows, int32_t n, float eps, void* stream) {
+  return rmsnorm(x, w, out, rows, n, eps, as_stream(stream));
+}
+
+int32_t zcu_swiglu(const float* gate, const float* up, float* out, size_t n, void* stream) {
+  return swiglu(gate, up, out, n, as_stream(stream));
+}
+
+int32_t zcu_rope(float* x, int32_t rows, int32_t heads, int32_t hd, const int32_t* pos, int32_t pos0,
+                 const float* cos_t, const float* sin_t, int32_t max_pos, void* stream) {
+  return rope(x, rows, heads, hd, pos, pos0, cos_t, sin_t, max_pos, as_stream(stream));
+}
+
+int32_t zcu_embed_q8_0(const int8_t* qs, const uint16_t* d, const int32_t* tokens, int32_t n_tokens, int32_t vocab,
+                       int32_t dim, float* out, void* stream) {
+  return embed_q8_0(qs, d, tokens, n_tokens, vocab, dim, out, as_stream(stream));
+}
+
+}  // extern "C"

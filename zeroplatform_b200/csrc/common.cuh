@@ -1,0 +1,74 @@
+// common.cuh -- shared device helpers for the ZeroLlm B200 kernels (sm_100a only).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "zeroplatform_b200 kernels are written for sm_100a (B200) only"
+#endif
+
+namespace zc {
+
+// Status codes shared by every entry point (0 = handled, as the reference bridge expects).
+enum Status : int {
+  kOk = 0,
+  kNotHandled = -1,      // caller should run its own (managed) path
+  kBadArgument = -2,     // sizes / alignment / null pointers
+  kCudaError = -3,       // a CUDA runtime call failed; details in zc_cuda_last_error()
+  kUnsupported = -4,     // a shape this build does not cover
+  kOutOfMemory = -5,     // device allocation failed
+  kTooLarge = -6,        // exceeds a fixed-capacity buffer
+};
+
+constexpr int QK = 32;            // elements per Q8_0 / Q4_0 block
+constexpr int Q8_BLOCK_BYTES = 34;
+constexpr int Q4_BLOCK_BYTES = 18;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// 128-bit streaming load that bypasses L1 allocation: weights are read exactly once per call.
+__device__ __forceinline__ int4 ld_stream_v4(const void* p) {
+  int4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.s32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ float4 ld_f4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+
+__device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+// Exact int8 -> fp32 for the four signed bytes of w: byte i becomes the float 2^23 + (q_i + 128),
+// from which one subtraction recovers q_i exactly (PRMT + FADD instead of a conversion unit op).
+__device__ __forceinline__ void s8x4_to_f32(uint32_t w, float& f0, float& f1, float& f2, float& f3) {
+  const uint32_t b = w ^ 0x80808080u;
+  const float bias = 8388736.0f;  // 2^23 + 128
+  f0 = __uint_as_float(__byte_perm(b, 0x4B000000u, 0x7650)) - bias;
+  f1 = __uint_as_float(__byte_perm(b, 0x4B000000u, 0x7651)) - bias;
+  f2 = __uint_as_float(__byte_perm(b, 0x4B000000u, 0x7652)) - bias;
+  f3 = __uint_as_float(__byte_perm(b, 0x4B000000u, 0x7653)) - bias;
+}
+
+// Exact nibble -> fp32 with the Q4_0 offset: byte i of v (each 0..15) becomes (v_i - 8).
+__device__ __forceinline__ void u4x4_to_f32(uint32_t v, float& f0, float& f1, float& f2, float& f3) {
+  const float bias = 8388616.0f;  // 2^23 + 8
+  f0 = __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7650)) - bias;
+  f1 = __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7651)) - bias;
+  f2 = __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7652)) - bias;
+  f3 = __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7653)) - bias;
+}
+
+}  // namespace zc

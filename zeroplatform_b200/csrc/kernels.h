@@ -1,0 +1,66 @@
+// kernels.h -- internal launch API of the CUDA kernels (C++ linkage; the public C ABI is in
+// include/zero_tensor_cuda.h and capi.cu).  All pointers are device pointers unless stated.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace zc {
+
+// ---- weight layout (gemv.cu) ----
+int repack_q8_0(const uint8_t* aos, int8_t* qs, uint16_t* d, size_t n, size_t k, cudaStream_t s);
+int repack_q4_0(const uint8_t* aos, uint8_t* qs, uint16_t* d, size_t n, size_t k, cudaStream_t s);
+
+// ---- fp32 -> packed AoS blocks (quant.cu); n = element count, a multiple of 32 ----
+int quantize_q8_0(const float* src, uint8_t* dst, size_t n, cudaStream_t s);
+int quantize_q4_0(const float* src, uint8_t* dst, size_t n, cudaStream_t s);
+
+// ---- decode GEMV (gemv.cu): y = W x (accumulate = 0) or y += W x ----
+int gemv_q8_0(const int8_t* qs, const uint16_t* d, const float* x, float* y, int n, int k, int accumulate,
+              cudaStream_t s);
+int gemv_q4_0(const uint8_t* qs, const uint16_t* d, const float* x, float* y, int n, int k, int accumulate,
+              cudaStream_t s);
+
+// ---- paged decode attention (attention.cu) ----
+// One query token per sequence. K/V element (page p, slot t, kv head h, dim e) lives at
+//   pool + p*page_stride + t*slot_stride + h*head_stride + e          (elements)
+// ctx_len[b] tokens of sequence b are attended (its page list is page_table[b*max_pages ...]).
+// q/out: [batch][hq][hd] fp32.  kv_half != 0: pools are fp16, else fp32.
+struct PagedAttnArgs {
+  const float* q;
+  const void* k_pool;
+  const void* v_pool;
+  const int32_t* page_table;
+  const int32_t* ctx_len;
+  float* out;
+  int batch, hq, hkv, hd, page_size, max_pages;
+  int num_pages;      // pages in each pool; entries outside [0, num_pages) are skipped (0 = unchecked)
+  long long page_stride, slot_stride, head_stride;
+  float scale;
+  int kv_half;
+  int max_ctx;        // upper bound of ctx_len over the batch (sizes the split grid)
+  float* workspace;   // split-K partials; may be null when splits == 1
+  int* counters;      // [batch*hq] zero-initialised arrival counters (left zeroed); null when splits == 1
+  int splits;         // 0 = choose automatically
+};
+size_t paged_attention_workspace_floats(int batch, int hq, int hd, int splits);
+int paged_attention_choose_splits(int batch, int hkv, int max_ctx, int page_size);
+int paged_attention(const PagedAttnArgs& a, cudaStream_t s);
+
+// ---- small decode-step operators (ops.cu) ----
+int rmsnorm(const float* x, const float* w, float* out, int rows, int n, float eps, cudaStream_t s);
+int swiglu(const float* gate, const float* up, float* out, size_t n, cudaStream_t s);
+int silu(const float* x, float* out, size_t n, cudaStream_t s);
+// Interleaved RoPE on [rows][heads][hd] at positions pos[row] (or pos0 + row when pos == null),
+// with host-precomputed cos/sin tables [max_pos][hd/2].
+int rope(float* x, int rows, int heads, int hd, const int32_t* pos, int pos0, const float* cos_t,
+         const float* sin_t, int max_pos, cudaStream_t s);
+int embed_q8_0(const int8_t* qs, const uint16_t* d, const int32_t* tokens, int n_tokens, int vocab, int dim,
+               float* out, cudaStream_t s);
+
+int rope_tensorops(float* x, int heads, int seq, int hd, int pos0, float theta, cudaStream_t s);
+int sgemm(int m, int n, int k, float alpha, const float* a, const float* b, float beta, float* c, cudaStream_t s);
+int dot_i8(const int8_t* a, const int8_t* b, size_t n, int32_t* out, cudaStream_t s);
+
+}  // namespace zc
