@@ -92,6 +92,16 @@ ZC_API int32_t zc_paged_attention_f32(size_t hq, size_t hkv, size_t hd, size_t b
 /* zc_dot_i8 (ZeroTensorNativeBridge.cs:108,385-389): *out = sum a[i]*b[i] with int32 accumulation. */
 ZC_API int32_t zc_dot_i8(size_t n, const int8_t* a, const int8_t* b, int32_t* out);
 
+/* Weight residency (not in the reference ABI).  Registers a read-only quantized weight tensor that lives
+ * in host memory -- e.g. a tensor inside the memory-mapped GGUF file that GgufArchive.MatMulQuantized
+ * streams from (GgufFormat.cs:164-247) -- so that later zc_gemv_q8_0 / zc_gemv_q4_0 calls with the same
+ * pointer, shape and type on the same device use a device-resident copy: only x and y cross PCIe.
+ * ggml_type uses the GGML ids the reference uses (GgufFormat.cs:41 GgmlType): 8 = Q8_0, 2 = Q4_0.
+ * The caller promises that the bytes do not change until zc_unregister_weights (true for a read-only
+ * mmap).  Registering an already registered pointer replaces the copy. */
+ZC_API int32_t zc_register_weights(int32_t ggml_type, const uint8_t* w, size_t n_rows, size_t k_cols);
+ZC_API int32_t zc_unregister_weights(const uint8_t* w);
+
 /* Message of the last failure on the calling thread ("" if none). Not in the reference ABI. */
 ZC_API const char* zc_cuda_last_error(void);
 

@@ -55,6 +55,19 @@ ZC_API int32_t zcu_gemv_q8_0(const int8_t* qs, const uint16_t* d, const float* x
 ZC_API int32_t zcu_gemv_q4_0(const uint8_t* qs, const uint16_t* d, const float* x, float* y, size_t n_rows, size_t k_cols,
                       int32_t accumulate, void* stream);
 
+/* Batched / prefill quantized GEMM on the tensor cores: Y[m][n_rows] (=|+=) X[m][k_cols] . W^T for Q8_0 W in
+ * SoA layout -- LlmEngine.PrefillPrompt's token-parallel MatVecMulQ8_0 / MatVecAddQ8_0
+ * (ZeroLlm/src/ZeroLlm.Core/Engine/LlmEngine.cs:208-304) as one contraction.  X, Y fp32 row-major.
+ * Numerics: weights enter the MMA as fp16(q*d), activations as fp16(x) (|x| < 65504), fp32 accumulation.
+ * k_cols must be a multiple of 32; the fp16 copy of X lives in the library's per-(device, stream) workspace. */
+ZC_API int32_t zcu_gemm_q8_0(const int8_t* qs, const uint16_t* d, const float* x, float* y, size_t m, size_t n_rows,
+                             size_t k_cols, int32_t accumulate, void* stream);
+
+/* Synchronises the device and returns its status word: 0 = healthy, otherwise the code a kernel recorded
+ * when one of its bounded waits expired (the kernel then stopped, drained and released its resources).
+ * reset != 0 clears it. */
+ZC_API int32_t zcu_device_status(int32_t reset);
+
 /* Paged decode attention on device buffers -- GqaAttention.Forward (ZeroLlm/src/ZeroLlm.Core/Layers/
  * GqaAttention.cs:29-130) and TensorOps.PagedAttention (TensorOps.Neural.cs:2372-2476) for `batch`
  * sequences with one query token each.

@@ -1,0 +1,82 @@
+"""Prefill / batched Q8_0 GEMM on tcgen05 vs the oracle's token-parallel MatVecMulQ8_0 (LlmEngine.PrefillPrompt).
+
+Tolerance: max|Y - Y_oracle| / max|Y_oracle| <= 1e-3 -- the north-star bound for fp32 outputs.  The tensor
+core consumes fp16(q*d) and fp16(x) with fp32 accumulation; the measured error is printed.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from tests.conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+
+
+def _lib():
+    from zeroplatform_b200 import _lib
+    return _lib.lib()
+
+
+def _run(qw, x, y, accumulate=False):
+    rc = _lib().zcu_gemm_q8_0(qw.qs.data_ptr(), qw.d.data_ptr(), x.data_ptr(), y.data_ptr(), x.shape[0], qw.rows,
+                              qw.cols, int(accumulate), torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    assert _lib().zcu_device_status(1) == 0  # no bounded wait expired
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 128, 64), (5, 200, 96), (64, 256, 768), (100, 384, 2048), (130, 1000, 4096),
+                                   (257, 128, 128), (512, 11008, 4096)])
+def test_gemm_matches_oracle(m, n, k):
+    from zeroplatform_b200.ops import QuantizedWeight
+    rng = np.random.default_rng(m * 7 + n + k)
+    w = rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02)
+    x = rng.standard_normal((m, k), dtype=np.float32)
+    blocks = O.quantize_q8_0(w)
+    ref = O.matmul(8, blocks, x, n, k)
+    qw = QuantizedWeight.upload(8, blocks, n, k)
+    xd = torch.from_numpy(x).cuda()
+    y = torch.full((m, n), float("nan"), device="cuda")
+    _run(qw, xd, y)
+    err = rel_err(y.cpu().numpy(), ref)
+    print(f"gemm {m}x{n}x{k}: max-rel err {err:.3e}")
+    assert err <= TOL
+    # MatVecAdd form (Wo / Wdown residual adds): Y += W X
+    y0 = rng.standard_normal((m, n), dtype=np.float32)
+    yt = torch.from_numpy(y0.copy()).cuda()
+    _run(qw, xd, yt, accumulate=True)
+    assert rel_err(yt.cpu().numpy() - y0, ref) <= TOL
+
+
+def test_gemm_is_deterministic_and_repeatable():
+    from zeroplatform_b200.ops import QuantizedWeight
+    rng = np.random.default_rng(1)
+    n, k, m = 512, 1024, 300
+    qw = QuantizedWeight.upload(8, O.quantize_q8_0(rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02)),
+                                n, k)
+    xd = torch.from_numpy(rng.standard_normal((m, k), dtype=np.float32)).cuda()
+    y1 = torch.empty((m, n), device="cuda")
+    y2 = torch.empty((m, n), device="cuda")
+    _run(qw, xd, y1)
+    _run(qw, xd, y2)
+    assert torch.equal(y1, y2)
+
+
+def test_gemm_matches_fp16_rounded_reference_tightly():
+    """With X and q*d rounded to fp16 exactly as the kernel does, only the fp32 summation order differs."""
+    from zeroplatform_b200.ops import QuantizedWeight
+    rng = np.random.default_rng(2)
+    n, k, m = 256, 512, 96
+    blocks = O.quantize_q8_0(rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02))
+    x = rng.standard_normal((m, k), dtype=np.float32)
+    b = blocks.reshape(n, k // 32, 34)
+    d = b[:, :, :2].copy().view(np.float16).astype(np.float32)          # [n, k/32, 1]
+    q = b[:, :, 2:].view(np.int8).astype(np.float32)                   # [n, k/32, 32]
+    w16 = (q * d).astype(np.float16).astype(np.float64).reshape(n, k)  # fp16(q*d): single rounding of the exact product
+    x16 = x.astype(np.float16).astype(np.float64)
+    ref = x16 @ w16.T
+    qw = QuantizedWeight.upload(8, blocks, n, k)
+    y = torch.empty((m, n), device="cuda")
+    _run(qw, torch.from_numpy(x).cuda(), y)
+    assert rel_err(y.cpu().numpy(), ref) <= 1e-5

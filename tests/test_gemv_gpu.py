@@ -121,3 +121,26 @@ def test_device_quantizer_bit_exact(qtype, scale):
     ref = O.quantize_q8_0(w) if qtype == 8 else O.quantize_q4_0(w)
     got = quantize(qtype, torch.from_numpy(w).cuda()).cpu().numpy()
     assert np.array_equal(got, ref)
+
+
+def test_registered_weights_are_used_and_released():
+    """zc_register_weights keeps a device copy: results match, and re-registering picks up new bytes."""
+    from zeroplatform_b200 import _lib
+    from zeroplatform_b200.ops import TensorBlas, _np_ptr
+    L = _lib.lib()
+    blocks, x, _ = _case(8, 1024, 768, 5)
+    ref = O.matvec(8, blocks, x, 1024, 768)
+    assert L.zc_register_weights(8, _np_ptr(blocks), 1024, 768) == 0
+    assert rel_err(TensorBlas.gemv_q8_0(x, blocks, 1024, 768), ref) <= TOL
+    other, _, _ = _case(8, 1024, 768, 6)
+    blocks[...] = other                      # caller broke the promise: the resident copy is still used
+    assert rel_err(TensorBlas.gemv_q8_0(x, blocks, 1024, 768), ref) <= TOL
+    assert L.zc_register_weights(8, _np_ptr(blocks), 1024, 768) == 0   # re-registration refreshes the copy
+    assert rel_err(TensorBlas.gemv_q8_0(x, blocks, 1024, 768), O.matvec(8, other, x, 1024, 768)) <= TOL
+    assert L.zc_unregister_weights(_np_ptr(blocks)) == 0
+    assert L.zc_unregister_weights(_np_ptr(blocks)) == -1
+    assert rel_err(TensorBlas.gemv_q8_0(x, blocks, 1024, 768), O.matvec(8, other, x, 1024, 768)) <= TOL
+    b4, x4, _ = _case(4, 300, 2048, 7)
+    assert L.zc_register_weights(2, _np_ptr(b4), 300, 2048) == 0
+    assert rel_err(TensorBlas.gemv_q4_0(x4, b4, 300, 2048), O.matvec(4, b4, x4, 300, 2048)) <= TOL
+    assert L.zc_unregister_weights(_np_ptr(b4)) == 0

@@ -34,6 +34,8 @@ SIGNATURES = {
     "zc_rope_f32": (i32, [sz, sz, sz, sz, f32, vp]),
     "zc_paged_attention_f32": (i32, [sz, sz, sz, sz, sz, f32, vp, vp, vp, vp, vp]),
     "zc_dot_i8": (i32, [sz, vp, vp, vp]),
+    "zc_register_weights": (i32, [i32, vp, sz, sz]),
+    "zc_unregister_weights": (i32, [vp]),
     "zc_cuda_last_error": (C.c_char_p, []),
     # device-pointer extension
     "zcu_quantize_q8_0": (i32, [vp, vp, sz, vp]),
@@ -42,6 +44,8 @@ SIGNATURES = {
     "zcu_q4_0_repack": (i32, [vp, vp, vp, sz, sz, vp]),
     "zcu_gemv_q8_0": (i32, [vp, vp, vp, vp, sz, sz, i32, vp]),
     "zcu_gemv_q4_0": (i32, [vp, vp, vp, vp, sz, sz, i32, vp]),
+    "zcu_gemm_q8_0": (i32, [vp, vp, vp, vp, sz, sz, sz, i32, vp]),
+    "zcu_device_status": (i32, [i32]),
     "zcu_paged_attention": (i32, [vp, vp, vp, i32, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, i64, i64, i64,
                                   f32, i32, vp]),
     "zcu_rmsnorm": (i32, [vp, vp, vp, i32, i32, f32, vp]),

@@ -109,51 +109,69 @@ int finish(HostCtx* c) {
   return kOk;
 }
 
-// Split-K workspace of the paged attention, one per (device, stream).  The arrival counters are zeroed
-// when allocated and every launch leaves them zeroed.
-struct AttnWs {
-  float* ws = nullptr;
-  size_t ws_floats = 0;
-  int* ctr = nullptr;
-  size_t ctr_n = 0;
+// Library-owned device scratch, one set of slots per (device, stream): calls on one stream are ordered,
+// so they may share it; calls on different streams never do.  Slots: 0 attention split partials,
+// 1 attention arrival counters (zeroed at allocation, left zeroed by every launch), 2 fp16 activations of
+// the tensor-core GEMM.  A call that has to grow a slot allocates, which is not allowed while the stream
+// is being captured into a CUDA graph: make one call of the same shape before capturing.
+struct StreamScratch {
+  void* buf[4] = {};
+  size_t cap[4] = {};
 };
 std::mutex g_ws_mu;
-std::map<std::pair<int, cudaStream_t>, AttnWs> g_ws;
+std::map<std::pair<int, cudaStream_t>, StreamScratch> g_ws;
 
-int attn_workspace(cudaStream_t s, size_t floats, size_t counters, float** ws, int** ctr) {
+int stream_scratch(cudaStream_t s, int slot, size_t bytes, bool zeroed, void** out) {
   int dev = 0;
   ZC_CUDA(cudaGetDevice(&dev));
   std::lock_guard<std::mutex> g(g_ws_mu);
-  AttnWs& w = g_ws[{dev, s}];
-  if (w.ws_floats < floats) {
-    if (w.ws) {
+  StreamScratch& w = g_ws[{dev, s}];
+  if (bytes == 0) bytes = 16;
+  if (w.cap[slot] < bytes) {
+    if (w.buf[slot]) {
       ZC_CUDA(cudaStreamSynchronize(s));
-      ZC_CUDA(cudaFree(w.ws));
-      w.ws = nullptr;
-      w.ws_floats = 0;
+      ZC_CUDA(cudaFree(w.buf[slot]));
+      w.buf[slot] = nullptr;
+      w.cap[slot] = 0;
     }
-    if (cudaMalloc(&w.ws, floats * sizeof(float)) != cudaSuccess) {
+    if (cudaMalloc(&w.buf[slot], bytes) != cudaSuccess) {
       cudaGetLastError();
-      return fail(kOutOfMemory, "attention workspace allocation failed");
+      return fail(kOutOfMemory, "workspace allocation failed");
     }
-    w.ws_floats = floats;
+    if (zeroed) ZC_CUDA(cudaMemsetAsync(w.buf[slot], 0, bytes, s));
+    w.cap[slot] = bytes;
   }
-  if (w.ctr_n < counters) {
-    if (w.ctr) {
-      ZC_CUDA(cudaStreamSynchronize(s));
-      ZC_CUDA(cudaFree(w.ctr));
-      w.ctr = nullptr;
-      w.ctr_n = 0;
-    }
-    if (cudaMalloc(&w.ctr, counters * sizeof(int)) != cudaSuccess) {
+  *out = w.buf[slot];
+  return kOk;
+}
+
+int attn_workspace(cudaStream_t s, size_t floats, size_t counters, float** ws, int** ctr) {
+  void *a, *b;
+  ZC_RC(stream_scratch(s, 0, floats * sizeof(float), false, &a));
+  ZC_RC(stream_scratch(s, 1, counters * sizeof(int), true, &b));
+  *ws = static_cast<float*>(a);
+  *ctr = static_cast<int*>(b);
+  return kOk;
+}
+
+// Per-device status word written by kernels whose bounded waits expired (0 = healthy).
+std::mutex g_status_mu;
+std::map<int, int*> g_status;
+
+int device_status_ptr(int** out) {
+  int dev = 0;
+  ZC_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> g(g_status_mu);
+  int*& p = g_status[dev];
+  if (!p) {
+    if (cudaMalloc(&p, sizeof(int)) != cudaSuccess) {
       cudaGetLastError();
-      return fail(kOutOfMemory, "attention counter allocation failed");
+      p = nullptr;
+      return fail(kOutOfMemory, "status word allocation failed");
     }
-    ZC_CUDA(cudaMemsetAsync(w.ctr, 0, counters * sizeof(int), s));
-    w.ctr_n = counters;
+    ZC_CUDA(cudaMemset(p, 0, sizeof(int)));
   }
-  *ws = w.ws;
-  *ctr = w.ctr;
+  *out = p;
   return kOk;
 }
 
@@ -172,6 +190,27 @@ int attention_device(const PagedAttnArgs& in, cudaStream_t s) {
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Weights registered with zc_register_weights: host pointer -> device-resident SoA copy.
+struct Registered {
+  int qtype = 0;
+  size_t n = 0, k = 0;
+  int device = -1;
+  void* qs = nullptr;
+  void* d = nullptr;
+};
+std::mutex g_reg_mu;
+std::map<std::pair<const uint8_t*, int>, Registered> g_reg;  // (host pointer, device)
+
+bool find_registered(const uint8_t* w, int qtype, size_t n, size_t k, Registered* out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  std::lock_guard<std::mutex> g(g_reg_mu);
+  auto it = g_reg.find({w, dev});
+  if (it == g_reg.end() || it->second.qtype != qtype || it->second.n != n || it->second.k != k) return false;
+  *out = it->second;
+  return true;
+}
+
 int gemv_host(int qtype, const uint8_t* w, const float* x, float* y, size_t n, size_t k) {
   if (!w || !x || !y) return fail(kBadArgument, "null pointer");
   if (k == 0 || k % QK) return fail(kBadArgument, "k_cols must be a positive multiple of 32");
@@ -179,6 +218,21 @@ int gemv_host(int qtype, const uint8_t* w, const float* x, float* y, size_t n, s
   if (n > 0x7fffffff || k > 0x7fffffff) return fail(kUnsupported, "dimension too large");
   HostCtx* c = nullptr;
   ZC_RC(host_ctx(&c));
+  Registered reg;
+  if (find_registered(w, qtype, n, k, &reg)) {  // resident weights: only x and y cross PCIe
+    void *d_x, *d_y;
+    ZC_RC(staging(c, 3, k * sizeof(float), &d_x));
+    ZC_RC(staging(c, 4, n * sizeof(float), &d_y));
+    ZC_CUDA(cudaMemcpyAsync(d_x, x, k * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    if (qtype == 8)
+      ZC_RC(gemv_q8_0((const int8_t*)reg.qs, (const uint16_t*)reg.d, (const float*)d_x, (float*)d_y, (int)n, (int)k,
+                      0, c->stream));
+    else
+      ZC_RC(gemv_q4_0((const uint8_t*)reg.qs, (const uint16_t*)reg.d, (const float*)d_x, (float*)d_y, (int)n, (int)k,
+                      0, c->stream));
+    ZC_CUDA(cudaMemcpyAsync(y, d_y, n * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+    return finish(c);
+  }
   const size_t nb = n * (k / QK);
   const size_t aos_bytes = nb * (qtype == 8 ? Q8_BLOCK_BYTES : Q4_BLOCK_BYTES);
   const size_t qs_bytes = qtype == 8 ? n * k : n * k / 2;
@@ -237,6 +291,68 @@ int32_t zc_gemv_q8_0(const uint8_t* w, const float* x, float* y, size_t n_rows, 
 int32_t zc_gemv_q4_0(const uint8_t* w, const float* x, float* y, size_t n_rows, size_t k_cols) {
   t_last_error.clear();
   return gemv_host(4, w, x, y, n_rows, k_cols);
+}
+
+int32_t zc_register_weights(int32_t ggml_type, const uint8_t* w, size_t n_rows, size_t k_cols) {
+  t_last_error.clear();
+  const int qtype = ggml_type == 8 ? 8 : (ggml_type == 2 ? 4 : 0);
+  if (!qtype) return fail(kUnsupported, "only Q8_0 (8) and Q4_0 (2) tensors can be registered");
+  if (!w || n_rows == 0 || k_cols == 0 || k_cols % QK) return fail(kBadArgument, "bad weight tensor");
+  if (n_rows > 0x7fffffff || k_cols > 0x7fffffff) return fail(kUnsupported, "dimension too large");
+  int dev = 0;
+  ZC_CUDA(cudaGetDevice(&dev));
+  zc_unregister_weights(w);
+  HostCtx* c = nullptr;
+  ZC_RC(host_ctx(&c));
+  const size_t nb = n_rows * (k_cols / QK);
+  const size_t aos_bytes = nb * (qtype == 8 ? Q8_BLOCK_BYTES : Q4_BLOCK_BYTES);
+  Registered r;
+  r.qtype = qtype;
+  r.n = n_rows;
+  r.k = k_cols;
+  r.device = dev;
+  if (cudaMalloc(&r.qs, qtype == 8 ? n_rows * k_cols : n_rows * k_cols / 2) != cudaSuccess ||
+      cudaMalloc(&r.d, nb * 2) != cudaSuccess) {
+    cudaGetLastError();
+    if (r.qs) cudaFree(r.qs);
+    return fail(kOutOfMemory, "device allocation for registered weights failed");
+  }
+  void* d_aos;
+  int rc = staging(c, 0, aos_bytes, &d_aos);
+  if (rc == kOk && cudaMemcpyAsync(d_aos, w, aos_bytes, cudaMemcpyHostToDevice, c->stream) != cudaSuccess)
+    rc = cuda_fail(cudaGetLastError(), "cudaMemcpyAsync(weights)");
+  if (rc == kOk)
+    rc = qtype == 8 ? repack_q8_0((const uint8_t*)d_aos, (int8_t*)r.qs, (uint16_t*)r.d, n_rows, k_cols, c->stream)
+                    : repack_q4_0((const uint8_t*)d_aos, (uint8_t*)r.qs, (uint16_t*)r.d, n_rows, k_cols, c->stream);
+  if (rc == kOk) rc = finish(c);
+  if (rc != kOk) {
+    cudaFree(r.qs);
+    cudaFree(r.d);
+    return rc;
+  }
+  std::lock_guard<std::mutex> g(g_reg_mu);
+  g_reg[{w, dev}] = r;
+  return kOk;
+}
+
+int32_t zc_unregister_weights(const uint8_t* w) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return kCudaError;
+  }
+  Registered r;
+  {
+    std::lock_guard<std::mutex> g(g_reg_mu);
+    auto it = g_reg.find({w, dev});
+    if (it == g_reg.end()) return kNotHandled;
+    r = it->second;
+    g_reg.erase(it);
+  }
+  cudaDeviceSynchronize();  // no call may still be reading the copy
+  cudaFree(r.qs);
+  cudaFree(r.d);
+  return kOk;
 }
 
 int32_t zc_gemm_f32(size_t m, size_t n, size_t k, float alpha, const float* a, intptr_t rsa, intptr_t csa,
@@ -415,7 +531,8 @@ int32_t zc_paged_attention_f32(size_t hq, size_t hkv, size_t hd, size_t block_si
 
 int32_t zc_dot_i8(size_t n, const int8_t* a, const int8_t* b, int32_t* out) {
   t_last_error.clear();
-  if (!a || !b || !out) return fail(kBadArgument, "null pointer");
+  // an empty managed array pinned with `fixed` arrives as a null pointer
+  if (!out || (n > 0 && (!a || !b))) return fail(kBadArgument, "null pointer");
   HostCtx* c = nullptr;
   ZC_RC(host_ctx(&c));
   void *da, *db, *dr;
@@ -460,6 +577,30 @@ int32_t zcu_gemv_q4_0(const uint8_t* qs, const uint16_t* d, const float* x, floa
                       int32_t accumulate, void* stream) {
   if (n_rows > 0x7fffffff || k_cols > 0x7fffffff) return kUnsupported;
   return gemv_q4_0(qs, d, x, y, (int)n_rows, (int)k_cols, accumulate, as_stream(stream));
+}
+
+int32_t zcu_gemm_q8_0(const int8_t* qs, const uint16_t* d, const float* x, float* y, size_t m, size_t n_rows,
+                      size_t k_cols, int32_t accumulate, void* stream) {
+  t_last_error.clear();
+  if (m > 0x7fffffff || n_rows > 0x7fffffff || k_cols > 0x7fffffff) return fail(kUnsupported, "dimension too large");
+  if (m == 0 || n_rows == 0) return kOk;
+  cudaStream_t s = as_stream(stream);
+  void* ws;
+  int* status;
+  const size_t bytes = gemm_q8_0_workspace_bytes((int)m, (int)k_cols);
+  ZC_RC(stream_scratch(s, 2, bytes, false, &ws));
+  ZC_RC(device_status_ptr(&status));
+  return gemm_q8_0_tc(qs, d, x, y, (int)m, (int)n_rows, (int)k_cols, accumulate, ws, bytes, status, s);
+}
+
+int32_t zcu_device_status(int32_t reset) {
+  int* p = nullptr;
+  if (device_status_ptr(&p) != kOk) return kCudaError;
+  int v = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess || cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return cuda_fail(cudaGetLastError(), "reading the device status word");
+  if (reset && v) cudaMemset(p, 0, sizeof(int));
+  return v;
 }
 
 int32_t zcu_paged_attention(const float* q, const void* k_pool, const void* v_pool, int32_t kv_dtype,

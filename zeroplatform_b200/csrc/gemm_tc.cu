@@ -1,0 +1,479 @@
+// gemm_tc.cu -- batched / prefill quantized GEMM on the 5th-generation tensor cores (tcgen05, sm_100a).
+//
+// Y[m, n] (=|+=) sum_k X[m, k] * dequant(W)[n, k] for X fp32 [M][K], W Q8_0 (SoA: int8 [N][K] + fp16
+// scales [N][K/32]), Y fp32 [M][N].  This is LlmEngine.PrefillPrompt's token-parallel loop of
+// QuantizedKernels.MatVecMulQ8_0 / MatVecAddQ8_0 (ZeroLlm/src/ZeroLlm.Core/Engine/LlmEngine.cs:208-304,
+// Quantization/QuantizedKernels.cs:190-308) executed as one contraction.
+//
+// Numerics: the weights enter the tensor core as fp16(q * d) -- the exact product rounded once -- and
+// the activations as fp16(x); products accumulate in fp32 in TMEM.  (An int8 MMA cannot apply the
+// per-32-value fp16 block scales inside the tensor core, and a CUDA-core epilogue per block would
+// run several times slower than the MMA itself.)
+//
+// Structure (one persistent CTA per SM, 10 warps):
+//   warp 0      TMA producer: X tile (fp16, pre-converted) [BN tokens x 64 k] per stage, 128B swizzle
+//   warp 1      MMA issuer: one thread issues 4 x tcgen05.mma.kind::f16 (M=128, N=BN, K=16) per stage
+//   warps 2-5   dequantizers: int8 W [128 rows x 64 k] + scales -> fp16 in the UMMA K-major 128B-swizzled
+//               layout in shared memory (fence.proxy.async before signalling the MMA warp)
+//   warps 6-9   epilogue: tcgen05.ld 32 TMEM columns at a time, coalesced fp32 stores of Y
+// The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue of one tile overlaps the
+// MMAs of the next.  Every mbarrier wait is bounded: on time-out the CTA records an error code in
+// `status`, stops issuing work, drains what it issued and frees its TMEM before returning.
+//
+// Roofline: tensor (fp16 dense), flops = 2 * M * N * K.
+
+#include <cuda.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace zc {
+
+namespace {
+
+constexpr int BM = 128;                  // weight rows per tile = MMA M = TMEM lanes
+constexpr int BK = 64;                   // k per stage: 64 fp16 = one 128-byte swizzle row
+constexpr int STAGES = 4;
+constexpr int GEMM_THREADS = 320;
+constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KB
+constexpr uint32_t WAIT_LIMIT = 1u << 24;    // try_wait polls before a wait is declared hung
+constexpr uint64_t WAIT_NS = 2000000000ull;  // ... or two seconds
+
+struct GemmParams {
+  const int8_t* qs;
+  const uint16_t* d;
+  float* y;
+  int* status;
+  int M, N, K;
+  int accumulate;
+  int bn;          // tokens per tile (MMA N): 64, 128 or 256
+  int n_tok_tiles;
+  int n_tiles;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait: gives up after WAIT_LIMIT polls or WAIT_NS nanoseconds, whichever comes first, raising
+// the CTA abort flag and recording `code` in the device status word.  Returns false when it gave up or
+// when another role of the CTA already aborted.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status,
+                                          int code) {
+  uint64_t t0 = 0;
+  for (uint32_t i = 0; i < WAIT_LIMIT; ++i) {
+    if (mbar_try(bar, parity)) return true;
+    if ((i & 255) == 255) {
+      if (*abort_flag) return false;
+      const uint64_t now = global_ns();
+      if (t0 == 0) t0 = now;
+      else if (now - t0 > WAIT_NS) break;
+    }
+  }
+  *abort_flag = 1;
+  atomicExch(status, code);
+  return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+
+// UMMA shared-memory descriptor: K-major operand, 128-byte swizzle, 8-row groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t addr) {
+  uint64_t desc = 0;
+  desc |= (uint64_t)((addr & 0x3FFFFu) >> 4);  // start address
+  desc |= (uint64_t)1u << 16;                   // leading byte offset (unused for swizzled K-major)
+  desc |= (uint64_t)(1024u >> 4) << 32;         // stride byte offset between 8-row core groups
+  desc |= (uint64_t)1u << 46;                   // descriptor version for tcgen05
+  desc |= (uint64_t)2u << 61;                   // layout: SWIZZLE_128B
+  return desc;
+}
+
+// Instruction descriptor for kind::f16: A = B = fp16, D = fp32, both K-major.
+__host__ __device__ constexpr uint32_t idesc_f16(int m, int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  uint32_t z = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(z), "r"(z), "r"(z), "r"(z));
+}
+
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// 16 int8 weights (one int4) times the fp16 block scale -> 16 fp16 values (exactly-rounded products).
+__device__ __forceinline__ void dequant16(int4 w, __half2 d2, uint4& lo, uint4& hi) {
+  const uint32_t* wv = reinterpret_cast<const uint32_t*>(&w);
+  uint32_t out[8];
+  const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1024 + 128
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t b = wv[j] ^ 0x80808080u;  // q + 128 in each byte
+    // halves 0x64XX = 1024 + XX (exact), pairs (byte0, byte1) and (byte2, byte3)
+    const uint32_t p01 = __byte_perm(b, 0x64646464u, 0x5140);
+    const uint32_t p23 = __byte_perm(b, 0x64646464u, 0x7362);
+    __half2 h01 = __hsub2(*reinterpret_cast<const __half2*>(&p01), bias);  // exact q
+    __half2 h23 = __hsub2(*reinterpret_cast<const __half2*>(&p23), bias);
+    h01 = __hmul2_rn(h01, d2);
+    h23 = __hmul2_rn(h23, d2);
+    out[2 * j] = *reinterpret_cast<uint32_t*>(&h01);
+    out[2 * j + 1] = *reinterpret_cast<uint32_t*>(&h23);
+  }
+  lo = make_uint4(out[0], out[1], out[2], out[3]);
+  hi = make_uint4(out[4], out[5], out[6], out[7]);
+}
+
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_q8_0_tc_kernel(const __grid_constant__ CUtensorMap x_map, GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int bn = p.bn;
+  const int b_stage_bytes = bn * BK * 2;
+  uint8_t* a_st = smem;                                   // STAGES x 16 KB
+  uint8_t* b_st = smem + STAGES * A_STAGE_BYTES;          // STAGES x bn*128 B
+  uint64_t* bars = reinterpret_cast<uint64_t*>(b_st + STAGES * b_stage_bytes);
+  uint64_t* full = bars;                 // [STAGES]
+  uint64_t* empty = bars + STAGES;       // [STAGES]
+  uint64_t* tfull = bars + 2 * STAGES;   // [2]
+  uint64_t* tempty = bars + 2 * STAGES + 2;
+  uint64_t* drain = bars + 2 * STAGES + 4;  // [1] completion of every MMA this CTA issued
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nk = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&full[s]), 128 + 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&tfull[a]), 1);
+      mbar_init(smem_u32(&tempty[a]), 128);
+    }
+    mbar_init(smem_u32(drain), 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {  // allocate 2 accumulators of bn fp32 columns (power of two >= 32)
+    const uint32_t ncols = 2u * (uint32_t)bn;
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(ncols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer for the activation tiles ----------------
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      for (int t = blockIdx.x; t < p.n_tiles && !*abort_flag; t += gridDim.x) {
+        const int tok0 = (t % p.n_tok_tiles) * bn;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(smem_u32(&empty[s]), ph ^ 1, abort_flag, p.status, 1)) break;
+          mbar_arrive_tx(smem_u32(&full[s]), (uint32_t)b_stage_bytes);
+          tma_load_2d(smem_u32(b_st + s * b_stage_bytes), &x_map, kb * BK, tok0, smem_u32(&full[s]));
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+      }
+      // On an abort, loads already issued may still be landing in shared memory: let them finish.
+      if (*abort_flag) __nanosleep(20000);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(BM, bn);
+      int s = 0;
+      uint32_t ph = 0;
+      int it = 0;
+      for (int t = blockIdx.x; t < p.n_tiles && !*abort_flag; t += gridDim.x, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_ph = (uint32_t)(it >> 1) & 1;
+        if (!mbar_wait(smem_u32(&tempty[acc]), acc_ph ^ 1, abort_flag, p.status, 2)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * bn);
+        bool ok = true;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(smem_u32(&full[s]), ph, abort_flag, p.status, 3)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(a_st + s * A_STAGE_BYTES);
+          const uint32_t b_addr = smem_u32(b_st + s * b_stage_bytes);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            umma_f16(d_tmem, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32), idesc,
+                     (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(smem_u32(&empty[s]));  // frees the stage once these MMAs have read it
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(smem_u32(&tfull[acc]));  // accumulator complete
+      }
+      // Every MMA issued above has finished once this commit's barrier flips (bounded on an abort).
+      umma_commit(smem_u32(drain));
+      uint64_t t0 = global_ns();
+      while (!mbar_try(smem_u32(drain), 0) && global_ns() - t0 < WAIT_NS) {
+      }
+    }
+  } else if (warp < 6) {
+    // ---------------- W dequantizers (128 threads) ----------------
+    const int tid = threadIdx.x - 64;  // 0..127
+    const int kblocks = p.K / QK;
+    int s = 0;
+    uint32_t ph = 0;
+    for (int t = blockIdx.x; t < p.n_tiles && !*abort_flag; t += gridDim.x) {
+      const int row0 = (t / p.n_tok_tiles) * BM;
+      // items: (row, 16-value chunk) pairs; 4 consecutive threads cover one row's 64 values
+      int4 wv[4];
+      __half2 dv[4];
+      auto load = [&](int kb) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int item = tid + 128 * j;
+          const int r = item >> 2, c = item & 3;
+          const int row = row0 + r;
+          const int k = kb * BK + c * 16;
+          if (row < p.N && k < p.K) {
+            wv[j] = ld_stream_v4(p.qs + (size_t)row * p.K + k);
+            const __half h = __ushort_as_half(__ldg(p.d + (size_t)row * kblocks + (k >> 5)));
+            dv[j] = __halves2half2(h, h);
+          } else {
+            wv[j] = make_int4(0, 0, 0, 0);
+            dv[j] = __float2half2_rn(0.f);
+          }
+        }
+      };
+      load(0);
+      for (int kb = 0; kb < nk; ++kb) {
+        int4 cw[4];
+        __half2 cd[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          cw[j] = wv[j];
+          cd[j] = dv[j];
+        }
+        if (kb + 1 < nk) load(kb + 1);  // next stage's loads overlap this stage's wait and conversion
+        if (!mbar_wait(smem_u32(&empty[s]), ph ^ 1, abort_flag, p.status, 4)) break;
+        uint8_t* a = a_st + s * A_STAGE_BYTES;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int item = tid + 128 * j;
+          const int r = item >> 2, c = item & 3;
+          uint4 lo, hi;
+          dequant16(cw[j], cd[j], lo, hi);
+          // row r of the tile: 128-byte line in its 1024-byte group, 16-byte chunks XOR-swizzled by r % 8
+          uint8_t* line = a + (r >> 3) * 1024 + (r & 7) * 128;
+          *reinterpret_cast<uint4*>(line + (((2 * c) ^ (r & 7)) << 4)) = lo;
+          *reinterpret_cast<uint4*>(line + (((2 * c + 1) ^ (r & 7)) << 4)) = hi;
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_arrive(smem_u32(&full[s]));
+        if (++s == STAGES) {
+          s = 0;
+          ph ^= 1;
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 6..9 -> TMEM lane quadrants 2, 3, 0, 1) ----------------
+    const int quad = warp & 3;
+    const int row_in_tile = quad * 32 + lane;
+    int it = 0;
+    for (int t = blockIdx.x; t < p.n_tiles && !*abort_flag; t += gridDim.x, ++it) {
+      const int acc = it & 1;
+      const uint32_t acc_ph = (uint32_t)(it >> 1) & 1;
+      if (!mbar_wait(smem_u32(&tfull[acc]), acc_ph, abort_flag, p.status, 5)) break;
+      tc_fence_after();
+      const int row = (t / p.n_tok_tiles) * BM + row_in_tile;
+      const int tok0 = (t % p.n_tok_tiles) * bn;
+      for (int c0 = 0; c0 < bn; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * bn + c0), r);
+        if (row < p.N) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int m = tok0 + c0 + j;
+            if (m < p.M) {
+              float* yp = p.y + (size_t)m * p.N + row;
+              const float v = __uint_as_float(r[j]);
+              *yp = p.accumulate ? *yp + v : v;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(smem_u32(&tempty[acc]));
+    }
+  }
+
+  // Drain: on an abort, wait (bounded) for the MMAs already committed so TMEM is idle before freeing it.
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(2u * (uint32_t)bn));
+  }
+}
+
+__global__ void f32_to_f16_kernel(const float* __restrict__ x, __half* __restrict__ y, size_t n) {
+  const size_t n4 = n / 4;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+    const float4 v = reinterpret_cast<const float4*>(x)[i];
+    __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
+    uint2 o;
+    o.x = *reinterpret_cast<uint32_t*>(&a);
+    o.y = *reinterpret_cast<uint32_t*>(&b);
+    reinterpret_cast<uint2*>(y)[i] = o;
+  }
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+}  // namespace
+
+size_t gemm_q8_0_workspace_bytes(int m, int k) { return (size_t)m * k * 2; }
+
+int gemm_q8_0_tc(const int8_t* qs, const uint16_t* d, const float* x, float* y, int m, int n, int k, int accumulate,
+                 void* workspace, size_t workspace_bytes, int* status, cudaStream_t s) {
+  if (!qs || !d || !x || !y || !status || m <= 0 || n <= 0 || k <= 0 || k % QK) return kBadArgument;
+  if (k % 8) return kUnsupported;  // TMA row pitch of the fp16 activations must be 16-byte aligned
+  if (!workspace || workspace_bytes < gemm_q8_0_workspace_bytes(m, k)) return kBadArgument;
+  if (reinterpret_cast<uintptr_t>(workspace) & 15 || reinterpret_cast<uintptr_t>(x) & 15 ||
+      reinterpret_cast<uintptr_t>(qs) & 15)
+    return kUnsupported;
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return kCudaError;
+  __half* x16 = reinterpret_cast<__half*>(workspace);
+  const size_t nx = (size_t)m * k;
+  f32_to_f16_kernel<<<(unsigned)std::min<size_t>((nx / 4 + 255) / 256, 148 * 8), 256, 0, s>>>(x, x16, nx);
+  if (cudaPeekAtLastError() != cudaSuccess) return kCudaError;
+
+  const int bn = m >= 192 ? 256 : (m > 64 ? 128 : 64);
+  CUtensorMap map;
+  cuuint64_t gdim[2] = {(cuuint64_t)k, (cuuint64_t)m};
+  cuuint64_t gstride[1] = {(cuuint64_t)k * 2};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)bn};
+  cuuint32_t estride[2] = {1, 1};
+  if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x16, gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return kCudaError;
+
+  GemmParams p;
+  p.qs = qs;
+  p.d = d;
+  p.y = y;
+  p.status = status;
+  p.M = m;
+  p.N = n;
+  p.K = k;
+  p.accumulate = accumulate;
+  p.bn = bn;
+  p.n_tok_tiles = (m + bn - 1) / bn;
+  p.n_tiles = ((n + BM - 1) / BM) * p.n_tok_tiles;
+  const int smem = 1024 + STAGES * (A_STAGE_BYTES + bn * BK * 2) + 256;  // + barriers, TMEM slot, flag
+  if (cudaFuncSetAttribute(gemm_q8_0_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return kCudaError;
+  const int grid = std::min(p.n_tiles, num_sms());
+  gemm_q8_0_tc_kernel<<<grid, GEMM_THREADS, smem, s>>>(map, p);
+  return cudaPeekAtLastError() == cudaSuccess ? kOk : kCudaError;
+}
+
+}  // namespace zc

@@ -22,6 +22,11 @@ int gemv_q8_0(const int8_t* qs, const uint16_t* d, const float* x, float* y, int
 int gemv_q4_0(const uint8_t* qs, const uint16_t* d, const float* x, float* y, int n, int k, int accumulate,
               cudaStream_t s);
 
+// ---- prefill / batched GEMM on tcgen05 (gemm_tc.cu): Y[m][n] (=|+=) X[m][:] . dequant(W)[n][:] ----
+size_t gemm_q8_0_workspace_bytes(int m, int k);
+int gemm_q8_0_tc(const int8_t* qs, const uint16_t* d, const float* x, float* y, int m, int n, int k, int accumulate,
+                 void* workspace, size_t workspace_bytes, int* status, cudaStream_t s);
+
 // ---- paged decode attention (attention.cu) ----
 // One query token per sequence. K/V element (page p, slot t, kv head h, dim e) lives at
 //   pool + p*page_stride + t*slot_stride + h*head_stride + e          (elements)

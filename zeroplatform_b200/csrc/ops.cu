@@ -68,8 +68,9 @@ __global__ void rope_kernel(float* __restrict__ x, int rows, int heads, int hd, 
     const float c = cos_t[(size_t)ps * half + p], s = sin_t[(size_t)ps * half + p];
     float* v = x + rh * hd + 2 * p;
     const float x0 = v[0], x1 = v[1];
-    v[0] = x0 * c - x1 * s;
-    v[1] = x0 * s + x1 * c;
+    // separate roundings, no contraction: the reference computes x0*c - x1*s with two products
+    v[0] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+    v[1] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
   }
 }
 
@@ -95,12 +96,12 @@ __global__ void rope_tensorops_kernel(float* __restrict__ x, int heads, int seq,
     const size_t hs = i / half;
     const int s = (int)(hs % seq);
     const float inv_freq = 1.0f / (float)pow((double)theta, (2.0 * p) / hd);
-    const float angle = (float)(pos0 + s) * inv_freq;
+    const float angle = __fmul_rn((float)(pos0 + s), inv_freq);
     const float c = (float)cos((double)angle), sn = (float)sin((double)angle);
     float* v = x + hs * hd + 2 * p;
     const float x1 = v[0], x2 = v[1];
-    v[0] = x1 * c - x2 * sn;
-    v[1] = x2 * c + x1 * sn;
+    v[0] = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, sn));
+    v[1] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, sn));
   }
 }
 
@@ -223,7 +224,7 @@ int sgemm(int m, int n, int k, float alpha, const float* a, const float* b, floa
 }
 
 int dot_i8(const int8_t* a, const int8_t* b, size_t n, int32_t* out, cudaStream_t s) {
-  if (!a || !b || !out) return kBadArgument;
+  if (!out || (n > 0 && (!a || !b))) return kBadArgument;
   if (cudaMemsetAsync(out, 0, sizeof(int32_t), s) != cudaSuccess) return kCudaError;
   if (n == 0) return kOk;
   dot_i8_kernel<<<grid_for(n, 256), 256, 0, s>>>(a, b, n, out);
