@@ -100,6 +100,68 @@ ZC_API int32_t zcu_rope(float* x, int32_t rows, int32_t heads, int32_t hd, const
 ZC_API int32_t zcu_embed_q8_0(const int8_t* qs, const uint16_t* d, const int32_t* tokens, int32_t n_tokens, int32_t vocab,
                        int32_t dim, float* out, void* stream);
 
+/* ---------------------------------------------------------------------------------------------------------
+ * Decode engine: LlmEngine (ZeroLlm/src/ZeroLlm.Core/Engine/LlmEngine.cs:19-568) for Q8_0 Llama-style models
+ * over a device-resident paged KV cache (Memory/PagedKvCache.cs:47-286, 16-token pages, fp16 K/V).
+ * The engine owns its device memory; weights are copied in once with zcu_engine_set_weight.
+ * ------------------------------------------------------------------------------------------------------- */
+typedef struct {
+  int32_t vocab, dim, layers, heads, kv_heads, ffn, context_length;  /* LlmModelConfig (LlmModelConfig.cs:6-41) */
+  float eps, rope_base;                                               /* RmsNormEps, RopeFreqBase */
+  int32_t total_pages, page_size;                                     /* PagedKvCache(totalBlocks, blockSize) */
+  int32_t max_batch;                                                  /* live sequences / decode batch */
+  int32_t max_pages_per_seq;                                          /* page-table width */
+  int32_t max_prefill_tokens;                                         /* longest prompt prefilled at once */
+  int32_t reference_causal_quirk; /* 1: non-final layers attend to [0, pos) as the reference does (LlmEngine.cs:254,
+                                     PagedKvCache.cs:139-142); 0: every layer attends to [0, pos] */
+} zcu_engine_config;
+
+/* Tensor kinds for zcu_engine_set_weight.  Q8_0 tensors are the reference's packed blocks [rows][cols/32]
+ * (LlmModel / LlmQuantizer layout, row-major [out][in]); norms are fp32 [dim].  `layer` is ignored for the
+ * whole-model tensors. */
+enum {
+  ZCU_W_TOK_EMB = 0,   /* Q8_0 [vocab][dim]   TokenEmbeddings_Q8 */
+  ZCU_W_LM_HEAD = 1,   /* Q8_0 [vocab][dim]   LmHead_Q8 */
+  ZCU_W_FINAL_NORM = 2,
+  ZCU_W_ATTN_NORM = 3,
+  ZCU_W_FFN_NORM = 4,
+  ZCU_W_Q = 5,         /* Q8_0 [heads*hd][dim] */
+  ZCU_W_K = 6,         /* Q8_0 [kv_heads*hd][dim] */
+  ZCU_W_V = 7,
+  ZCU_W_O = 8,         /* Q8_0 [dim][heads*hd] */
+  ZCU_W_GATE = 9,      /* Q8_0 [ffn][dim] */
+  ZCU_W_UP = 10,
+  ZCU_W_DOWN = 11      /* Q8_0 [dim][ffn] */
+};
+
+/* stream: the CUDA stream the engine enqueues on (NULL: the engine creates its own). */
+ZC_API int32_t zcu_engine_create(const zcu_engine_config* cfg, void* stream, void** engine);
+ZC_API int32_t zcu_engine_destroy(void* engine);
+ZC_API const char* zcu_engine_last_error(void* engine);
+ZC_API int32_t zcu_engine_set_weight(void* engine, int32_t kind, int32_t layer, const void* host, size_t bytes);
+/* LlmEngine.PrefillPrompt (LlmEngine.cs:157-315): n prompt tokens at positions start_pos.. of seq_id; writes the
+ * last token's logits [vocab] to host memory when logits != NULL.  n == 1 is ForwardToken. */
+ZC_API int32_t zcu_engine_prefill(void* engine, int32_t seq_id, const int32_t* tokens, int32_t n, int32_t start_pos,
+                                  float* logits);
+/* LlmEngine.ForwardToken (LlmEngine.cs:347-461) for `batch` sequences at once (one token each, host arrays);
+ * logits [batch][vocab] and/or greedy next tokens [batch] to host memory (either may be NULL). */
+ZC_API int32_t zcu_engine_decode(void* engine, const int32_t* seq_ids, const int32_t* tokens, const int32_t* positions,
+                                 int32_t batch, float* logits, int32_t* next_tokens);
+/* GenerateStreamAsync with greedy sampling (LlmEngine.cs:71-150, LlmSampler.cs:21-72): prefill, then n_new
+ * sample -> ForwardToken steps replayed from one captured CUDA graph with the state on the device.
+ * repetition_penalty <= 1 disables it; eos_token < 0 never stops.  Returns the number of tokens written to
+ * out_tokens (or a negative status); timing_ms[0] = prefill ms, timing_ms[1] = decode ms (device events). */
+ZC_API int32_t zcu_engine_generate(void* engine, int32_t seq_id, const int32_t* prompt, int32_t n_prompt,
+                                   int32_t n_new, float repetition_penalty, int32_t eos_token, int32_t* out_tokens,
+                                   float* timing_ms);
+/* PagedKvCache.FreeSequence / GetSequenceLength / FreeBlockCount / the page table / GetKey+GetValue. */
+ZC_API int32_t zcu_engine_free_sequence(void* engine, int32_t seq_id);
+ZC_API int32_t zcu_engine_seq_len(void* engine, int32_t seq_id);
+ZC_API int32_t zcu_engine_free_pages(void* engine);
+ZC_API int32_t zcu_engine_page_table(void* engine, int32_t seq_id, int32_t* out, int32_t cap);
+ZC_API int32_t zcu_engine_get_kv(void* engine, int32_t seq_id, int32_t layer, int32_t token, int32_t want_value,
+                                 float* out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -55,6 +55,31 @@ SIGNATURES = {
 }
 
 
+class EngineConfig(C.Structure):
+    """zcu_engine_config (include/zero_tensor_cuda.h)."""
+
+    _fields_ = [(n, C.c_int32) for n in ("vocab", "dim", "layers", "heads", "kv_heads", "ffn", "context_length")] + \
+        [("eps", C.c_float), ("rope_base", C.c_float)] + \
+        [(n, C.c_int32) for n in ("total_pages", "page_size", "max_batch", "max_pages_per_seq", "max_prefill_tokens",
+                                  "reference_causal_quirk")]
+
+
+SIGNATURES.update({
+    "zcu_engine_create": (i32, [C.POINTER(EngineConfig), vp, C.POINTER(vp)]),
+    "zcu_engine_destroy": (i32, [vp]),
+    "zcu_engine_last_error": (C.c_char_p, [vp]),
+    "zcu_engine_set_weight": (i32, [vp, i32, i32, vp, sz]),
+    "zcu_engine_prefill": (i32, [vp, i32, vp, i32, i32, vp]),
+    "zcu_engine_decode": (i32, [vp, vp, vp, vp, i32, vp, vp]),
+    "zcu_engine_generate": (i32, [vp, i32, vp, i32, i32, f32, i32, vp, vp]),
+    "zcu_engine_free_sequence": (i32, [vp, i32]),
+    "zcu_engine_seq_len": (i32, [vp, i32]),
+    "zcu_engine_free_pages": (i32, [vp]),
+    "zcu_engine_page_table": (i32, [vp, i32, vp, i32]),
+    "zcu_engine_get_kv": (i32, [vp, i32, i32, i32, i32, vp]),
+})
+
+
 class ZcError(RuntimeError):
     pass
 

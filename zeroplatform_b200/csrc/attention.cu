@@ -71,6 +71,8 @@ struct AttnDev {
   int* counters;
   int hq, group, page_size, max_pages, num_pages;
   long long page_stride, slot_stride, head_stride;
+  long long q_stride, out_stride, pt_stride;
+  const int32_t* pt_rows;
   float scale_log2;
 };
 
@@ -96,14 +98,14 @@ __global__ void __launch_bounds__(ATT_THREADS) paged_attn_kernel(AttnDev a) {
   const int pps = (n_pages + splits - 1) / splits;
   const int t_begin = min(ctx, split * pps * P);
   const int t_end = min(ctx, (split + 1) * pps * P);
-  const int32_t* pt = a.page_table + (size_t)b * a.max_pages;
+  const int32_t* pt = a.page_table + (size_t)(a.pt_rows ? a.pt_rows[b] : b) * a.pt_stride;
   const KV* kp = reinterpret_cast<const KV*>(a.k_pool);
   const KV* vp = reinterpret_cast<const KV*>(a.v_pool);
 
   float q[GT][8], m[GT], l[GT], acc[GT][8];
 #pragma unroll
   for (int g = 0; g < GT; ++g) {
-    const float* qg = a.q + ((size_t)b * a.hq + qh0 + g) * HD + 8 * sub;
+    const float* qg = a.q + (size_t)b * a.q_stride + (size_t)(qh0 + g) * HD + 8 * sub;
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       q[g][e] = qg[e] * a.scale_log2;
@@ -182,7 +184,7 @@ __global__ void __launch_bounds__(ATT_THREADS) paged_attn_kernel(AttnDev a) {
     }
     const size_t head = (size_t)b * a.hq + qh0 + g;
     if (splits == 1) {
-      a.out[head * HD + e] = L > 0.f ? O / L : 0.f;
+      a.out[(size_t)b * a.out_stride + (size_t)(qh0 + g) * HD + e] = L > 0.f ? O / L : 0.f;
     } else {
       float* ws = a.ws + (head * splits + split) * (HD + 2);
       ws[e] = O;
@@ -220,7 +222,7 @@ __global__ void __launch_bounds__(ATT_THREADS) paged_attn_kernel(AttnDev a) {
         O = fmaf(__ldcg(ws + s * (HD + 2) + e), w, O);
       }
     }
-    a.out[head * HD + e] = L > 0.f ? O / L : 0.f;
+    a.out[(size_t)b * a.out_stride + (size_t)(qh0 + g) * HD + e] = L > 0.f ? O / L : 0.f;
   }
   if (threadIdx.x == 0) a.counters[(size_t)b * tiles + tile] = 0;  // ready for the next call
 }
@@ -303,6 +305,10 @@ int paged_attention(const PagedAttnArgs& a, cudaStream_t s) {
   d.slot_stride = a.slot_stride;
   d.head_stride = a.head_stride;
   d.scale_log2 = a.scale * LOG2E;
+  d.q_stride = a.q_stride > 0 ? a.q_stride : (long long)a.hq * a.hd;
+  d.out_stride = a.out_stride > 0 ? a.out_stride : (long long)a.hq * a.hd;
+  d.pt_stride = a.pt_stride >= 0 ? a.pt_stride : (long long)a.max_pages;
+  d.pt_rows = a.pt_rows;
   const int tiles = a.hq / gt;
   return a.kv_half ? launch_kv<__half>(d, a.hd, a.batch, tiles, gt, splits, s)
                    : launch_kv<float>(d, a.hd, a.batch, tiles, gt, splits, s);

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
 #error "zeroplatform_b200 kernels are written for sm_100a (B200) only"
 #endif
@@ -47,6 +49,12 @@ __device__ __forceinline__ int4 ld_stream_v4(const void* p) {
   return r;
 }
 
+// Programmatic dependent launch: let the next kernel in the stream start its prologue now, and wait until the
+// previous kernel's memory is visible before touching anything it produced.  Both are no-ops when the kernel
+// was launched without the programmatic-serialization attribute.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ float4 ld_f4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
 
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
@@ -69,6 +77,24 @@ __device__ __forceinline__ void u4x4_to_f32(uint32_t v, float& f0, float& f1, fl
   f1 = __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7651)) - bias;
   f2 = __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7652)) - bias;
   f3 = __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7653)) - bias;
+}
+
+// Launches `kernel` with programmatic stream serialization, so it may overlap the tail of the previous
+// kernel in the stream (the kernel itself calls pdl_wait() before reading that kernel's outputs).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 }  // namespace zc

@@ -1,0 +1,203 @@
+// engine_ops.cu -- small kernels of the device decode step (LlmEngine.ForwardToken / PrefillPrompt pieces).
+//
+//   rope_append_kv   RoPE.ApplyInplace on q and k (Layers/RoPE.cs:131-163) + PagedKvCache.AppendToken /
+//                    AppendTokenAt (Memory/PagedKvCache.cs:237-316) into fp16 pages [page][kv head][slot][hd]
+//   swiglu_rows      SwiGLU.Forward (Layers/SwiGLU.cs:13-51) on [T][gate | up] rows
+//   greedy_sample    LlmSampler.Sample greedy branch with repetition penalty (Sampling/LlmSampler.cs:21-72)
+//   causal_lengths   per-layer causal context lengths (LlmEngine.cs:254, PagedKvCache.cs:139-142)
+//   advance_generation  GenerateStreamAsync bookkeeping between steps (Engine/LlmEngine.cs:115-141)
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace zc {
+
+namespace {
+
+__global__ void rope_append_kernel(float* __restrict__ qkv, int T, int hq, int hkv, int hd,
+                                   const int32_t* __restrict__ pos, const int32_t* __restrict__ rows,
+                                   const int32_t* __restrict__ page_table, int max_pages, int page_size,
+                                   const float* __restrict__ cos_t, const float* __restrict__ sin_t, int max_pos,
+                                   __half* __restrict__ k_pool, __half* __restrict__ v_pool) {
+  const int half = hd / 2;
+  const int q_dim = hq * hd, kv_dim = hkv * hd;
+  const int row_len = q_dim + 2 * kv_dim;
+  const int heads = hq + 2 * hkv;  // q heads, k heads, v heads
+  const size_t total = (size_t)T * heads * half;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int p = (int)(i % half);
+    const int h = (int)((i / half) % heads);
+    const int t = (int)(i / ((size_t)half * heads));
+    const int ps = pos[t];
+    float* row = qkv + (size_t)t * row_len;
+    float* v = row + (size_t)h * hd + 2 * p;  // q, k and v heads are consecutive in the row
+    float x0 = v[0], x1 = v[1];
+    if (h < hq + hkv) {  // rotate q and k
+      const int pc = min(max(ps, 0), max_pos - 1);
+      const float c = cos_t[(size_t)pc * half + p], s = sin_t[(size_t)pc * half + p];
+      const float r0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+      const float r1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+      x0 = r0;
+      x1 = r1;
+      if (h < hq) {
+        v[0] = x0;
+        v[1] = x1;
+        continue;
+      }
+    }
+    // k or v head: append to the page pool
+    const int lp = ps / page_size;
+    if (ps < 0 || lp >= max_pages) continue;
+    const int page = page_table[(size_t)rows[t] * max_pages + lp];
+    if (page < 0) continue;
+    const int kvh = h < hq + hkv ? h - hq : h - hq - hkv;
+    __half* pool = h < hq + hkv ? k_pool : v_pool;
+    const size_t off = (((size_t)page * hkv + kvh) * page_size + (ps % page_size)) * hd + 2 * p;
+    *reinterpret_cast<__half2*>(pool + off) = __floats2half2_rn(x0, x1);
+    if (h < hq + hkv) {  // the rotated k is also kept in the row (used by nothing downstream, kept for tests)
+      v[0] = x0;
+      v[1] = x1;
+    }
+  }
+}
+
+__global__ void swiglu_rows_kernel(const float* __restrict__ gu, float* __restrict__ out, int T, int ffn) {
+  const size_t total = (size_t)T * ffn;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int t = (int)(i / ffn), j = (int)(i % ffn);
+    const float g = gu[(size_t)t * 2 * ffn + j];
+    const float u = gu[(size_t)t * 2 * ffn + ffn + j];
+    const float sg = 1.0f / (1.0f + expf(-g));
+    out[i] = __fmul_rn(__fmul_rn(g, sg), u);
+  }
+}
+
+// One CTA per row.  The penalty is applied occurrence by occurrence, in order, as the reference loops over
+// pastTokens (a token seen c times is divided c times); only thread 0 touches the penalised logits.
+__global__ void greedy_kernel(float* __restrict__ logits, int vocab, const int32_t* __restrict__ past,
+                              const int32_t* __restrict__ past_len, int past_cap, float penalty,
+                              int32_t* __restrict__ out) {
+  float* lg = logits + (size_t)blockIdx.x * vocab;
+  if (penalty > 1.0f && past && past_len) {
+    if (threadIdx.x == 0) {
+      const int n = min(past_len[blockIdx.x], past_cap);
+      const int32_t* pt = past + (size_t)blockIdx.x * past_cap;
+      for (int i = 0; i < n; ++i) {
+        const unsigned tok = (unsigned)pt[i];
+        if (tok < (unsigned)vocab) lg[tok] = lg[tok] > 0 ? lg[tok] / penalty : lg[tok] * penalty;
+      }
+    }
+    __syncthreads();
+  }
+  float best = -INFINITY;
+  int idx = 0x7fffffff;
+  for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
+    const float v = lg[i];
+    if (v > best || (v == best && i < idx)) {
+      best = v;
+      idx = i;
+    }
+  }
+  __shared__ float sb[32];
+  __shared__ int si[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (ob > best || (ob == best && oi < idx)) {
+      best = ob;
+      idx = oi;
+    }
+  }
+  if ((threadIdx.x & 31) == 0) {
+    sb[threadIdx.x >> 5] = best;
+    si[threadIdx.x >> 5] = idx;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float b = sb[0];
+    int bi = si[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+      if (sb[w] > b || (sb[w] == b && si[w] < bi)) {
+        b = sb[w];
+        bi = si[w];
+      }
+    // all-NaN rows keep index 0, as the reference's scan does
+    out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
+  }
+}
+
+__global__ void causal_kernel(const int32_t* __restrict__ pos, int B, int32_t* __restrict__ ex,
+                              int32_t* __restrict__ in) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b < B) {
+    ex[b] = pos[b];
+    in[b] = pos[b] + 1;
+  }
+}
+
+__global__ void advance_kernel(const int32_t* __restrict__ tok, int32_t* __restrict__ pos, int32_t* __restrict__ out,
+                               int32_t* __restrict__ step, int32_t* __restrict__ past, int32_t* __restrict__ past_len,
+                               int past_cap, int eos, int32_t* __restrict__ done) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  if (*done) return;
+  const int t = tok[0];
+  if (eos >= 0 && t == eos) {
+    *done = 1;
+    return;
+  }
+  out[*step] = t;
+  if (*past_len < past_cap) past[*past_len] = t;
+  *past_len += 1;
+  *step += 1;
+}
+
+inline int grid_for(size_t n, int threads) {
+  size_t g = (n + threads - 1) / threads;
+  if (g > 148 * 16) g = 148 * 16;
+  return g < 1 ? 1 : (int)g;
+}
+
+inline int launched() { return cudaPeekAtLastError() == cudaSuccess ? kOk : kCudaError; }
+
+}  // namespace
+
+int rope_append_kv(float* qkv, int T, int hq, int hkv, int hd, const int32_t* pos, const int32_t* rows,
+                   const int32_t* page_table, int max_pages, int page_size, const float* cos_t, const float* sin_t,
+                   int max_pos, __half* k_pool, __half* v_pool, cudaStream_t s) {
+  if (!qkv || !pos || !rows || !page_table || !cos_t || !sin_t || !k_pool || !v_pool || (hd & 1)) return kBadArgument;
+  if (T <= 0) return kOk;
+  const size_t n = (size_t)T * (hq + 2 * hkv) * (hd / 2);
+  rope_append_kernel<<<grid_for(n, 256), 256, 0, s>>>(qkv, T, hq, hkv, hd, pos, rows, page_table, max_pages,
+                                                       page_size, cos_t, sin_t, max_pos, k_pool, v_pool);
+  return launched();
+}
+
+int swiglu_rows(const float* gu, float* out, int T, int ffn, cudaStream_t s) {
+  if (!gu || !out) return kBadArgument;
+  if (T <= 0) return kOk;
+  swiglu_rows_kernel<<<grid_for((size_t)T * ffn, 256), 256, 0, s>>>(gu, out, T, ffn);
+  return launched();
+}
+
+int greedy_sample(float* logits, int rows, int vocab, const int32_t* past, const int32_t* past_len, int past_cap,
+                  float penalty, int32_t* out, cudaStream_t s) {
+  if (!logits || !out || rows <= 0 || vocab <= 0) return kBadArgument;
+  greedy_kernel<<<rows, 1024, 0, s>>>(logits, vocab, past, past_len, past_cap, penalty, out);
+  return launched();
+}
+
+int causal_lengths(const int32_t* pos, int B, int32_t* ctx_excl, int32_t* ctx_incl, cudaStream_t s) {
+  if (!pos || !ctx_excl || !ctx_incl) return kBadArgument;
+  if (B <= 0) return kOk;
+  causal_kernel<<<(B + 255) / 256, 256, 0, s>>>(pos, B, ctx_excl, ctx_incl);
+  return launched();
+}
+
+int advance_generation(const int32_t* tok, int32_t* pos, int32_t* out, int32_t* step, int32_t* past,
+                       int32_t* past_len, int past_cap, int eos, int32_t* done, cudaStream_t s) {
+  advance_kernel<<<1, 32, 0, s>>>(tok, pos, out, step, past, past_len, past_cap, eos, done);
+  return launched();
+}
+
+}  // namespace zc

@@ -61,6 +61,43 @@ struct XPlain {  // x as given
   __device__ __forceinline__ float get(int i, const float*) const { return x[i]; }
 };
 
+// x = RmsNorm(x_raw) * w, fused: RmsNorm.Forward (Layers/RmsNorm.cs:14-59) computed per CTA -- mean of
+// squares in fp32, 1 / (float)sqrt((double)(ms + eps)), then (x * inv) * w as the reference orders it.
+struct XRmsNorm {
+  const float* x;
+  const float* w;
+  float eps;
+  int n;
+  __device__ __forceinline__ void prepare(float* red) const {
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t = 0.f;
+      for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += red[i];
+      red[blockDim.x >> 5] = 1.0f / (float)sqrt((double)(t / (float)n + eps));
+    }
+    __syncthreads();
+  }
+  __device__ __forceinline__ float get(int i, const float* red) const {
+    return __fmul_rn(__fmul_rn(x[i], red[blockDim.x >> 5]), w[i]);
+  }
+};
+
+// x = SwiGLU(gate, up) with gate = gu[0:ffn], up = gu[ffn:2ffn] (SwiGLU.Forward, Layers/SwiGLU.cs:13-51).
+struct XSwiGLU {
+  const float* gu;
+  int ffn;
+  __device__ __forceinline__ void prepare(float*) const {}
+  __device__ __forceinline__ float get(int i, const float*) const {
+    const float g = gu[i];
+    const float sg = 1.0f / (1.0f + expf(-g));
+    return __fmul_rn(__fmul_rn(g, sg), gu[ffn + i]);
+  }
+};
+
 // Chunk geometry: Q8 chunks hold 16 values (4 float4), Q4 chunks hold 32 values (8 float4).
 template <int F4_PER_CHUNK>
 __device__ __forceinline__ int swz(int chunk, int j) {
@@ -114,6 +151,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_q8_0_kernel(const int8_t* _
   extern __shared__ float4 sx[];
   __shared__ float red[GEMV_WARPS + 1];
   constexpr int U = UNROLL;
+  static_assert(GEMV_THREADS / 32 == GEMV_WARPS, "red[] holds one partial per warp plus the result");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = (blockIdx.x * GEMV_WARPS + warp) * R;
   const int kb = K / QK;
@@ -127,8 +165,11 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_q8_0_kernel(const int8_t* _
   for (int k0 = 0; k0 < K; k0 += SEG_Q8) {
     const int len = min(SEG_Q8, K - k0);
     const int nch = len / 16;  // 16-value chunks (half a block)
-    // The first batch of weight loads is issued before x is staged so both are in flight together.
+    // The first batch of weight loads is issued before x is staged so both are in flight together; the
+    // weights do not depend on the previous kernel, so they are issued before the dependency wait.
+    if (k0 == 0) pdl_trigger();
     load_batch<R, U, 16, 2>(w, sc, q, dsc, (size_t)K, kb, row0, N, k0 / 16, k0 / QK, 0, nch, lane);
+    if (k0 == 0) pdl_wait();
     if (k0 > 0) __syncthreads();
     stage_x<4>(sx, xp, k0, len, red);
     __syncthreads();
@@ -186,7 +227,9 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_q4_0_kernel(const uint8_t* 
   for (int k0 = 0; k0 < K; k0 += SEG_Q4) {
     const int len = min(SEG_Q4, K - k0);
     const int nch = len / QK;  // one chunk = one 32-value block = 16 bytes
+    if (k0 == 0) pdl_trigger();
     load_batch<R, U, 16, 1>(w, sc, qs, dsc, (size_t)K / 2, kb, row0, N, k0 / QK, k0 / QK, 0, nch, lane);
+    if (k0 == 0) pdl_wait();
     if (k0 > 0) __syncthreads();
     stage_x<8>(sx, xp, k0, len, red);
     __syncthreads();
@@ -269,8 +312,36 @@ int gemv_q8_0(const int8_t* qs, const uint16_t* d, const float* x, float* y, int
   const int smem = min(k, SEG_Q8) * 4;
   auto kern = gemv_q8_0_kernel<Q8_R, XPlain>;
   if (set_smem(kern, smem) != kOk) return kCudaError;
-  kern<<<grid, GEMV_THREADS, smem, s>>>(qs, d, XPlain{x}, y, n, k, accumulate);
-  return cudaPeekAtLastError() == cudaSuccess ? kOk : kCudaError;
+  return launch_pdl(kern, dim3(grid), dim3(GEMV_THREADS), smem, s, qs, d, XPlain{x}, y, n, k, accumulate) == cudaSuccess
+             ? kOk
+             : kCudaError;
+}
+
+template <class XP>
+static int launch_q8(const int8_t* qs, const uint16_t* d, const XP& xp, float* y, int n, int k, int accumulate,
+                     cudaStream_t s) {
+  if (!qs || !d || !y || n < 0 || k <= 0 || k % QK) return kBadArgument;
+  if (n == 0) return kOk;
+  const int rows_per_cta = GEMV_WARPS * Q8_R;
+  const int grid = (n + rows_per_cta - 1) / rows_per_cta;
+  const int smem = min(k, SEG_Q8) * 4;
+  auto kern = gemv_q8_0_kernel<Q8_R, XP>;
+  if (set_smem(kern, smem) != kOk) return kCudaError;
+  return launch_pdl(kern, dim3(grid), dim3(GEMV_THREADS), smem, s, qs, d, xp, y, n, k, accumulate) == cudaSuccess
+             ? kOk
+             : kCudaError;
+}
+
+int gemv_q8_0_rmsnorm(const int8_t* qs, const uint16_t* d, const float* x, const float* norm_w, float eps, float* y,
+                      int n, int k, int accumulate, cudaStream_t s) {
+  if (!x || !norm_w) return kBadArgument;
+  return launch_q8(qs, d, XRmsNorm{x, norm_w, eps, k}, y, n, k, accumulate, s);
+}
+
+int gemv_q8_0_swiglu(const int8_t* qs, const uint16_t* d, const float* gate_up, float* y, int n, int k,
+                     int accumulate, cudaStream_t s) {
+  if (!gate_up) return kBadArgument;
+  return launch_q8(qs, d, XSwiGLU{gate_up, k}, y, n, k, accumulate, s);
 }
 
 int gemv_q4_0(const uint8_t* qs, const uint16_t* d, const float* x, float* y, int n, int k, int accumulate,
@@ -282,8 +353,9 @@ int gemv_q4_0(const uint8_t* qs, const uint16_t* d, const float* x, float* y, in
   const int smem = min(k, SEG_Q4) * 4;
   auto kern = gemv_q4_0_kernel<Q4_R, XPlain>;
   if (set_smem(kern, smem) != kOk) return kCudaError;
-  kern<<<grid, GEMV_THREADS, smem, s>>>(qs, d, XPlain{x}, y, n, k, accumulate);
-  return cudaPeekAtLastError() == cudaSuccess ? kOk : kCudaError;
+  return launch_pdl(kern, dim3(grid), dim3(GEMV_THREADS), smem, s, qs, d, XPlain{x}, y, n, k, accumulate) == cudaSuccess
+             ? kOk
+             : kCudaError;
 }
 
 }  // namespace zc

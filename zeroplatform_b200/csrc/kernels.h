@@ -21,6 +21,11 @@ int gemv_q8_0(const int8_t* qs, const uint16_t* d, const float* x, float* y, int
               cudaStream_t s);
 int gemv_q4_0(const uint8_t* qs, const uint16_t* d, const float* x, float* y, int n, int k, int accumulate,
               cudaStream_t s);
+// Fused prologues for the decode step: x = RmsNorm(x_raw) * norm_w, or x = SwiGLU(gate_up[0:k], gate_up[k:2k]).
+int gemv_q8_0_rmsnorm(const int8_t* qs, const uint16_t* d, const float* x, const float* norm_w, float eps, float* y,
+                      int n, int k, int accumulate, cudaStream_t s);
+int gemv_q8_0_swiglu(const int8_t* qs, const uint16_t* d, const float* gate_up, float* y, int n, int k,
+                     int accumulate, cudaStream_t s);
 
 // ---- prefill / batched GEMM on tcgen05 (gemm_tc.cu): Y[m][n] (=|+=) X[m][:] . dequant(W)[n][:] ----
 size_t gemm_q8_0_workspace_bytes(int m, int k);
@@ -48,6 +53,10 @@ struct PagedAttnArgs {
   float* workspace;   // split-K partials; may be null when splits == 1
   int* counters;      // [batch*hq] zero-initialised arrival counters (left zeroed); null when splits == 1
   int splits;         // 0 = choose automatically
+  long long q_stride = 0;     // elements between consecutive queries (0: hq*hd)
+  long long out_stride = 0;   // elements between consecutive outputs (0: hq*hd)
+  long long pt_stride = -1;   // elements between page-table rows (-1: max_pages; 0: all queries share row 0)
+  const int32_t* pt_rows = nullptr;  // optional page-table row per query (default: the query index)
 };
 size_t paged_attention_workspace_floats(int batch, int hq, int hd, int splits);
 int paged_attention_choose_splits(int batch, int hkv, int max_ctx, int page_size);
@@ -63,6 +72,25 @@ int rope(float* x, int rows, int heads, int hd, const int32_t* pos, int pos0, co
          const float* sin_t, int max_pos, cudaStream_t s);
 int embed_q8_0(const int8_t* qs, const uint16_t* d, const int32_t* tokens, int n_tokens, int vocab, int dim,
                float* out, cudaStream_t s);
+
+// Decode-step pieces used by the engine (engine_ops.cu).
+// qkv rows [T][q_dim + 2*kv_dim]: rotates q and k of row t at position pos[t] (RoPE.ApplyInplace), then stores
+// k and v as fp16 into the layer's pools [page][kv_head][slot][hd] at page_table[rows[t]][pos/P], pos % P.
+int rope_append_kv(float* qkv, int T, int hq, int hkv, int hd, const int32_t* pos, const int32_t* rows,
+                   const int32_t* page_table, int max_pages, int page_size, const float* cos_t, const float* sin_t,
+                   int max_pos, __half* k_pool, __half* v_pool, cudaStream_t s);
+// out[t][i] = SwiGLU(gu[t][i], gu[t][ffn + i])
+int swiglu_rows(const float* gu, float* out, int T, int ffn, cudaStream_t s);
+// LlmSampler greedy branch per row: repetition penalty over past[row][0:past_len[row]] then argmax
+// (first index wins ties).  penalty <= 1 disables the penalty.  out[row] = token.
+int greedy_sample(float* logits, int rows, int vocab, const int32_t* past, const int32_t* past_len, int past_cap,
+                  float penalty, int32_t* out, cudaStream_t s);
+// ctx_excl[b] = pos[b], ctx_incl[b] = pos[b] + 1 (the reference's per-layer causal lengths).
+int causal_lengths(const int32_t* pos, int B, int32_t* ctx_excl, int32_t* ctx_incl, cudaStream_t s);
+// Generation bookkeeping after a sampled step (B = 1): out[*step] = tok[0]; past[past_len] = tok[0];
+// past_len++; pos[0]++; (*step)++ -- unless a stop token was already produced.
+int advance_generation(const int32_t* tok, int32_t* pos, int32_t* out, int32_t* step, int32_t* past,
+                       int32_t* past_len, int past_cap, int eos, int32_t* done, cudaStream_t s);
 
 int rope_tensorops(float* x, int heads, int seq, int hd, int pos0, float theta, cudaStream_t s);
 int sgemm(int m, int n, int k, float alpha, const float* a, const float* b, float beta, float* c, cudaStream_t s);
