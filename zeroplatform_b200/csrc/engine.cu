@@ -134,9 +134,19 @@ int alloc_weight(Engine* E, DevW& w, int n, int k) {
   return kOk;
 }
 
-// y (=|+=) W x for `rows` activation rows: GEMV for one row, the tensor-core GEMM otherwise.
+// Below this many rows a batched linear runs as one fp32 GEMV per row -- exactly the reference's token-parallel
+// MatVec loop -- and above it on the fp16 tensor cores.
+constexpr int kGemmMinRows = 9;
+
+// y (=|+=) W x for `rows` activation rows.
 int linear(Engine* E, const DevW& w, const float* x, float* y, int rows, int accumulate) {
-  if (rows == 1) return gemv_q8_0(w.qs, w.d, x, y, w.n, w.k, accumulate, E->stream);
+  if (rows < kGemmMinRows) {
+    for (int r = 0; r < rows; ++r) {
+      const int rc = gemv_q8_0(w.qs, w.d, x + (size_t)r * w.k, y + (size_t)r * w.n, w.n, w.k, accumulate, E->stream);
+      if (rc != kOk) return rc;
+    }
+    return kOk;
+  }
   return gemm_q8_0_tc(w.qs, w.d, x, y, rows, w.n, w.k, accumulate, E->gemm_ws, E->gemm_ws_bytes, E->status,
                       E->stream);
 }

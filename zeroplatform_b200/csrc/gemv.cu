@@ -122,7 +122,7 @@ constexpr int GEMV_THREADS = 256;
 constexpr int GEMV_WARPS = GEMV_THREADS / 32;
 constexpr int SEG_Q8 = 8192;   // activations staged per K segment (32 KB of shared memory)
 constexpr int SEG_Q4 = 8192;
-constexpr int UNROLL = 8;      // chunks in flight per lane per row
+constexpr int UNROLL = 8;      // chunks in flight per lane per row (Q4_0)
 
 // Loads one batch of UNROLL chunks per row (and the block scales they need) for lane `lane`.
 template <int R, int U, int CHUNK_BYTES, int CHUNKS_PER_BLOCK>
@@ -143,14 +143,13 @@ __device__ __forceinline__ void load_batch(int4 (&w)[R][U], float (&sc)[R][U], c
     }
 }
 
-template <int R, class XP>
+template <int R, int U, class XP>
 __global__ void __launch_bounds__(GEMV_THREADS) gemv_q8_0_kernel(const int8_t* __restrict__ qs,
                                                                  const uint16_t* __restrict__ dsc, XP xp,
                                                                  float* __restrict__ y, int N, int K,
                                                                  int accumulate) {
   extern __shared__ float4 sx[];
   __shared__ float red[GEMV_WARPS + 1];
-  constexpr int U = UNROLL;
   static_assert(GEMV_THREADS / 32 == GEMV_WARPS, "red[] holds one partial per warp plus the result");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = (blockIdx.x * GEMV_WARPS + warp) * R;
@@ -300,36 +299,34 @@ static int set_smem(Kern k, int bytes) {
   return kOk;
 }
 
-constexpr int Q8_R = 2;
 constexpr int Q4_R = 4;
 
-int gemv_q8_0(const int8_t* qs, const uint16_t* d, const float* x, float* y, int n, int k, int accumulate,
-              cudaStream_t s) {
-  if (!qs || !d || !x || !y || n < 0 || k <= 0 || k % QK) return kBadArgument;
-  if (n == 0) return kOk;
-  const int rows_per_cta = GEMV_WARPS * Q8_R;
-  const int grid = (n + rows_per_cta - 1) / rows_per_cta;
-  const int smem = min(k, SEG_Q8) * 4;
-  auto kern = gemv_q8_0_kernel<Q8_R, XPlain>;
-  if (set_smem(kern, smem) != kOk) return kCudaError;
-  return launch_pdl(kern, dim3(grid), dim3(GEMV_THREADS), smem, s, qs, d, XPlain{x}, y, n, k, accumulate) == cudaSuccess
-             ? kOk
-             : kCudaError;
-}
-
+// Rows per warp (R) and 16-byte chunks per lane per row (U) for a row of K int8 values: R * U stays at 16
+// loads in flight per lane, so short rows (K = 768: 48 chunks) still keep ~8 KB per warp in flight.
 template <class XP>
 static int launch_q8(const int8_t* qs, const uint16_t* d, const XP& xp, float* y, int n, int k, int accumulate,
                      cudaStream_t s) {
   if (!qs || !d || !y || n < 0 || k <= 0 || k % QK) return kBadArgument;
   if (n == 0) return kOk;
-  const int rows_per_cta = GEMV_WARPS * Q8_R;
-  const int grid = (n + rows_per_cta - 1) / rows_per_cta;
   const int smem = min(k, SEG_Q8) * 4;
-  auto kern = gemv_q8_0_kernel<Q8_R, XP>;
-  if (set_smem(kern, smem) != kOk) return kCudaError;
-  return launch_pdl(kern, dim3(grid), dim3(GEMV_THREADS), smem, s, qs, d, xp, y, n, k, accumulate) == cudaSuccess
-             ? kOk
-             : kCudaError;
+  const int chunks = min(k, SEG_Q8) / 16;
+  auto go = [&](auto kern, int r) -> int {
+    if (set_smem(kern, smem) != kOk) return kCudaError;
+    const int rows_per_cta = GEMV_WARPS * r;
+    const int grid = (n + rows_per_cta - 1) / rows_per_cta;
+    return launch_pdl(kern, dim3(grid), dim3(GEMV_THREADS), smem, s, qs, d, xp, y, n, k, accumulate) == cudaSuccess
+               ? kOk
+               : kCudaError;
+  };
+  if (chunks > 64) return go(gemv_q8_0_kernel<2, 8, XP>, 2);  // K >= 1056
+  if (chunks > 32) return go(gemv_q8_0_kernel<8, 2, XP>, 8);  // K in (512, 1024]
+  return go(gemv_q8_0_kernel<16, 1, XP>, 16);                 // K <= 512
+}
+
+int gemv_q8_0(const int8_t* qs, const uint16_t* d, const float* x, float* y, int n, int k, int accumulate,
+              cudaStream_t s) {
+  if (!x) return kBadArgument;
+  return launch_q8(qs, d, XPlain{x}, y, n, k, accumulate, s);
 }
 
 int gemv_q8_0_rmsnorm(const int8_t* qs, const uint16_t* d, const float* x, const float* norm_w, float eps, float* y,
