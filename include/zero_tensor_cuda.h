@@ -87,6 +87,23 @@ ZC_API int32_t zcu_paged_attention(const float* q, const void* k_pool, const voi
                             int64_t page_stride, int64_t slot_stride, int64_t head_stride, float scale,
                             int32_t max_ctx, void* stream);
 
+/* The same paged attention for callers that cannot allocate device memory when they run it -- a caller
+ * recording a CUDA graph (cudaMalloc is not allowed while a stream is captured), a server that gave all free
+ * HBM to its KV page pool, or a decode loop that forbids allocation after start-up.  No counterpart in the
+ * reference (its managed fallback allocates nothing on a device).  Same arguments as zcu_paged_attention;
+ * the split-K scratch is a fixed 1 MiB array inside the library (held by every GPU that loads it until the
+ * process exits), so shapes needing more than 8,192 arrival counters (batch * hq) or 253,952 partial floats
+ * (batch * hq * splits * (hd + 2)) return -6 with a message in zc_cuda_last_error().  It never calls
+ * cudaMalloc or cudaFree.  The first call on a device looks the array up (cudaGetSymbolAddress): make it
+ * before any stream capture.  All calls on a device share the array: calls whose kernels overlap on the GPU
+ * race (calls on one stream are ordered); each call clears the counters it uses before launching. */
+ZC_API int32_t zcu_paged_attention_noalloc(const float* q, const void* k_pool, const void* v_pool, int32_t kv_dtype,
+                                           const int32_t* page_table, const int32_t* ctx_len, float* out,
+                                           int32_t batch, int32_t hq, int32_t hkv, int32_t hd, int32_t page_size,
+                                           int32_t max_pages, int32_t num_pages, int64_t page_stride,
+                                           int64_t slot_stride, int64_t head_stride, float scale, int32_t max_ctx,
+                                           void* stream);
+
 /* RmsNorm.Forward (Layers/RmsNorm.cs:14-59) on `rows` rows of n elements. */
 ZC_API int32_t zcu_rmsnorm(const float* x, const float* w, float* out, int32_t rows, int32_t n, float eps, void* stream);
 /* SwiGLU.Forward (Layers/SwiGLU.cs:13-51). */

@@ -48,6 +48,8 @@ SIGNATURES = {
     "zcu_device_status": (i32, [i32]),
     "zcu_paged_attention": (i32, [vp, vp, vp, i32, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, i64, i64, i64,
                                   f32, i32, vp]),
+    "zcu_paged_attention_noalloc": (i32, [vp, vp, vp, i32, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, i64, i64,
+                                          i64, f32, i32, vp]),
     "zcu_rmsnorm": (i32, [vp, vp, vp, i32, i32, f32, vp]),
     "zcu_swiglu": (i32, [vp, vp, vp, sz, vp]),
     "zcu_rope": (i32, [vp, i32, i32, i32, vp, i32, vp, vp, i32, vp]),

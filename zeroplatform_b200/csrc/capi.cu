@@ -259,6 +259,10 @@ int gemv_host(int qtype, const uint8_t* w, const float* x, float* y, size_t n, s
 
 }  // namespace
 
+namespace zc {
+void set_last_error(const std::string& msg) { t_last_error = msg; }
+}  // namespace zc
+
 extern "C" {
 
 // ------------------------------------------------------------------------------------------
