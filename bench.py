@@ -176,6 +176,106 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+
+# ----------------------------------------------------------------------------------------------------------
+# Other configurations, reported beside the headline (same run, same GPU)
+# ----------------------------------------------------------------------------------------------------------
+def _peak_tflops():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured bf16 dense (fp16 runs at the same rate)"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def prefill_gemm_leg(dev, L, iters=20):
+    """Batched prefill GEMM: X fp32 [512, 4096] ~ N(0,1), W Q8_0 [11008, 4096] ~ N(0,0.02)."""
+    import torch
+    from zeroplatform_b200.ops import QuantizedWeight, quantize
+    M, N, K = 512, 11008, 4096
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    w = QuantizedWeight.upload(8, quantize(8, torch.randn((N, K), generator=g, device=dev) * 0.02), N, K, device=dev)
+    x = torch.randn((M, K), generator=g, device=dev)
+    y = torch.empty((M, N), device=dev)
+    s = torch.cuda.current_stream()
+
+    def run():
+        if L.zcu_gemm_q8_0(w.qs.data_ptr(), w.d.data_ptr(), x.data_ptr(), y.data_ptr(), M, N, K, 0, s.cuda_stream):
+            raise RuntimeError("zcu_gemm_q8_0 failed")
+
+    for _ in range(3):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(iters):
+        run()
+    e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / iters
+    flops = 2.0 * M * N * K
+    peak, src = _peak_tflops()
+    tf = flops / (ms * 1e-3) / 1e12
+    status = L.zcu_device_status(1)
+    return {"ms": round(ms, 4), "tflops": round(tf, 1), "weight_GBs": round(w.nbytes / (ms * 1e-3) / 1e9, 1),
+            "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(tf / peak, 3), "peak_source": src},
+            "note": "fp16(q*d) x fp16(x) on tcgen05 kind::f16, fp32 accumulate; includes the fp32->fp16 "
+                    "activation conversion kernel", "device_status": status}
+
+
+def decode_12l_leg(dev, with_cpu, n_prompt=512, n_new=128):
+    """BASELINE config 2: 12 layers, d 768, 12 heads x 64, SwiGLU 2048, vocab 32000, Q8_0 from N(0,0.02);
+    512 random prompt ids then 128 greedy tokens (repetition penalty 1.0), 16-token fp16 KV pages."""
+    import numpy as np
+    import torch
+    from zeroplatform_b200.engine import LlmEngine
+    from zeroplatform_b200.ops import quantize
+    vocab, dim, layers, heads, ffn = 32000, 768, 12, 12, 2048
+    g = torch.Generator(device=dev)
+    g.manual_seed(11)
+
+    def q8(rows, cols, n=None):
+        shape = (rows, cols) if n is None else (n, rows, cols)
+        return quantize(8, torch.randn(shape, generator=g, device=dev) * 0.02).cpu().numpy()
+
+    m = dict(vocab=vocab, dim=dim, layers=layers, heads=heads, kv_heads=heads, ffn=ffn, context_length=2048, eps=1e-5,
+             rope_base=10000.0, tok_emb=q8(vocab, dim), lm_head=q8(vocab, dim), wq=q8(dim, dim, layers),
+             wk=q8(dim, dim, layers), wv=q8(dim, dim, layers), wo=q8(dim, dim, layers), wgate=q8(ffn, dim, layers),
+             wup=q8(ffn, dim, layers), wdown=q8(dim, ffn, layers),
+             attn_norm=np.ones((layers, dim), np.float32), ffn_norm=np.ones((layers, dim), np.float32),
+             final_norm=np.ones(dim, np.float32))
+    prompt = np.random.default_rng(5).integers(0, vocab, n_prompt).astype(np.int32)
+    e = LlmEngine(m, total_pages=64, page_size=16, max_batch=1, max_pages_per_seq=64, max_prefill_tokens=n_prompt)
+    e.generate_greedy(0, prompt, 8)            # warm-up: captures the decode-step graph
+    e.free_sequence(0)
+    toks, pre_ms, dec_ms = e.generate_greedy(1, prompt, n_new)
+    e.close()
+    # packed Q8_0 bytes streamed per decode token (every projection and the LM head; one embedding row)
+    weight_bytes = sum(int(np.prod(m[k].shape)) for k in ("lm_head", "wq", "wk", "wv", "wo", "wgate", "wup", "wdown"))
+    out = {"prefill_ms": round(pre_ms, 3), "decode_ms": round(dec_ms, 3),
+           "decode_tok_s": round(n_new / (dec_ms * 1e-3), 1), "prompt_tok_s": round(n_prompt / (pre_ms * 1e-3), 1),
+           "tokens": int(len(toks)), "weight_bytes_per_token": int(weight_bytes),
+           "decode_weight_GBs": round(weight_bytes * n_new / (dec_ms * 1e-3) / 1e9, 1)}
+    if with_cpu:  # the oracle LlmEngine (C++ restatement of the reference C#) on the host cores, bounded sample
+        import oracle as O
+        ref = O.Engine(m, total_pages=64, page_size=16)
+        t0 = time.perf_counter()
+        logits = ref.prefill(1, prompt[:64], 0)
+        t1 = time.perf_counter()
+        n_cpu = 16
+        tok = int(np.argmax(logits))
+        for i in range(n_cpu):
+            logits = ref.forward_token(1, tok, 64 + i)
+            tok = int(np.argmax(logits))
+        t2 = time.perf_counter()
+        ref.close()
+        out["cpu"] = {"decode_tok_s": round(n_cpu / (t2 - t1), 2), "prompt_tok_s": round(64 / (t1 - t0), 2),
+                      "cores": O.lib().orc_num_threads(), "kind": "port",
+                      "sample": f"oracle LlmEngine: 64-token prompt then {n_cpu} greedy decode steps (context 64-80)"}
+    return out
+
 # ----------------------------------------------------------------------------------------------------------
 # GPU arm
 # ----------------------------------------------------------------------------------------------------------
@@ -315,6 +415,16 @@ def run_ours(args):
     except Exception as ex:  # keep the device-timed line even if an e2e leg fails
         e2e, e2e_copy = {"value": None, "unit": "GB/s", "error": str(ex)[:200]}, None
 
+    extra = {}
+    if not args.no_extra:
+        try:
+            extra["prefill_gemm_512x11008x4096"] = prefill_gemm_leg(dev, L)
+        except Exception as ex:
+            extra["prefill_gemm_512x11008x4096"] = {"error": str(ex)[:200]}
+        try:
+            extra["decode_12l_d768"] = decode_12l_leg(dev, rank == 0 and world == 1 and not args.no_cpu)
+        except Exception as ex:
+            extra["decode_12l_d768"] = {"error": str(ex)[:200]}
     cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu) else None
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -330,7 +440,7 @@ def run_ours(args):
                              "traffic": NCU_TRAFFIC_BYTES, "algorithmic_bytes_per_launch": ALGO_BYTES,
                              "kernel": "gemv_q8_0_kernel", "launch_us": round(launch_s * 1e6, 3)},
                 "e2e": e2e, "e2e_weights_copied_per_call": e2e_copy, "gpu_launches": launches,
-                "clocks": sampler.summary(), "cpu_baseline": cpu}
+                "clocks": sampler.summary(), "cpu_baseline": cpu, "extra_configs": extra}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -344,6 +454,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-extra", action="store_true", help="skip the prefill-GEMM and decoder legs")
     ap.add_argument("--min-warmup-s", type=float, default=1.0,
                     help="keep warming up for at least this long (clock samples under load)")
     args = ap.parse_args()
