@@ -37,9 +37,9 @@ ALGO_BYTES = QBYTES + COLS * 4 + ROWS * 4        # + x read + y written
 AOS_BYTES = ROWS * (COLS // 32) * 34             # the reference's packed weight bytes
 # Published CPU figure for this exact GEMV (ZeroTensor/README.md:198-203): 3.79 ms for the 17.8 MB weight.
 PUBLISHED_GBS = AOS_BYTES / 3.79e-3 / 1e9
-# dram__bytes_read.sum + dram__bytes_write.sum of one gemv_q8_0_kernel launch, from the ncu capture summarised
-# in profiles/gemv_q8_0_4096x4096.md (None until that capture exists).
-NCU_TRAFFIC_BYTES = None
+# dram__bytes_read.sum + dram__bytes_write.sum of one gemv_q8_0_kernel launch of this workload, from the ncu
+# capture summarised in profiles/gemv_q8_0_4096x4096.md (17,873,920 read + 0 written).
+NCU_TRAFFIC_BYTES = 17873920
 
 
 def _peaks():
