@@ -27,7 +27,8 @@ def _run(qw, x, y, accumulate=False):
 
 
 @pytest.mark.parametrize("m,n,k", [(1, 128, 64), (5, 200, 96), (64, 256, 768), (100, 384, 2048), (130, 1000, 4096),
-                                   (257, 128, 128), (512, 11008, 4096)])
+                                   (257, 128, 128), (512, 11008, 4096), (32, 4096, 4096), (32, 4096, 11008),
+                                   (9, 2304, 768), (128, 11008, 4096), (33, 96, 4096)])
 def test_gemm_matches_oracle(m, n, k):
     from zeroplatform_b200.ops import QuantizedWeight
     rng = np.random.default_rng(m * 7 + n + k)

@@ -591,7 +591,7 @@ int32_t zcu_gemm_q8_0(const int8_t* qs, const uint16_t* d, const float* x, float
   cudaStream_t s = as_stream(stream);
   void* ws;
   int* status;
-  const size_t bytes = gemm_q8_0_workspace_bytes((int)m, (int)k_cols);
+  const size_t bytes = gemm_q8_0_workspace_bytes((int)m, (int)n_rows, (int)k_cols);
   ZC_RC(stream_scratch(s, 2, bytes, false, &ws));
   ZC_RC(device_status_ptr(&status));
   return gemm_q8_0_tc(qs, d, x, y, (int)m, (int)n_rows, (int)k_cols, accumulate, ws, bytes, status, s);

@@ -401,7 +401,14 @@ int32_t zcu_engine_create(const zcu_engine_config* cfg, void* stream, void** out
   step(dalloc(E, &E->attn_ws, std::max<size_t>(16, paged_attention_workspace_floats(c.max_batch, c.heads, hd,
                                                                                    E->attn_splits))));
   step(dalloc(E, &E->attn_ctr, (size_t)R * c.heads));
-  E->gemm_ws_bytes = gemm_q8_0_workspace_bytes(R, std::max(c.dim, std::max(c.ffn, E->q_dim)));
+  {  // the largest workspace any batched linear of this engine can ask for
+    const int shapes[5][2] = {{E->qkv_dim, c.dim}, {c.dim, E->q_dim}, {2 * c.ffn, c.dim}, {c.dim, c.ffn}, {c.vocab, c.dim}};
+    size_t ws = 0;
+    for (auto& sh : shapes)
+      for (int rows_m : {R, c.max_batch, kGemmMinRows, std::min(R, 128)})
+        if (rows_m >= kGemmMinRows) ws = std::max(ws, gemm_q8_0_workspace_bytes(rows_m, sh[0], sh[1]));
+    E->gemm_ws_bytes = std::max<size_t>(ws, 256);
+  }
   step(dalloc(E, reinterpret_cast<uint8_t**>(&E->gemm_ws), E->gemm_ws_bytes));
   step(dalloc(E, &E->status, 1));
   E->gen_cap = c.max_pages_per_seq * c.page_size + 16;

@@ -31,24 +31,27 @@ namespace zc {
 
 namespace {
 
-constexpr int BM = 128;                  // weight rows per tile = MMA M = TMEM lanes
-constexpr int BK = 64;                   // k per stage: 64 fp16 = one 128-byte swizzle row
-constexpr int STAGES = 4;
-constexpr int GEMM_THREADS = 320;
-constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KB
+constexpr int BM = 128;                   // weight rows per tile = MMA M = TMEM lanes
+constexpr int BK = 64;                    // k per stage: 64 fp16 = one 128-byte swizzle row
+constexpr int WSTAGES = 8;                // raw int8 weight tiles in flight (TMA ring)
+constexpr int GEMM_THREADS = 384;         // 12 warps, roles below
+constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KB of fp16 A per stage
+constexpr int W_STAGE_BYTES = BM * BK;      // 8 KB of int8 W per stage
 constexpr uint32_t WAIT_LIMIT = 1u << 24;    // try_wait polls before a wait is declared hung
 constexpr uint64_t WAIT_NS = 2000000000ull;  // ... or two seconds
 
 struct GemmParams {
-  const int8_t* qs;
   const uint16_t* d;
-  float* y;
+  float* y;         // output, or split partials [splits][M][N] when splits > 1
   int* status;
   int M, N, K;
   int accumulate;
-  int bn;          // tokens per tile (MMA N): 64, 128 or 256
+  int bn;           // tokens per tile (MMA N): 32, 64, 128 or 256
+  int ab_stages;    // A/B pipeline depth (3 for bn = 256, else 4)
   int n_tok_tiles;
-  int n_tiles;
+  int n_tiles;      // output tiles
+  int splits;       // K ranges per tile (split-K); work units = n_tiles * splits
+  int kb_per_split;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -181,29 +184,39 @@ __device__ __forceinline__ void dequant16(int4 w, __half2 d2, uint4& lo, uint4& 
 }
 
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
-    gemm_q8_0_tc_kernel(const __grid_constant__ CUtensorMap x_map, GemmParams p) {
+    gemm_q8_0_tc_kernel(const __grid_constant__ CUtensorMap x_map, const __grid_constant__ CUtensorMap w_map,
+                        GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int bn = p.bn;
+  const int AST = p.ab_stages;
   const int b_stage_bytes = bn * BK * 2;
-  uint8_t* a_st = smem;                                   // STAGES x 16 KB
-  uint8_t* b_st = smem + STAGES * A_STAGE_BYTES;          // STAGES x bn*128 B
-  uint64_t* bars = reinterpret_cast<uint64_t*>(b_st + STAGES * b_stage_bytes);
-  uint64_t* full = bars;                 // [STAGES]
-  uint64_t* empty = bars + STAGES;       // [STAGES]
-  uint64_t* tfull = bars + 2 * STAGES;   // [2]
-  uint64_t* tempty = bars + 2 * STAGES + 2;
-  uint64_t* drain = bars + 2 * STAGES + 4;  // [1] completion of every MMA this CTA issued
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  uint8_t* a_st = smem;                                  // AST x 16 KB (fp16 A, SW128)
+  uint8_t* b_st = a_st + AST * A_STAGE_BYTES;            // AST x bn*128 B (fp16 X, SW128 by TMA)
+  uint8_t* w_st = b_st + AST * b_stage_bytes;            // WSTAGES x 8 KB (int8 W, TMA, unswizzled)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(w_st + WSTAGES * W_STAGE_BYTES);
+  uint64_t* ab_full = bars;                      // [AST]: 128 dequant arrivals + 1 X TMA (tx)
+  uint64_t* ab_empty = bars + 4;                 // [AST]: MMA commit
+  uint64_t* w_full = bars + 8;                   // [WSTAGES]: W TMA (tx)
+  uint64_t* w_empty = bars + 8 + WSTAGES;        // [WSTAGES]: 128 dequant arrivals
+  uint64_t* tfull = bars + 8 + 2 * WSTAGES;      // [2]
+  uint64_t* tempty = tfull + 2;                  // [2]
+  uint64_t* drain = tempty + 2;                  // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nk = (p.K + BK - 1) / BK;
+  const int n_units = p.n_tiles * p.splits;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(smem_u32(&full[s]), 128 + 1);
-      mbar_init(smem_u32(&empty[s]), 1);
+    for (int s = 0; s < AST; ++s) {
+      mbar_init(smem_u32(&ab_full[s]), 128 + 1);
+      mbar_init(smem_u32(&ab_empty[s]), 1);
+    }
+    for (int s = 0; s < WSTAGES; ++s) {
+      mbar_init(smem_u32(&w_full[s]), 1);
+      mbar_init(smem_u32(&w_empty[s]), 128);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(smem_u32(&tfull[a]), 1);
@@ -214,7 +227,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
-  if (warp == 1) {  // allocate 2 accumulators of bn fp32 columns (power of two >= 32)
+  if (warp == 1) {  // 2 accumulators of bn fp32 columns (power of two >= 32)
     const uint32_t ncols = 2u * (uint32_t)bn;
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(ncols));
@@ -225,24 +238,47 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  // Work unit u -> output tile u / splits (weight tile major), K range (u % splits).
+  auto unit_tile = [&](int u) { return u / p.splits; };
+  auto unit_kb0 = [&](int u) { return (u % p.splits) * p.kb_per_split; };
+  auto unit_kb1 = [&](int u) { return min(nk, (u % p.splits + 1) * p.kb_per_split); };
+
   if (warp == 0) {
-    // ---------------- TMA producer for the activation tiles ----------------
+    // ---------------- TMA producer: raw int8 weight tiles [128 rows x 64 k] ----------------
     if (lane == 0) {
       int s = 0;
       uint32_t ph = 0;
-      for (int t = blockIdx.x; t < p.n_tiles && !*abort_flag; t += gridDim.x) {
-        const int tok0 = (t % p.n_tok_tiles) * bn;
-        for (int kb = 0; kb < nk; ++kb) {
-          if (!mbar_wait(smem_u32(&empty[s]), ph ^ 1, abort_flag, p.status, 1)) break;
-          mbar_arrive_tx(smem_u32(&full[s]), (uint32_t)b_stage_bytes);
-          tma_load_2d(smem_u32(b_st + s * b_stage_bytes), &x_map, kb * BK, tok0, smem_u32(&full[s]));
-          if (++s == STAGES) {
+      for (int u = blockIdx.x; u < n_units && !*abort_flag; u += gridDim.x) {
+        const int row0 = (unit_tile(u) / p.n_tok_tiles) * BM;
+        for (int kb = unit_kb0(u); kb < unit_kb1(u); ++kb) {
+          if (!mbar_wait(smem_u32(&w_empty[s]), ph ^ 1, abort_flag, p.status, 1)) break;
+          mbar_arrive_tx(smem_u32(&w_full[s]), (uint32_t)W_STAGE_BYTES);
+          tma_load_2d(smem_u32(w_st + s * W_STAGE_BYTES), &w_map, kb * BK, row0, smem_u32(&w_full[s]));
+          if (++s == WSTAGES) {
             s = 0;
             ph ^= 1;
           }
         }
       }
-      // On an abort, loads already issued may still be landing in shared memory: let them finish.
+      if (*abort_flag) __nanosleep(20000);  // let issued loads land before the CTA can exit
+    }
+  } else if (warp == 2) {
+    // ---------------- TMA producer: fp16 activation tiles [bn tokens x 64 k] ----------------
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      for (int u = blockIdx.x; u < n_units && !*abort_flag; u += gridDim.x) {
+        const int tok0 = (unit_tile(u) % p.n_tok_tiles) * bn;
+        for (int kb = unit_kb0(u); kb < unit_kb1(u); ++kb) {
+          if (!mbar_wait(smem_u32(&ab_empty[s]), ph ^ 1, abort_flag, p.status, 6)) break;
+          mbar_arrive_tx(smem_u32(&ab_full[s]), (uint32_t)b_stage_bytes);
+          tma_load_2d(smem_u32(b_st + s * b_stage_bytes), &x_map, kb * BK, tok0, smem_u32(&ab_full[s]));
+          if (++s == AST) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+      }
       if (*abort_flag) __nanosleep(20000);
     }
   } else if (warp == 1) {
@@ -252,15 +288,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       int s = 0;
       uint32_t ph = 0;
       int it = 0;
-      for (int t = blockIdx.x; t < p.n_tiles && !*abort_flag; t += gridDim.x, ++it) {
+      for (int u = blockIdx.x; u < n_units && !*abort_flag; u += gridDim.x, ++it) {
         const int acc = it & 1;
         const uint32_t acc_ph = (uint32_t)(it >> 1) & 1;
         if (!mbar_wait(smem_u32(&tempty[acc]), acc_ph ^ 1, abort_flag, p.status, 2)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * bn);
         bool ok = true;
-        for (int kb = 0; kb < nk; ++kb) {
-          if (!mbar_wait(smem_u32(&full[s]), ph, abort_flag, p.status, 3)) {
+        const int kb0 = unit_kb0(u);
+        for (int kb = kb0; kb < unit_kb1(u); ++kb) {
+          if (!mbar_wait(smem_u32(&ab_full[s]), ph, abort_flag, p.status, 3)) {
             ok = false;
             break;
           }
@@ -270,10 +307,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
             umma_f16(d_tmem, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32), idesc,
-                     (kb | kk) != 0 ? 1u : 0u);
+                     (kb != kb0 || kk != 0) ? 1u : 0u);
           }
-          umma_commit(smem_u32(&empty[s]));  // frees the stage once these MMAs have read it
-          if (++s == STAGES) {
+          umma_commit(smem_u32(&ab_empty[s]));  // frees the A/B stage once these MMAs have read it
+          if (++s == AST) {
             s = 0;
             ph ^= 1;
           }
@@ -287,46 +324,60 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       while (!mbar_try(smem_u32(drain), 0) && global_ns() - t0 < WAIT_NS) {
       }
     }
-  } else if (warp < 6) {
-    // ---------------- W dequantizers (128 threads) ----------------
-    const int tid = threadIdx.x - 64;  // 0..127
+  } else if (warp >= 4 && warp < 8) {
+    // ---------------- W dequantizers (128 threads): int8 tile in smem -> fp16(q*d) in the SW128 layout ----------------
+    const int tid = threadIdx.x - 128;  // 0..127
     const int kblocks = p.K / QK;
-    int s = 0;
-    uint32_t ph = 0;
-    for (int t = blockIdx.x; t < p.n_tiles && !*abort_flag; t += gridDim.x) {
-      const int row0 = (t / p.n_tok_tiles) * BM;
-      // items: (row, 16-value chunk) pairs; 4 consecutive threads cover one row's 64 values
-      int4 wv[4];
-      __half2 dv[4];
-      auto load = [&](int kb) {
+    int ws = 0, as = 0;
+    uint32_t wph = 0, aph = 0;
+    for (int u = blockIdx.x; u < n_units && !*abort_flag; u += gridDim.x) {
+      const int row0 = (unit_tile(u) / p.n_tok_tiles) * BM;
+      const int kb0 = unit_kb0(u), kb1 = unit_kb1(u);
+      // items: (row, 16-value chunk); 4 consecutive threads cover one row's 64 values
+      auto load_scales = [&](int kb, __half2 (&dv)[4]) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int item = tid + 128 * j;
-          const int r = item >> 2, c = item & 3;
-          const int row = row0 + r;
-          const int k = kb * BK + c * 16;
-          if (row < p.N && k < p.K) {
-            wv[j] = ld_stream_v4(p.qs + (size_t)row * p.K + k);
-            const __half h = __ushort_as_half(__ldg(p.d + (size_t)row * kblocks + (k >> 5)));
-            dv[j] = __halves2half2(h, h);
-          } else {
-            wv[j] = make_int4(0, 0, 0, 0);
-            dv[j] = __float2half2_rn(0.f);
-          }
+          const int row = row0 + (item >> 2);
+          const int k = kb * BK + (item & 3) * 16;
+          const __half h = (kb < kb1 && row < p.N && k < p.K) ? __ushort_as_half(__ldg(p.d + (size_t)row * kblocks + (k >> 5)))
+                                                              : __ushort_as_half((unsigned short)0);
+          dv[j] = __halves2half2(h, h);
         }
       };
-      load(0);
-      for (int kb = 0; kb < nk; ++kb) {
-        int4 cw[4];
+      __half2 d0[4], d1[4], d2[4], d3[4];  // scales for stages kb .. kb+3 (register ring)
+      load_scales(kb0, d0);
+      load_scales(kb0 + 1, d1);
+      load_scales(kb0 + 2, d2);
+      load_scales(kb0 + 3, d3);
+      bool stop = false;
+      for (int kb = kb0; kb < kb1 && !stop; ++kb) {
+        // take this stage's scales, then refill the ring slot with the stage 4 ahead
         __half2 cd[4];
 #pragma unroll
+        for (int j = 0; j < 4; ++j) cd[j] = d0[j];
+#pragma unroll
         for (int j = 0; j < 4; ++j) {
-          cw[j] = wv[j];
-          cd[j] = dv[j];
+          d0[j] = d1[j];
+          d1[j] = d2[j];
+          d2[j] = d3[j];
         }
-        if (kb + 1 < nk) load(kb + 1);  // next stage's loads overlap this stage's wait and conversion
-        if (!mbar_wait(smem_u32(&empty[s]), ph ^ 1, abort_flag, p.status, 4)) break;
-        uint8_t* a = a_st + s * A_STAGE_BYTES;
+        load_scales(kb + 4, d3);
+        if (!mbar_wait(smem_u32(&w_full[ws]), wph, abort_flag, p.status, 4)) break;
+        int4 cw[4];
+        const uint8_t* wsrc = w_st + ws * W_STAGE_BYTES;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) cw[j] = *reinterpret_cast<const int4*>(wsrc + (tid + 128 * j) * 16);
+        mbar_arrive(smem_u32(&w_empty[ws]));  // the raw tile is in registers: release it to the TMA producer
+        if (++ws == WSTAGES) {
+          ws = 0;
+          wph ^= 1;
+        }
+        if (!mbar_wait(smem_u32(&ab_empty[as]), aph ^ 1, abort_flag, p.status, 5)) {
+          stop = true;
+          break;
+        }
+        uint8_t* a = a_st + as * A_STAGE_BYTES;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int item = tid + 128 * j;
@@ -339,25 +390,28 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           *reinterpret_cast<uint4*>(line + (((2 * c + 1) ^ (r & 7)) << 4)) = hi;
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        mbar_arrive(smem_u32(&full[s]));
-        if (++s == STAGES) {
-          s = 0;
-          ph ^= 1;
+        mbar_arrive(smem_u32(&ab_full[as]));
+        if (++as == AST) {
+          as = 0;
+          aph ^= 1;
         }
       }
     }
-  } else {
-    // ---------------- epilogue (warps 6..9 -> TMEM lane quadrants 2, 3, 0, 1) ----------------
+  } else if (warp >= 8) {
+    // ---------------- epilogue (warps 8..11 -> TMEM lane quadrants 0..3) ----------------
     const int quad = warp & 3;
     const int row_in_tile = quad * 32 + lane;
     int it = 0;
-    for (int t = blockIdx.x; t < p.n_tiles && !*abort_flag; t += gridDim.x, ++it) {
+    for (int u = blockIdx.x; u < n_units && !*abort_flag; u += gridDim.x, ++it) {
       const int acc = it & 1;
       const uint32_t acc_ph = (uint32_t)(it >> 1) & 1;
-      if (!mbar_wait(smem_u32(&tfull[acc]), acc_ph, abort_flag, p.status, 5)) break;
+      if (!mbar_wait(smem_u32(&tfull[acc]), acc_ph, abort_flag, p.status, 7)) break;
       tc_fence_after();
+      const int t = unit_tile(u);
       const int row = (t / p.n_tok_tiles) * BM + row_in_tile;
       const int tok0 = (t % p.n_tok_tiles) * bn;
+      float* out = p.splits > 1 ? p.y + (size_t)(u % p.splits) * p.M * p.N : p.y;
+      const bool acc_mode = p.splits == 1 && p.accumulate;
       for (int c0 = 0; c0 < bn; c0 += 32) {
         uint32_t r[32];
         tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * bn + c0), r);
@@ -366,9 +420,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           for (int j = 0; j < 32; ++j) {
             const int m = tok0 + c0 + j;
             if (m < p.M) {
-              float* yp = p.y + (size_t)m * p.N + row;
+              float* yp = out + (size_t)m * p.N + row;
               const float v = __uint_as_float(r[j]);
-              *yp = p.accumulate ? *yp + v : v;
+              *yp = acc_mode ? *yp + v : v;
             }
           }
         }
@@ -378,12 +432,22 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
   }
 
-  // Drain: on an abort, wait (bounded) for the MMAs already committed so TMEM is idle before freeing it.
+  // Drain: TMEM is idle once the MMA thread's drain commit flipped (or timed out); free it.
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(2u * (uint32_t)bn));
+  }
+}
+
+// Split-K reduction in a fixed order (deterministic): y (=|+=) sum_s part[s].
+__global__ void splitk_reduce_kernel(const float* __restrict__ part, float* __restrict__ y, size_t mn, int splits,
+                                     int accumulate) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < mn; i += (size_t)gridDim.x * blockDim.x) {
+    float v = part[i];
+    for (int s = 1; s < splits; ++s) v += part[(size_t)s * mn + i];
+    y[i] = accumulate ? y[i] + v : v;
   }
 }
 
@@ -426,54 +490,118 @@ int num_sms() {
   return n;
 }
 
+struct GemmConfig {
+  int bn, splits, kb_per, ab_stages, n_tok_tiles, n_tiles;
+};
+
+// Tile width and split-K for an M x N x K problem.  Cost model: waves of work units on the SMs, each unit
+// costing (its k-stages) x (bn + 64) (the 64 stands for the A-operand traffic every stage pays whatever bn
+// is), plus a small charge per extra split for the partial-sum traffic.  Split-K only when M <= 128 (small
+// decode batches), where the partials are small.
+static GemmConfig choose_config(int m, int n, int k) {
+  const int sms = num_sms();
+  const int nk = (k + BK - 1) / BK;
+  GemmConfig best{};
+  double best_cost = 1e30;
+  const int bns[4] = {32, 64, 128, 256};
+  for (int bn : bns) {
+    if (bn > 32 && m <= bn / 2) continue;  // a narrower tile already covers every token
+    const int tok_tiles = (m + bn - 1) / bn;
+    const int tiles = ((n + BM - 1) / BM) * tok_tiles;
+    const int max_s = m <= 128 ? 8 : 1;
+    for (int sp = 1; sp <= max_s; ++sp) {
+      const int kb_per = (nk + sp - 1) / sp;
+      if (sp > 1 && kb_per < 4) break;
+      const int real_sp = (nk + kb_per - 1) / kb_per;
+      const int units = tiles * real_sp;
+      const int waves = (units + sms - 1) / sms;
+      const double cost = (double)waves * kb_per * (bn + 64) + (real_sp > 1 ? 0.02 * real_sp * nk * (bn + 64) : 0.0);
+      if (cost < best_cost - 1e-9) {
+        best_cost = cost;
+        best = GemmConfig{bn, real_sp, kb_per, bn == 256 ? 3 : 4, tok_tiles, tiles};
+      }
+    }
+  }
+  return best;
+}
+
+static size_t align256(size_t b) { return (b + 255) & ~size_t(255); }
+
 }  // namespace
 
-size_t gemm_q8_0_workspace_bytes(int m, int k) { return (size_t)m * k * 2; }
+size_t gemm_q8_0_workspace_bytes(int m, int n, int k) {
+  const GemmConfig c = choose_config(m, n, k);
+  size_t b = align256((size_t)m * k * 2);
+  if (c.splits > 1) b += (size_t)c.splits * m * n * sizeof(float);
+  return b;
+}
 
 int gemm_q8_0_tc(const int8_t* qs, const uint16_t* d, const float* x, float* y, int m, int n, int k, int accumulate,
                  void* workspace, size_t workspace_bytes, int* status, cudaStream_t s) {
   if (!qs || !d || !x || !y || !status || m <= 0 || n <= 0 || k <= 0 || k % QK) return kBadArgument;
-  if (k % 8) return kUnsupported;  // TMA row pitch of the fp16 activations must be 16-byte aligned
-  if (!workspace || workspace_bytes < gemm_q8_0_workspace_bytes(m, k)) return kBadArgument;
-  if (reinterpret_cast<uintptr_t>(workspace) & 15 || reinterpret_cast<uintptr_t>(x) & 15 ||
+  if (k % 16) return kUnsupported;  // TMA row pitches (fp16 activations, int8 weights) must be 16-byte multiples
+  if (!workspace || workspace_bytes < gemm_q8_0_workspace_bytes(m, n, k)) return kBadArgument;
+  if (reinterpret_cast<uintptr_t>(workspace) & 255 || reinterpret_cast<uintptr_t>(x) & 15 ||
       reinterpret_cast<uintptr_t>(qs) & 15)
     return kUnsupported;
   EncodeTiledFn enc = encode_fn();
   if (!enc) return kCudaError;
+  const GemmConfig c = choose_config(m, n, k);
   __half* x16 = reinterpret_cast<__half*>(workspace);
+  float* part = reinterpret_cast<float*>(static_cast<char*>(workspace) + align256((size_t)m * k * 2));
   const size_t nx = (size_t)m * k;
   f32_to_f16_kernel<<<(unsigned)std::min<size_t>((nx / 4 + 255) / 256, 148 * 8), 256, 0, s>>>(x, x16, nx);
   if (cudaPeekAtLastError() != cudaSuccess) return kCudaError;
 
-  const int bn = m >= 192 ? 256 : (m > 64 ? 128 : 64);
-  CUtensorMap map;
-  cuuint64_t gdim[2] = {(cuuint64_t)k, (cuuint64_t)m};
-  cuuint64_t gstride[1] = {(cuuint64_t)k * 2};
-  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)bn};
-  cuuint32_t estride[2] = {1, 1};
-  if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x16, gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
-          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-    return kCudaError;
+  CUtensorMap xmap, wmap;
+  {
+    cuuint64_t gdim[2] = {(cuuint64_t)k, (cuuint64_t)m};
+    cuuint64_t gstride[1] = {(cuuint64_t)k * 2};
+    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)c.bn};
+    cuuint32_t estride[2] = {1, 1};
+    if (enc(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x16, gdim, gstride, box, estride,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return kCudaError;
+  }
+  {
+    cuuint64_t gdim[2] = {(cuuint64_t)k, (cuuint64_t)n};
+    cuuint64_t gstride[1] = {(cuuint64_t)k};
+    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)BM};
+    cuuint32_t estride[2] = {1, 1};
+    if (enc(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(qs), gdim, gstride, box, estride,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return kCudaError;
+  }
 
   GemmParams p;
-  p.qs = qs;
   p.d = d;
-  p.y = y;
+  p.y = c.splits > 1 ? part : y;
   p.status = status;
   p.M = m;
   p.N = n;
   p.K = k;
   p.accumulate = accumulate;
-  p.bn = bn;
-  p.n_tok_tiles = (m + bn - 1) / bn;
-  p.n_tiles = ((n + BM - 1) / BM) * p.n_tok_tiles;
-  const int smem = 1024 + STAGES * (A_STAGE_BYTES + bn * BK * 2) + 256;  // + barriers, TMEM slot, flag
+  p.bn = c.bn;
+  p.ab_stages = c.ab_stages;
+  p.n_tok_tiles = c.n_tok_tiles;
+  p.n_tiles = c.n_tiles;
+  p.splits = c.splits;
+  p.kb_per_split = c.kb_per;
+  const int smem = 1024 + c.ab_stages * (A_STAGE_BYTES + c.bn * BK * 2) + WSTAGES * W_STAGE_BYTES + 512;
   if (cudaFuncSetAttribute(gemm_q8_0_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return kCudaError;
-  const int grid = std::min(p.n_tiles, num_sms());
-  gemm_q8_0_tc_kernel<<<grid, GEMM_THREADS, smem, s>>>(map, p);
-  return cudaPeekAtLastError() == cudaSuccess ? kOk : kCudaError;
+  const int grid = std::min(c.n_tiles * c.splits, num_sms());
+  gemm_q8_0_tc_kernel<<<grid, GEMM_THREADS, smem, s>>>(xmap, wmap, p);
+  if (cudaPeekAtLastError() != cudaSuccess) return kCudaError;
+  if (c.splits > 1) {
+    const size_t mn = (size_t)m * n;
+    splitk_reduce_kernel<<<(unsigned)std::min<size_t>((mn + 255) / 256, 148 * 8), 256, 0, s>>>(part, y, mn, c.splits,
+                                                                                               accumulate);
+    if (cudaPeekAtLastError() != cudaSuccess) return kCudaError;
+  }
+  return kOk;
 }
 
 }  // namespace zc

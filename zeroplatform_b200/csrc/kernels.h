@@ -28,7 +28,7 @@ int gemv_q8_0_swiglu(const int8_t* qs, const uint16_t* d, const float* gate_up, 
                      int accumulate, cudaStream_t s);
 
 // ---- prefill / batched GEMM on tcgen05 (gemm_tc.cu): Y[m][n] (=|+=) X[m][:] . dequant(W)[n][:] ----
-size_t gemm_q8_0_workspace_bytes(int m, int k);
+size_t gemm_q8_0_workspace_bytes(int m, int n, int k);  // fp16 activations + split-K partials
 int gemm_q8_0_tc(const int8_t* qs, const uint16_t* d, const float* x, float* y, int m, int n, int k, int accumulate,
                  void* workspace, size_t workspace_bytes, int* status, cudaStream_t s);
 
