@@ -10,12 +10,14 @@
 // per-32-value fp16 block scales inside the tensor core, and a CUDA-core epilogue per block would
 // run several times slower than the MMA itself.)
 //
-// Structure (one persistent CTA per SM, 10 warps):
-//   warp 0      TMA producer: X tile (fp16, pre-converted) [BN tokens x 64 k] per stage, 128B swizzle
+// Structure (one persistent CTA per SM, 16 warps):
+//   warp 0      TMA producer: raw int8 W tiles [128 rows x 256 k] into a shared-memory ring (2-3 deep)
 //   warp 1      MMA issuer: one thread issues 4 x tcgen05.mma.kind::f16 (M=128, N=BN, K=16) per stage
-//   warps 2-5   dequantizers: int8 W [128 rows x 64 k] + scales -> fp16 in the UMMA K-major 128B-swizzled
-//               layout in shared memory (fence.proxy.async before signalling the MMA warp)
-//   warps 6-9   epilogue: tcgen05.ld 32 TMEM columns at a time, coalesced fp32 stores of Y
+//   warp 2      TMA producer: activation tiles (fp16, pre-converted) [BN tokens x 64 k], 128B swizzle
+//   warps 4-11  dequantizers: int8 W tile (shared memory) x fp16 block scales -> fp16 q*d in the UMMA
+//               K-major 128B-swizzled layout (fence.proxy.async before signalling the MMA warp)
+//   warps 12-15 epilogue: tcgen05.ld 32 TMEM columns at a time, coalesced fp32 stores of Y (or of the
+//               split-K partials, reduced afterwards in a fixed order)
 // The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue of one tile overlaps the
 // MMAs of the next.  Every mbarrier wait is bounded: on time-out the CTA records an error code in
 // `status`, stops issuing work, drains what it issued and frees its TMEM before returning.
@@ -33,10 +35,17 @@ namespace {
 
 constexpr int BM = 128;                   // weight rows per tile = MMA M = TMEM lanes
 constexpr int BK = 64;                    // k per stage: 64 fp16 = one 128-byte swizzle row
-constexpr int WSTAGES = 8;                // raw int8 weight tiles in flight (TMA ring)
-constexpr int GEMM_THREADS = 384;         // 12 warps, roles below
+constexpr int MAX_STAGES = 8;             // ring depth limit (barrier arrays are sized for it)
+constexpr int DQ_WARPS = 8;               // weight dequantizer warps (two per SM sub-partition)
+constexpr int DQ_THREADS = DQ_WARPS * 32;
+constexpr int DQ_ITEMS = BM * BK / 16 / DQ_THREADS;  // 16-value chunks per dequantizer thread per stage
+constexpr int EPI_WARP0 = 4 + DQ_WARPS;       // first of the four epilogue warps
+constexpr int GEMM_THREADS = (EPI_WARP0 + 4) * 32;
 constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KB of fp16 A per stage
-constexpr int W_STAGE_BYTES = BM * BK;      // 8 KB of int8 W per stage
+constexpr int W_SUB = 4;                    // k-stages per int8 weight tile (one TMA box of 256 bytes x 128 rows)
+constexpr int W_TILE_BYTES = BM * BK * W_SUB;     // 32 KB of int8 W per weight stage
+constexpr int S_TILE_BYTES = BM * BK * W_SUB / QK * 2;  // + 2 KB of its fp16 block scales (8 per row)
+constexpr int W_STAGE_BYTES = W_TILE_BYTES + S_TILE_BYTES;
 constexpr uint32_t WAIT_LIMIT = 1u << 24;    // try_wait polls before a wait is declared hung
 constexpr uint64_t WAIT_NS = 2000000000ull;  // ... or two seconds
 
@@ -47,11 +56,13 @@ struct GemmParams {
   int M, N, K;
   int accumulate;
   int bn;           // tokens per tile (MMA N): 32, 64, 128 or 256
-  int ab_stages;    // A/B pipeline depth (3 for bn = 256, else 4)
+  int ab_stages;    // A/B pipeline depth
+  int w_stages;     // int8 weight ring depth
   int n_tok_tiles;
   int n_tiles;      // output tiles
   int splits;       // K ranges per tile (split-K); work units = n_tiles * splits
-  int kb_per_split;
+  int kb_per_split;  // a multiple of W_SUB
+  int scale_tma;     // 1: block scales arrive by TMA with their weight tile (K % 256 == 0), 0: loaded per item
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -185,21 +196,22 @@ __device__ __forceinline__ void dequant16(int4 w, __half2 d2, uint4& lo, uint4& 
 
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_q8_0_tc_kernel(const __grid_constant__ CUtensorMap x_map, const __grid_constant__ CUtensorMap w_map,
-                        GemmParams p) {
+                        const __grid_constant__ CUtensorMap s_map, GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int bn = p.bn;
   const int AST = p.ab_stages;
+  const int WSTAGES = p.w_stages;
   const int b_stage_bytes = bn * BK * 2;
   uint8_t* a_st = smem;                                  // AST x 16 KB (fp16 A, SW128)
   uint8_t* b_st = a_st + AST * A_STAGE_BYTES;            // AST x bn*128 B (fp16 X, SW128 by TMA)
   uint8_t* w_st = b_st + AST * b_stage_bytes;            // WSTAGES x 8 KB (int8 W, TMA, unswizzled)
   uint64_t* bars = reinterpret_cast<uint64_t*>(w_st + WSTAGES * W_STAGE_BYTES);
-  uint64_t* ab_full = bars;                      // [AST]: 128 dequant arrivals + 1 X TMA (tx)
-  uint64_t* ab_empty = bars + 4;                 // [AST]: MMA commit
-  uint64_t* w_full = bars + 8;                   // [WSTAGES]: W TMA (tx)
-  uint64_t* w_empty = bars + 8 + WSTAGES;        // [WSTAGES]: 128 dequant arrivals
-  uint64_t* tfull = bars + 8 + 2 * WSTAGES;      // [2]
+  uint64_t* ab_full = bars;                            // [AST]: DQ_THREADS dequant arrivals + 1 X TMA (tx)
+  uint64_t* ab_empty = bars + MAX_STAGES;              // [AST]: MMA commit
+  uint64_t* w_full = bars + 2 * MAX_STAGES;            // [WSTAGES]: W TMA (tx)
+  uint64_t* w_empty = bars + 3 * MAX_STAGES;           // [WSTAGES]: DQ_THREADS dequant arrivals
+  uint64_t* tfull = bars + 4 * MAX_STAGES;             // [2]
   uint64_t* tempty = tfull + 2;                  // [2]
   uint64_t* drain = tempty + 2;                  // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -211,12 +223,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < AST; ++s) {
-      mbar_init(smem_u32(&ab_full[s]), 128 + 1);
+      mbar_init(smem_u32(&ab_full[s]), DQ_THREADS + 1);
       mbar_init(smem_u32(&ab_empty[s]), 1);
     }
     for (int s = 0; s < WSTAGES; ++s) {
       mbar_init(smem_u32(&w_full[s]), 1);
-      mbar_init(smem_u32(&w_empty[s]), 128);
+      mbar_init(smem_u32(&w_empty[s]), DQ_THREADS);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(smem_u32(&tfull[a]), 1);
@@ -250,10 +262,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       uint32_t ph = 0;
       for (int u = blockIdx.x; u < n_units && !*abort_flag; u += gridDim.x) {
         const int row0 = (unit_tile(u) / p.n_tok_tiles) * BM;
-        for (int kb = unit_kb0(u); kb < unit_kb1(u); ++kb) {
+        for (int kb = unit_kb0(u); kb < unit_kb1(u); kb += W_SUB) {  // one box covers W_SUB k-stages
           if (!mbar_wait(smem_u32(&w_empty[s]), ph ^ 1, abort_flag, p.status, 1)) break;
-          mbar_arrive_tx(smem_u32(&w_full[s]), (uint32_t)W_STAGE_BYTES);
+          mbar_arrive_tx(smem_u32(&w_full[s]), (uint32_t)(p.scale_tma ? W_STAGE_BYTES : W_TILE_BYTES));
           tma_load_2d(smem_u32(w_st + s * W_STAGE_BYTES), &w_map, kb * BK, row0, smem_u32(&w_full[s]));
+          if (p.scale_tma)  // the 8 scales per row of these 256 k (x = kb * 2, a multiple of 8 scales = 16 bytes)
+            tma_load_2d(smem_u32(w_st + s * W_STAGE_BYTES + W_TILE_BYTES), &s_map, kb * (BK / QK), row0,
+                        smem_u32(&w_full[s]));
           if (++s == WSTAGES) {
             s = 0;
             ph ^= 1;
@@ -324,54 +339,43 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       while (!mbar_try(smem_u32(drain), 0) && global_ns() - t0 < WAIT_NS) {
       }
     }
-  } else if (warp >= 4 && warp < 8) {
-    // ---------------- W dequantizers (128 threads): int8 tile in smem -> fp16(q*d) in the SW128 layout ----------------
-    const int tid = threadIdx.x - 128;  // 0..127
-    const int kblocks = p.K / QK;
+  } else if (warp >= 4 && warp < EPI_WARP0) {
+    // ---------------- W dequantizers: int8 tile in smem -> fp16(q*d) in the SW128 layout ----------------
+    const int tid = threadIdx.x - 128;  // 0..DQ_THREADS-1
     int ws = 0, as = 0;
     uint32_t wph = 0, aph = 0;
     for (int u = blockIdx.x; u < n_units && !*abort_flag; u += gridDim.x) {
       const int row0 = (unit_tile(u) / p.n_tok_tiles) * BM;
       const int kb0 = unit_kb0(u), kb1 = unit_kb1(u);
-      // items: (row, 16-value chunk); 4 consecutive threads cover one row's 64 values
-      auto load_scales = [&](int kb, __half2 (&dv)[4]) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int item = tid + 128 * j;
-          const int row = row0 + (item >> 2);
-          const int k = kb * BK + (item & 3) * 16;
-          const __half h = (kb < kb1 && row < p.N && k < p.K) ? __ushort_as_half(__ldg(p.d + (size_t)row * kblocks + (k >> 5)))
-                                                              : __ushort_as_half((unsigned short)0);
-          dv[j] = __halves2half2(h, h);
-        }
-      };
-      __half2 d0[4], d1[4], d2[4], d3[4];  // scales for stages kb .. kb+3 (register ring)
-      load_scales(kb0, d0);
-      load_scales(kb0 + 1, d1);
-      load_scales(kb0 + 2, d2);
-      load_scales(kb0 + 3, d3);
       bool stop = false;
       for (int kb = kb0; kb < kb1 && !stop; ++kb) {
-        // take this stage's scales, then refill the ring slot with the stage 4 ahead
-        __half2 cd[4];
+        const int sub = (kb - kb0) % W_SUB;  // which 64-byte column block of the current weight tile
+        if (sub == 0 && !mbar_wait(smem_u32(&w_full[ws]), wph, abort_flag, p.status, 4)) break;
+        int4 cw[DQ_ITEMS];
+        __half2 cd[DQ_ITEMS];
+        const uint8_t* wsrc = w_st + ws * W_STAGE_BYTES + sub * BK;
+        const uint16_t* ssrc = reinterpret_cast<const uint16_t*>(w_st + ws * W_STAGE_BYTES + W_TILE_BYTES);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) cd[j] = d0[j];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          d0[j] = d1[j];
-          d1[j] = d2[j];
-          d2[j] = d3[j];
+        for (int j = 0; j < DQ_ITEMS; ++j) {
+          const int item = tid + DQ_THREADS * j;
+          const int r = item >> 2, c = item & 3;
+          cw[j] = *reinterpret_cast<const int4*>(wsrc + r * (BK * W_SUB) + c * 16);
+          __half h;
+          if (p.scale_tma) {
+            h = __ushort_as_half(ssrc[r * (W_SUB * BK / QK) + sub * (BK / QK) + (c >> 1)]);
+          } else {  // K not a multiple of 256: scales straight from global memory
+            const int row = row0 + r, k = kb * BK + c * 16;
+            h = __ushort_as_half((row < p.N && k < p.K) ? __ldg(p.d + (size_t)row * (p.K / QK) + (k >> 5))
+                                                        : (unsigned short)0);
+          }
+          cd[j] = __halves2half2(h, h);
         }
-        load_scales(kb + 4, d3);
-        if (!mbar_wait(smem_u32(&w_full[ws]), wph, abort_flag, p.status, 4)) break;
-        int4 cw[4];
-        const uint8_t* wsrc = w_st + ws * W_STAGE_BYTES;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) cw[j] = *reinterpret_cast<const int4*>(wsrc + (tid + 128 * j) * 16);
-        mbar_arrive(smem_u32(&w_empty[ws]));  // the raw tile is in registers: release it to the TMA producer
-        if (++ws == WSTAGES) {
-          ws = 0;
-          wph ^= 1;
+        if (sub == W_SUB - 1 || kb == kb1 - 1) {  // last use of this tile: release it to the TMA producer
+          mbar_arrive(smem_u32(&w_empty[ws]));
+          if (++ws == WSTAGES) {
+            ws = 0;
+            wph ^= 1;
+          }
         }
         if (!mbar_wait(smem_u32(&ab_empty[as]), aph ^ 1, abort_flag, p.status, 5)) {
           stop = true;
@@ -379,8 +383,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
         uint8_t* a = a_st + as * A_STAGE_BYTES;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int item = tid + 128 * j;
+        for (int j = 0; j < DQ_ITEMS; ++j) {
+          const int item = tid + DQ_THREADS * j;
           const int r = item >> 2, c = item & 3;
           uint4 lo, hi;
           dequant16(cw[j], cd[j], lo, hi);
@@ -397,8 +401,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
       }
     }
-  } else if (warp >= 8) {
-    // ---------------- epilogue (warps 8..11 -> TMEM lane quadrants 0..3) ----------------
+  } else if (warp >= EPI_WARP0) {
+    // ---------------- epilogue (4 warps -> TMEM lane quadrants warp % 4) ----------------
     const int quad = warp & 3;
     const int row_in_tile = quad * 32 + lane;
     int it = 0;
@@ -491,8 +495,20 @@ int num_sms() {
 }
 
 struct GemmConfig {
-  int bn, splits, kb_per, ab_stages, n_tok_tiles, n_tiles;
+  int bn, splits, kb_per, ab_stages, w_stages, n_tok_tiles, n_tiles;
 };
+
+constexpr int SMEM_LIMIT = 232448;  // 227 KB of dynamic shared memory per CTA
+constexpr int SMEM_FIXED = 1024 + 512;  // alignment slack + barriers, TMEM slot, abort flag
+
+// Ring depths from the shared-memory budget: the A/B ring (fp16 A + fp16 X per stage) as deep as fits after
+// the int8 weight ring, at most MAX_STAGES.  Deep rings keep several stages in flight across the
+// dequantize -> MMA -> commit round trip.
+static void ring_depths(int bn, int& ab, int& w) {
+  w = bn <= 64 ? 3 : 2;
+  ab = (SMEM_LIMIT - SMEM_FIXED - w * W_STAGE_BYTES) / (A_STAGE_BYTES + bn * BK * 2);
+  if (ab > MAX_STAGES) ab = MAX_STAGES;
+}
 
 // Tile width and split-K for an M x N x K problem.  Cost model: waves of work units on the SMs, each unit
 // costing (its k-stages) x (bn + 64) (the 64 stands for the A-operand traffic every stage pays whatever bn
@@ -510,15 +526,17 @@ static GemmConfig choose_config(int m, int n, int k) {
     const int tiles = ((n + BM - 1) / BM) * tok_tiles;
     const int max_s = m <= 128 ? 8 : 1;
     for (int sp = 1; sp <= max_s; ++sp) {
-      const int kb_per = (nk + sp - 1) / sp;
-      if (sp > 1 && kb_per < 4) break;
+      const int kb_per = ((nk + sp - 1) / sp + W_SUB - 1) / W_SUB * W_SUB;  // whole weight tiles per split
+      if (sp > 1 && kb_per < 8) break;
       const int real_sp = (nk + kb_per - 1) / kb_per;
       const int units = tiles * real_sp;
       const int waves = (units + sms - 1) / sms;
       const double cost = (double)waves * kb_per * (bn + 64) + (real_sp > 1 ? 0.02 * real_sp * nk * (bn + 64) : 0.0);
       if (cost < best_cost - 1e-9) {
         best_cost = cost;
-        best = GemmConfig{bn, real_sp, kb_per, bn == 256 ? 3 : 4, tok_tiles, tiles};
+        int ab, w;
+        ring_depths(bn, ab, w);
+        best = GemmConfig{bn, real_sp, kb_per, ab, w, tok_tiles, tiles};
       }
     }
   }
@@ -542,7 +560,7 @@ int gemm_q8_0_tc(const int8_t* qs, const uint16_t* d, const float* x, float* y, 
   if (k % 16) return kUnsupported;  // TMA row pitches (fp16 activations, int8 weights) must be 16-byte multiples
   if (!workspace || workspace_bytes < gemm_q8_0_workspace_bytes(m, n, k)) return kBadArgument;
   if (reinterpret_cast<uintptr_t>(workspace) & 255 || reinterpret_cast<uintptr_t>(x) & 15 ||
-      reinterpret_cast<uintptr_t>(qs) & 15)
+      reinterpret_cast<uintptr_t>(qs) & 15 || reinterpret_cast<uintptr_t>(d) & 15)
     return kUnsupported;
   EncodeTiledFn enc = encode_fn();
   if (!enc) return kCudaError;
@@ -567,7 +585,7 @@ int gemm_q8_0_tc(const int8_t* qs, const uint16_t* d, const float* x, float* y, 
   {
     cuuint64_t gdim[2] = {(cuuint64_t)k, (cuuint64_t)n};
     cuuint64_t gstride[1] = {(cuuint64_t)k};
-    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)BM};
+    cuuint32_t box[2] = {(cuuint32_t)(BK * W_SUB), (cuuint32_t)BM};
     cuuint32_t estride[2] = {1, 1};
     if (enc(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(qs), gdim, gstride, box, estride,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -575,8 +593,23 @@ int gemm_q8_0_tc(const int8_t* qs, const uint16_t* d, const float* x, float* y, 
       return kCudaError;
   }
 
+  // Block scales [N][K/32] fp16 by TMA, 8 per row per weight tile (needs a 16-byte row pitch: K % 256 == 0).
+  const int scale_tma = (k % 256 == 0) ? 1 : 0;
+  CUtensorMap smap = wmap;
+  if (scale_tma) {
+    cuuint64_t gdim[2] = {(cuuint64_t)(k / QK), (cuuint64_t)n};
+    cuuint64_t gstride[1] = {(cuuint64_t)(k / QK) * 2};
+    cuuint32_t box[2] = {(cuuint32_t)(BK * W_SUB / QK), (cuuint32_t)BM};
+    cuuint32_t estride[2] = {1, 1};
+    if (enc(&smap, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint16_t*>(d), gdim, gstride, box, estride,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return kCudaError;
+  }
+
   GemmParams p;
   p.d = d;
+  p.scale_tma = scale_tma;
   p.y = c.splits > 1 ? part : y;
   p.status = status;
   p.M = m;
@@ -585,15 +618,16 @@ int gemm_q8_0_tc(const int8_t* qs, const uint16_t* d, const float* x, float* y, 
   p.accumulate = accumulate;
   p.bn = c.bn;
   p.ab_stages = c.ab_stages;
+  p.w_stages = c.w_stages;
   p.n_tok_tiles = c.n_tok_tiles;
   p.n_tiles = c.n_tiles;
   p.splits = c.splits;
   p.kb_per_split = c.kb_per;
-  const int smem = 1024 + c.ab_stages * (A_STAGE_BYTES + c.bn * BK * 2) + WSTAGES * W_STAGE_BYTES + 512;
+  const int smem = SMEM_FIXED + c.ab_stages * (A_STAGE_BYTES + c.bn * BK * 2) + c.w_stages * W_STAGE_BYTES;
   if (cudaFuncSetAttribute(gemm_q8_0_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return kCudaError;
   const int grid = std::min(c.n_tiles * c.splits, num_sms());
-  gemm_q8_0_tc_kernel<<<grid, GEMM_THREADS, smem, s>>>(xmap, wmap, p);
+  gemm_q8_0_tc_kernel<<<grid, GEMM_THREADS, smem, s>>>(xmap, wmap, smap, p);
   if (cudaPeekAtLastError() != cudaSuccess) return kCudaError;
   if (c.splits > 1) {
     const size_t mn = (size_t)m * n;
