@@ -276,6 +276,88 @@ def decode_12l_leg(dev, with_cpu, n_prompt=512, n_new=128):
                       "sample": f"oracle LlmEngine: 64-token prompt then {n_cpu} greedy decode steps (context 64-80)"}
     return out
 
+def decode_7b_leg(dev, rank, world, batch=32, n_ctx=2048, n_new=128, n_warm=3, layers=32):
+    """Llama-2-7B-shaped decoder (32 layers, d 4096, 32 heads, FFN 11008, vocab 32000, Q8_0
+    from N(0,0.02)), decode batch 32, each sequence with a 2048-token context in 16-token fp16 pages, then 128
+    greedy tokens per sequence; tensor parallel over the `world` GPUs of this job (one engine per rank).
+
+    Weights are drawn on the device from one seed per tensor (the same full tensor on every rank, each rank
+    keeps its slice) and quantized by zcu_quantize_q8_0.  The 2048-token contexts are written as synthetic
+    N(0,1) K/V with zcu_engine_append_kv (PagedKvCache.AppendTokenAt) instead of being prefilled: the decode
+    step reads the same pages either way, and a 65,536-token prefill is not part of this metric."""
+    import torch
+    import torch.distributed as dist
+    from zeroplatform_b200.engine import LlmEngine, nccl_unique_id
+    from zeroplatform_b200.ops import quantize
+    vocab, dim, heads, ffn = 32000, 4096, 32, 11008
+    hd = dim // heads
+    model = dict(vocab=vocab, dim=dim, layers=layers, heads=heads, kv_heads=heads, ffn=ffn, context_length=4096)
+    uid = None
+    if world > 1:
+        t = torch.zeros(128, dtype=torch.uint8, device=dev)
+        if rank == 0:
+            t.copy_(torch.frombuffer(bytearray(nccl_unique_id()), dtype=torch.uint8))
+        dist.broadcast(t, 0)
+        uid = bytes(t.cpu().numpy().tobytes())
+    pages = (n_ctx + n_new + 15) // 16
+    e = LlmEngine(model, total_pages=batch * pages, page_size=16, max_batch=batch, max_pages_per_seq=pages,
+                  max_prefill_tokens=batch, tp_size=world, tp_rank=rank, nccl_id=uid, load=False)
+    g = torch.Generator(device=dev)
+
+    def q8(seed, rows, cols):
+        g.manual_seed(seed)
+        return quantize(8, torch.randn((rows, cols), generator=g, device=dev) * 0.02)
+
+    t0 = time.perf_counter()
+    e.set_weight("tok_emb", 0, q8(1, vocab, dim))
+    e.set_weight("lm_head", 0, q8(2, vocab, dim))
+    shapes = {"wq": (dim, dim), "wk": (dim, dim), "wv": (dim, dim), "wo": (dim, dim), "wgate": (ffn, dim),
+              "wup": (ffn, dim), "wdown": (dim, ffn)}
+    for layer in range(layers):
+        for j, (name, (r, c)) in enumerate(shapes.items()):
+            e.set_weight(name, layer, q8(1000 + 10 * layer + j, r, c))
+    t_weights = time.perf_counter() - t0
+    # synthetic contexts: n_ctx - n_warm tokens per sequence (warm-up steps bring them to n_ctx)
+    n_fill = n_ctx - n_warm
+    for layer in range(layers):
+        g.manual_seed(50000 + layer)
+        k = torch.randn((n_fill, heads, hd), generator=g, device=dev).half()
+        v = torch.randn((n_fill, heads, hd), generator=g, device=dev).half()
+        for sid in range(batch):
+            e.append_kv(sid, layer, 0, k, v)
+    torch.cuda.synchronize()
+    toks = np.random.default_rng(9).integers(0, vocab, batch).astype(np.int32)
+    out, _ = e.generate_batch(list(range(batch)), toks, n_warm)           # captures the step graph
+    out, ms = e.generate_batch(list(range(batch)), out[:, -1], n_new)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    sh = e.shard()
+    e.close()
+    step_s = ms * 1e-3 / n_new
+    # bytes one rank streams per step: its Q8_0 weight slice (SoA int8 + fp16 scales) and its K/V heads
+    w_rank = layers * ((3 * sh["heads"] * hd + 2 * sh["ffn"]) * dim + dim * (sh["heads"] * hd + sh["ffn"])) \
+        + sh["vocab"] * dim
+    w_rank = w_rank * 34 // 32
+    mean_ctx = n_ctx + (n_new + 1) / 2.0
+    kv_rank = batch * mean_ctx * layers * 2 * sh["kv_heads"] * hd * 2
+    peak, src = _peaks()
+    gbs = (w_rank + kv_rank) / step_s / 1e9
+    return {"decode_tok_s": round(batch * n_new / (ms * 1e-3), 1), "ms_per_step": round(ms / n_new, 4),
+            "n_gpus": world, "parallelism": f"tp{world}", "layers": layers, "batch": batch, "context_at_start": n_ctx,
+            "new_tokens": n_new, "weight_bytes_per_step_per_gpu": int(w_rank),
+            "kv_bytes_per_step_per_gpu": int(kv_rank),
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 3), "peak_source": src,
+                         "what": "weights + K/V one rank streams per step / device step time"},
+            "setup_s": round(t_weights, 2),
+            "data": "synthetic: weights N(0,0.02) -> Q8_0 on device; contexts are N(0,1) fp16 K/V written with "
+                    "zcu_engine_append_kv, not prefilled; greedy tokens from random first ids",
+            "timing": "device events around 128 replays of the captured batch step (NCCL all-reduces inside), "
+                      "max over ranks"}
+
+
 # ----------------------------------------------------------------------------------------------------------
 # GPU arm
 # ----------------------------------------------------------------------------------------------------------
@@ -326,7 +408,8 @@ def run_ours(args):
             dist.barrier()
 
     sampler = ClockSampler(local)
-    with sampler:
+    # graph.replay() launches on torch's current stream: every replay and both events go to `stream`
+    with sampler, torch.cuda.stream(stream):
         # warm-up: at least W steps and at least --min-warmup-s of load so the clock samples cover a busy GPU
         t_w = time.perf_counter()
         n_w = 0
@@ -425,6 +508,11 @@ def run_ours(args):
             extra["decode_12l_d768"] = decode_12l_leg(dev, rank == 0 and world == 1 and not args.no_cpu)
         except Exception as ex:
             extra["decode_12l_d768"] = {"error": str(ex)[:200]}
+        try:
+            extra[f"decode_7b_b32_tp{world}"] = decode_7b_leg(dev, rank, world, layers=args.layers,
+                                                              n_new=args.new_tokens)
+        except Exception as ex:
+            extra[f"decode_7b_b32_tp{world}"] = {"error": str(ex)[:300]}
     cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu) else None
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -438,7 +526,7 @@ def run_ours(args):
                 "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                              "frac": round(achieved / peak, 3), "peak_source": peak_kind,
                              "traffic": NCU_TRAFFIC_BYTES, "algorithmic_bytes_per_launch": ALGO_BYTES,
-                             "kernel": "gemv_q8_0_kernel", "launch_us": round(launch_s * 1e6, 3)},
+                             "kernel": "gemv_direct_kernel<8,1,8,XPlain>", "launch_us": round(launch_s * 1e6, 3)},
                 "e2e": e2e, "e2e_weights_copied_per_call": e2e_copy, "gpu_launches": launches,
                 "clocks": sampler.summary(), "cpu_baseline": cpu, "extra_configs": extra}
         print(json.dumps(line), flush=True)
@@ -447,8 +535,33 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_leg(args):
+    """`--leg decode_7b`: only the 7B-shaped tensor-parallel decode, printed as its own JSON line (rank 0).
+    --layers / --new-tokens shrink it for profiler captures."""
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    res = decode_7b_leg(dev, rank, world, n_new=args.new_tokens, layers=args.layers)
+    if rank == 0:
+        print(json.dumps({"leg": f"decode_7b_b32_tp{world}", **res}), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--leg", choices=["all", "decode_7b"], default="all",
+                    help="all: the headline and every extra leg; decode_7b: only the 7B tensor-parallel decode")
+    ap.add_argument("--layers", type=int, default=32, help="decode_7b: decoder layers (32 = the 7B shape)")
+    ap.add_argument("--new-tokens", type=int, default=128, help="decode_7b: generated tokens per sequence")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
@@ -462,6 +575,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.leg == "decode_7b":
+        run_leg(args)
     else:
         run_ours(args)
 

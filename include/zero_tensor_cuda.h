@@ -153,9 +153,32 @@ enum {
 
 /* stream: the CUDA stream the engine enqueues on (NULL: the engine creates its own). */
 ZC_API int32_t zcu_engine_create(const zcu_engine_config* cfg, void* stream, void** engine);
+
+/* Tensor parallelism over tp_size GPUs of one node: one engine per GPU (one process or thread each), every
+ * rank making the same calls in the same order.  Rank r keeps query heads [head_begin, +heads) with their Wq
+ * rows, Wo columns and K/V pages; K/V heads [kv_head_begin, +kv_heads) with their Wk/Wv rows; FFN units
+ * [ffn_begin, +ffn) (whole 32-blocks) with their Wgate/Wup rows and Wdown columns; LM-head rows [vocab_begin,
+ * +vocab).  Embedding and norms are replicated.  After Wo and after Wdown the residual stream is summed over
+ * ranks (NCCL all-reduce); greedy sampling takes the arg-max of every rank's slice and merges them.
+ * zcu_tp_plan is host-only (no GPU needed) and fails when heads or kv_heads do not divide by tp_size, when a
+ * rank's Wo column slice is not a whole number of 32-blocks, or when there are fewer FFN blocks than ranks. */
+typedef struct {
+  int32_t head_begin, heads;
+  int32_t kv_head_begin, kv_heads;
+  int32_t ffn_begin, ffn;
+  int32_t vocab_begin, vocab;
+} zcu_tp_shard;
+ZC_API int32_t zcu_tp_plan(const zcu_engine_config* cfg, int32_t tp_size, int32_t tp_rank, zcu_tp_shard* out);
+/* 128-byte NCCL unique id, made by one rank and given to all (e.g. by a torch.distributed broadcast). */
+ZC_API int32_t zcu_nccl_unique_id(uint8_t* out, size_t cap);
+/* Collective: every rank calls it with its own tp_rank and the same nccl_id (ignored when tp_size == 1). */
+ZC_API int32_t zcu_engine_create_tp(const zcu_engine_config* cfg, int32_t tp_size, int32_t tp_rank,
+                                   const uint8_t* nccl_id, void* stream, void** engine);
 ZC_API int32_t zcu_engine_destroy(void* engine);
 ZC_API const char* zcu_engine_last_error(void* engine);
-ZC_API int32_t zcu_engine_set_weight(void* engine, int32_t kind, int32_t layer, const void* host, size_t bytes);
+/* `src` is host or device memory holding the FULL tensor; a tensor-parallel rank keeps its own slice.  The
+ * call first waits for all work queued on the device (a device source may be written by any stream). */
+ZC_API int32_t zcu_engine_set_weight(void* engine, int32_t kind, int32_t layer, const void* src, size_t bytes);
 /* LlmEngine.PrefillPrompt (LlmEngine.cs:157-315): n prompt tokens at positions start_pos.. of seq_id; writes the
  * last token's logits [vocab] to host memory when logits != NULL.  n == 1 is ForwardToken. */
 ZC_API int32_t zcu_engine_prefill(void* engine, int32_t seq_id, const int32_t* tokens, int32_t n, int32_t start_pos,
@@ -171,7 +194,20 @@ ZC_API int32_t zcu_engine_decode(void* engine, const int32_t* seq_ids, const int
 ZC_API int32_t zcu_engine_generate(void* engine, int32_t seq_id, const int32_t* prompt, int32_t n_prompt,
                                    int32_t n_new, float repetition_penalty, int32_t eos_token, int32_t* out_tokens,
                                    float* timing_ms);
-/* PagedKvCache.FreeSequence / GetSequenceLength / FreeBlockCount / the page table / GetKey+GetValue. */
+/* Batched greedy generation (GenerateStreamAsync for `batch` live sequences at once, repetition penalty 1):
+ * tokens[b] is fed at position seq_len(seq_ids[b]); each of n_new steps runs ForwardToken for every sequence
+ * and samples greedily, replayed from one captured CUDA graph (collectives included).  out_tokens[b * n_new + i]
+ * is sequence b's i-th sampled token.  timing_ms[0] = device ms of the n_new steps.  Returns n_new or < 0. */
+ZC_API int32_t zcu_engine_generate_batch(void* engine, int32_t batch, const int32_t* seq_ids, const int32_t* tokens,
+                                         int32_t n_new, int32_t* out_tokens, float* timing_ms);
+/* PagedKvCache.AppendTokenAt (Memory/PagedKvCache.cs:149-183) for tokens [start_pos, start_pos + n) of one layer:
+ * k, v are [n][kv_heads][hd] (host or device; kv_dtype 0 = fp32, 1 = fp16).  Appending the last layer sets the
+ * sequence length, as the reference counts a token once its last layer is stored.  Like set_weight, the call
+ * first waits for all work queued on the device. */
+ZC_API int32_t zcu_engine_append_kv(void* engine, int32_t seq_id, int32_t layer, int32_t start_pos, int32_t n_tokens,
+                                    const void* k, const void* v, int32_t kv_dtype);
+/* PagedKvCache.FreeSequence / GetSequenceLength / FreeBlockCount / the page table / GetKey+GetValue
+ * (a tensor-parallel rank writes only its own K/V heads into `out`). */
 ZC_API int32_t zcu_engine_free_sequence(void* engine, int32_t seq_id);
 ZC_API int32_t zcu_engine_seq_len(void* engine, int32_t seq_id);
 ZC_API int32_t zcu_engine_free_pages(void* engine);

@@ -1,7 +1,11 @@
 """Decode GEMV parity: CUDA (libzero_tensor.so) vs the CPU oracle on identical seeded inputs.
 
-Tolerance: max|y - y_oracle| / max|y_oracle| <= 1e-5.  Both sides accumulate fp32 products of the same
-exactly-dequantized weights; only the summation order differs (the north-star bound is 1e-3).
+Tolerance: max|y - y_oracle| / max|y_oracle| <= 3e-4 (the north-star bound is 1e-3).  GEMVs below 64 MB of
+weights keep x in fp32 (only the summation order differs: ~1e-6).  The streaming form for large weights
+re-expresses x per 32-value block as int16 (scale max|x| / 32767, so each value is within 2^-16 of the block
+maximum) and sums int16 x int8 products exactly in int32 (DP2A): for N(0,1) activations and N(0,0.02) weights
+at K = 4096 that error has a standard deviation of about 2.4e-5 per output against max|y| of about 4.5
+(max-rel ~2e-5).  The oracle keeps x in fp32, as the reference does.
 """
 import numpy as np
 import pytest
@@ -11,10 +15,13 @@ import oracle as O
 from tests.conftest import rel_err
 
 pytestmark = pytest.mark.gpu
-TOL = 1e-5
+TOL = 3e-4
 
+# (32768, 4096) is large enough (>= 64 MB of weights) for the streaming form (int16 activations, DP2A, L2
+# prefetch); the others run the fp32-activation form, K > 8192 in segments.
 SHAPES = [(1, 32), (3, 64), (17, 96), (1023, 768), (2304, 768), (4096, 4096), (768, 2048), (4096, 11008),
-          (11008, 4096), (257, 14336), (33, 20480)]
+          (11008, 4096), (257, 14336), (33, 20480), (64, 1056), (40, 2080), (150, 256), (149, 512), (2, 4096),
+          (32768, 4096)]
 
 
 def _case(qtype, rows, cols, seed):

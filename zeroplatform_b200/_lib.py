@@ -79,6 +79,25 @@ SIGNATURES.update({
     "zcu_engine_free_pages": (i32, [vp]),
     "zcu_engine_page_table": (i32, [vp, i32, vp, i32]),
     "zcu_engine_get_kv": (i32, [vp, i32, i32, i32, i32, vp]),
+    "zcu_engine_append_kv": (i32, [vp, i32, i32, i32, i32, vp, vp, i32]),
+    "zcu_engine_generate_batch": (i32, [vp, i32, vp, vp, i32, vp, vp]),
+    "zcu_nccl_unique_id": (i32, [vp, sz]),
+})
+
+
+class TpShard(C.Structure):
+    """zcu_tp_shard (include/zero_tensor_cuda.h): one rank's slice of a tensor-parallel model."""
+
+    _fields_ = [(n, C.c_int32) for n in ("head_begin", "heads", "kv_head_begin", "kv_heads", "ffn_begin", "ffn",
+                                         "vocab_begin", "vocab")]
+
+    def as_dict(self):
+        return {n: int(getattr(self, n)) for n, _ in self._fields_}
+
+
+SIGNATURES.update({
+    "zcu_tp_plan": (i32, [C.POINTER(EngineConfig), i32, i32, C.POINTER(TpShard)]),
+    "zcu_engine_create_tp": (i32, [C.POINTER(EngineConfig), i32, i32, vp, vp, C.POINTER(vp)]),
 })
 
 

@@ -17,21 +17,71 @@
 // standard rule (pos + 1 everywhere).
 // Greedy generation (GenerateStreamAsync, :71-150) runs as replays of one captured CUDA graph per token with
 // the sampled token, position and outputs kept on the device (no host round trip per token).
+//
+// Tensor parallelism (tp_size > 1, one engine per GPU): every rank holds the query heads, K/V heads, FFN units
+// and vocabulary rows that zcu_tp_plan assigns it.  Wq|Wk|Wv and Wgate|Wup are split by output rows, Wo and
+// Wdown by input columns on 32-block boundaries, so each rank's Wo / Wdown product is a partial sum of the
+// residual update: rank 0 adds its partial to x, the other ranks write theirs over x, and one in-place NCCL
+// all-reduce of x [T][dim] leaves x + sum(partials) on every rank (two all-reduces per layer).  Attention
+// needs no exchange (whole heads and their pages stay on one rank; page tables are replicated because every
+// rank runs the same allocator on the same calls).  Greedy sampling: each rank's arg-max over its vocabulary
+// slice, an all-gather of (value, index) pairs, and a merge that keeps the lowest index on ties.
 
 #include <cuda_runtime.h>
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <string>
 #include <vector>
 
 #include "../../include/zero_tensor_cuda.h"
+#include "collective.h"
 #include "common.cuh"
 #include "kernels.h"
 
 namespace zc {
+
+// Message for zc_cuda_last_error() on the calling thread (capi.cu).
+void set_last_error(const std::string& msg);
+
+// Host-only shard plan (also exported as zcu_tp_plan).
+int tp_plan(const zcu_engine_config& c, int tp, int rank, zcu_tp_shard* out, std::string* err) {
+  if (tp < 1 || rank < 0 || rank >= tp || c.heads <= 0 || c.kv_heads <= 0 || c.dim % c.heads) {
+    if (err) *err = "bad tp_size / tp_rank or head counts";
+    return kBadArgument;
+  }
+  const int hd = c.dim / c.heads;
+  if (c.heads % tp || c.kv_heads % tp) {
+    if (err) *err = "heads and kv_heads must be multiples of tp_size";
+    return kUnsupported;
+  }
+  const int hq = c.heads / tp, hkv = c.kv_heads / tp;
+  if (tp > 1 && (hq * hd) % QK) {
+    if (err) *err = "a rank's Wo column slice (heads/tp * head_dim) must be a multiple of 32";
+    return kUnsupported;
+  }
+  const int ffn_blocks = c.ffn / QK;
+  if (c.ffn % QK || ffn_blocks < tp || c.vocab < tp) {
+    if (err) *err = "ffn must be a multiple of 32 with at least one 32-block, and one vocabulary row, per rank";
+    return kUnsupported;
+  }
+  zcu_tp_shard s{};
+  s.head_begin = rank * hq;
+  s.heads = hq;
+  s.kv_head_begin = rank * hkv;
+  s.kv_heads = hkv;
+  const int fb0 = (int)((long long)rank * ffn_blocks / tp), fb1 = (int)((long long)(rank + 1) * ffn_blocks / tp);
+  s.ffn_begin = fb0 * QK;
+  s.ffn = (fb1 - fb0) * QK;
+  const int v0 = (int)((long long)rank * c.vocab / tp), v1 = (int)((long long)(rank + 1) * c.vocab / tp);
+  s.vocab_begin = v0;
+  s.vocab = v1 - v0;
+  *out = s;
+  return kOk;
+}
 
 namespace {
 
@@ -53,6 +103,12 @@ struct Seq {
 
 struct Engine {
   zcu_engine_config cfg{};
+  // tensor-parallel shard; hq / hkv / ffn / vocab are this rank's (the whole model's when tp_size == 1)
+  int tp_rank = 0, tp_size = 1;
+  zcu_tp_shard shard{};
+  Comm* comm = nullptr;
+  int timeout_ms = 120000;
+  int hq = 0, hkv = 0, ffn = 0, vocab = 0, vocab_chunk = 0;
   int hd = 0, q_dim = 0, kv_dim = 0, qkv_dim = 0;
   int device = 0;
   cudaStream_t stream = nullptr;
@@ -74,7 +130,14 @@ struct Engine {
   int32_t* page_table = nullptr;  // [max_batch][max_pages_per_seq]
   int max_rows = 0;               // activation rows: max(max_batch, max_prefill_tokens)
   float *x = nullptr, *xn = nullptr, *qkv = nullptr, *attn = nullptr, *gu = nullptr, *sw = nullptr;
-  float* logits = nullptr;  // [max_batch][vocab]
+  float* logits = nullptr;      // [max_batch][vocab] (this rank's vocabulary slice)
+  float* logits_all = nullptr;  // [tp][max_batch * vocab_chunk] gathered slices (tp > 1)
+  int2* pairs = nullptr;        // [max_batch] arg-max of this rank's slice (tp > 1)
+  int2* pairs_all = nullptr;    // [tp][max_batch]
+  void* stage = nullptr;        // upload staging buffer (grown on demand)
+  size_t stage_bytes = 0;
+  int32_t* batch_out = nullptr;  // [max_batch][gen_cap] tokens of zcu_engine_generate_batch
+  int32_t* batch_step = nullptr;
   int32_t *tokens = nullptr, *pos = nullptr, *rows = nullptr, *ctx_ex = nullptr, *ctx_in = nullptr,
           *next = nullptr;
   float* attn_ws = nullptr;
@@ -91,7 +154,8 @@ struct Engine {
   std::vector<int> free_stack;
   std::vector<int> free_rows;
   std::map<int, Seq> seqs;
-  std::map<int, cudaGraphExec_t> step_graphs;  // decode step graphs (B = 1 generation)
+  std::map<int, cudaGraphExec_t> step_graphs;   // decode step graphs (B = 1 generation)
+  std::map<int, cudaGraphExec_t> batch_graphs;  // batched generation step graphs, by batch size
   std::string err;
 };
 
@@ -161,13 +225,13 @@ int attention(Engine* E, int layer, int T, const int32_t* ctx) {
   a.ctx_len = ctx;
   a.out = E->attn;
   a.batch = T;
-  a.hq = E->cfg.heads;
-  a.hkv = E->cfg.kv_heads;
+  a.hq = E->hq;
+  a.hkv = E->hkv;
   a.hd = E->hd;
   a.page_size = E->cfg.page_size;
   a.max_pages = E->cfg.max_pages_per_seq;
   a.num_pages = E->cfg.total_pages;
-  a.page_stride = (long long)E->cfg.kv_heads * E->cfg.page_size * E->hd;
+  a.page_stride = (long long)E->hkv * E->cfg.page_size * E->hd;
   a.slot_stride = E->hd;
   a.head_stride = (long long)E->cfg.page_size * E->hd;
   a.scale = 1.0f / (float)std::sqrt((double)E->hd);  // GqaAttention.cs:45
@@ -181,11 +245,20 @@ int attention(Engine* E, int layer, int T, const int32_t* ctx) {
   return paged_attention(a, E->stream);
 }
 
+// Residual update of a row-split projection: rank 0 adds its partial to x, the others overwrite x with theirs.
+inline int residual_mode(const Engine* E) { return E->tp_rank == 0 ? 1 : 0; }
+
+int allreduce_x(Engine* E, int T) {
+  return comm_allreduce_sum_f32(E->comm, E->x, (size_t)T * E->cfg.dim, E->stream, &E->err);
+}
+
 // The forward pass over T activation rows already embedded in E->x, with tokens' positions in E->pos and
-// page-table rows in E->rows.  Leaves the last row's logits (or every row's when all_logits) in E->logits.
+// page-table rows in E->rows.  Leaves the last row's logits (or every row's when all_logits) of this rank's
+// vocabulary slice in E->logits.
 int forward(Engine* E, int T, bool all_logits) {
   const zcu_engine_config& c = E->cfg;
   const int L = c.layers;
+  const int acc = residual_mode(E);
   E_RC(causal_lengths(E->pos, T, E->ctx_ex, E->ctx_in, E->stream));
   for (int l = 0; l < L; ++l) {
     const float* an = E->attn_norm + (size_t)l * c.dim;
@@ -196,32 +269,67 @@ int forward(Engine* E, int T, bool all_logits) {
       E_RC(rmsnorm(E->x, an, E->xn, T, c.dim, c.eps, E->stream));
       E_RC(linear(E, E->wqkv[l], E->xn, E->qkv, T, 0));
     }
-    E_RC(rope_append_kv(E->qkv, T, c.heads, c.kv_heads, E->hd, E->pos, E->rows, E->page_table, c.max_pages_per_seq,
+    E_RC(rope_append_kv(E->qkv, T, E->hq, E->hkv, E->hd, E->pos, E->rows, E->page_table, c.max_pages_per_seq,
                         c.page_size, E->cos_t, E->sin_t, E->max_pos, E->kpool + (size_t)l * E->layer_pool_elems,
                         E->vpool + (size_t)l * E->layer_pool_elems, E->stream));
     const int32_t* ctx = (c.reference_causal_quirk && l != L - 1) ? E->ctx_ex : E->ctx_in;
     E_RC(attention(E, l, T, ctx));
-    E_RC(linear(E, E->wo[l], E->attn, E->x, T, 1));  // x += Wo . attn (MatVecAddQ8_0)
+    E_RC(linear(E, E->wo[l], E->attn, E->x, T, acc));  // x += Wo . attn (MatVecAddQ8_0)
+    E_RC(allreduce_x(E, T));
     if (T == 1) {
-      E_RC(gemv_q8_0_rmsnorm(E->wgu[l].qs, E->wgu[l].d, E->x, fn, c.eps, E->gu, 2 * c.ffn, c.dim, 0, E->stream));
-      E_RC(gemv_q8_0_swiglu(E->wdown[l].qs, E->wdown[l].d, E->gu, E->x, c.dim, c.ffn, 1, E->stream));
+      E_RC(gemv_q8_0_rmsnorm(E->wgu[l].qs, E->wgu[l].d, E->x, fn, c.eps, E->gu, 2 * E->ffn, c.dim, 0, E->stream));
+      E_RC(gemv_q8_0_swiglu(E->wdown[l].qs, E->wdown[l].d, E->gu, E->x, c.dim, E->ffn, acc, E->stream));
     } else {
       E_RC(rmsnorm(E->x, fn, E->xn, T, c.dim, c.eps, E->stream));
       E_RC(linear(E, E->wgu[l], E->xn, E->gu, T, 0));
-      E_RC(swiglu_rows(E->gu, E->sw, T, c.ffn, E->stream));
-      E_RC(linear(E, E->wdown[l], E->sw, E->x, T, 1));
+      E_RC(swiglu_rows(E->gu, E->sw, T, E->ffn, E->stream));
+      E_RC(linear(E, E->wdown[l], E->sw, E->x, T, acc));
     }
+    E_RC(allreduce_x(E, T));
   }
   if (all_logits && T > 1) {
     E_RC(rmsnorm(E->x, E->final_norm, E->xn, T, c.dim, c.eps, E->stream));
     E_RC(linear(E, E->lm_head, E->xn, E->logits, T, 0));
   } else {  // LM head only for the last row (PrefillPrompt, LlmEngine.cs:307-314)
     const float* xl = E->x + (size_t)(T - 1) * c.dim;
-    E_RC(gemv_q8_0_rmsnorm(E->lm_head.qs, E->lm_head.d, xl, E->final_norm, c.eps, E->logits, c.vocab, c.dim, 0,
+    E_RC(gemv_q8_0_rmsnorm(E->lm_head.qs, E->lm_head.d, xl, E->final_norm, c.eps, E->logits, E->vocab, c.dim, 0,
                            E->stream));
   }
   return kOk;
 }
+
+// Greedy next token of `rows` logit rows (this rank's slices) into out; tp > 1 merges the ranks' arg-maxes.
+int sample(Engine* E, int rows, const int32_t* past, const int32_t* past_len, int past_cap, float penalty,
+           int32_t* out) {
+  if (E->tp_size == 1) return greedy_sample(E->logits, rows, E->vocab, past, past_len, past_cap, penalty, out, E->stream);
+  E_RC(greedy_partial(E->logits, rows, E->vocab, E->shard.vocab_begin, past, past_len, past_cap, penalty, E->pairs,
+                      E->stream));
+  E_RC(comm_allgather_bytes(E->comm, E->pairs, E->pairs_all, (size_t)rows * sizeof(int2), E->stream, &E->err));
+  return greedy_merge(E->pairs_all, E->tp_size, rows, out, E->stream);
+}
+
+// Copies `rows` rows of full-vocabulary logits to host memory (gathering the ranks' slices when tp > 1).
+int logits_to_host(Engine* E, int rows, float* host) {
+  const int V = E->cfg.vocab;
+  if (E->tp_size == 1) {
+    E_CUDA(cudaMemcpyAsync(host, E->logits, (size_t)rows * V * 4, cudaMemcpyDeviceToHost, E->stream));
+    return kOk;
+  }
+  const size_t chunk = (size_t)rows * E->vocab_chunk;
+  E_RC(comm_allgather_bytes(E->comm, E->logits, E->logits_all, chunk * 4, E->stream, &E->err));
+  std::vector<float> all(chunk * E->tp_size);
+  E_CUDA(cudaMemcpyAsync(all.data(), E->logits_all, all.size() * 4, cudaMemcpyDeviceToHost, E->stream));
+  E_RC(comm_wait(E->comm, E->stream, E->timeout_ms, &E->err));
+  for (int r = 0; r < E->tp_size; ++r) {
+    zcu_tp_shard sh{};
+    E_RC(tp_plan(E->cfg, E->tp_size, r, &sh, &E->err));
+    for (int b = 0; b < rows; ++b)
+      std::memcpy(host + (size_t)b * V + sh.vocab_begin, all.data() + r * chunk + (size_t)b * sh.vocab, sh.vocab * 4);
+  }
+  return kOk;
+}
+
+int wait(Engine* E) { return comm_wait(E->comm, E->stream, E->timeout_ms, &E->err); }
 
 // Pages covering positions [0, upto) of a sequence; allocates from the free stack and updates the device row.
 int ensure_pages(Engine* E, Seq& s, int upto) {
@@ -262,29 +370,50 @@ int get_seq(Engine* E, int seq_id, Seq** out) {
   return kOk;
 }
 
-int upload_q8(Engine* E, DevW& dst, size_t row_offset, const void* host, int n, int k) {
-  const size_t nb = (size_t)n * (k / QK);
-  uint8_t* aos = nullptr;
-  if (cudaMalloc(&aos, nb * Q8_BLOCK_BYTES) != cudaSuccess) {
-    cudaGetLastError();
-    E->err = "staging allocation failed";
-    return kOutOfMemory;
+int stage(Engine* E, size_t bytes, void** out) {
+  if (bytes > E->stage_bytes) {
+    if (E->stage) {
+      cudaStreamSynchronize(E->stream);
+      cudaFree(E->stage);
+      E->stage = nullptr;
+      E->stage_bytes = 0;
+    }
+    if (cudaMalloc(&E->stage, bytes) != cudaSuccess) {
+      cudaGetLastError();
+      E->err = "staging allocation failed";
+      return kOutOfMemory;
+    }
+    E->stage_bytes = bytes;
   }
-  int rc = kOk;
-  if (cudaMemcpyAsync(aos, host, nb * Q8_BLOCK_BYTES, cudaMemcpyHostToDevice, E->stream) != cudaSuccess) rc = kCudaError;
-  if (rc == kOk)
-    rc = repack_q8_0(aos, dst.qs + row_offset * dst.k, dst.d + row_offset * (dst.k / QK), n, k, E->stream);
-  if (cudaStreamSynchronize(E->stream) != cudaSuccess) rc = kCudaError;
-  cudaFree(aos);
-  if (rc != kOk) E->err = "weight upload failed";
-  return rc;
+  *out = E->stage;
+  return kOk;
+}
+
+// Rows [r0, r0 + nr) x 32-blocks [b0, b0 + nb) of a full Q8_0 tensor with `full_blocks` blocks per row (the
+// reference's packed AoS blocks, in host or device memory) into rows dst_row.. of dst (dst.k == nb * 32).
+int upload_q8(Engine* E, DevW& dst, size_t dst_row, const void* src, int full_blocks, int r0, int nr, int b0, int nb) {
+  if (nb * QK != dst.k || dst_row + nr > (size_t)dst.n) {
+    E->err = "weight slice does not match the engine's tensor";
+    return kBadArgument;
+  }
+  void* aos = nullptr;
+  E_RC(stage(E, (size_t)nr * nb * Q8_BLOCK_BYTES, &aos));
+  const size_t row_bytes = (size_t)full_blocks * Q8_BLOCK_BYTES, part = (size_t)nb * Q8_BLOCK_BYTES;
+  const char* base = static_cast<const char*>(src) + (size_t)r0 * row_bytes + (size_t)b0 * Q8_BLOCK_BYTES;
+  if (part == row_bytes)
+    E_CUDA(cudaMemcpyAsync(aos, base, part * nr, cudaMemcpyDefault, E->stream));
+  else
+    E_CUDA(cudaMemcpy2DAsync(aos, part, base, row_bytes, part, nr, cudaMemcpyDefault, E->stream));
+  E_RC(repack_q8_0(static_cast<const uint8_t*>(aos), dst.qs + dst_row * dst.k, dst.d + dst_row * (dst.k / QK), nr,
+                   dst.k, E->stream));
+  E_CUDA(cudaStreamSynchronize(E->stream));
+  return kOk;
 }
 
 int capture_gen_step(Engine* E, float penalty, int eos, cudaGraphExec_t* out) {
   cudaGraph_t g;
   E_CUDA(cudaStreamBeginCapture(E->stream, cudaStreamCaptureModeThreadLocal));
-  int rc = greedy_sample(E->logits, 1, E->cfg.vocab, E->gen_past, E->gen_past_len, E->gen_cap, penalty, E->tokens,
-                         E->stream);
+  int rc = sample(E, 1, E->gen_past, E->gen_past_len, E->gen_cap, penalty, E->tokens);
   if (rc == kOk)
     rc = advance_generation(E->tokens, E->pos, E->gen_out, E->gen_step, E->gen_past, E->gen_past_len, E->gen_cap, eos,
                             E->gen_done, E->stream);
@@ -303,6 +432,23 @@ int capture_gen_step(Engine* E, float penalty, int eos, cudaGraphExec_t* out) {
   return kOk;
 }
 
+// One step of batched generation for B sequences: embed E->tokens -> forward -> greedy -> advance.
+int capture_batch_step(Engine* E, int B, cudaGraphExec_t* out) {
+  cudaGraph_t g;
+  E_CUDA(cudaStreamBeginCapture(E->stream, cudaStreamCaptureModeThreadLocal));
+  int rc = embed_q8_0(E->tok_emb.qs, E->tok_emb.d, E->tokens, B, E->cfg.vocab, E->cfg.dim, E->x, E->stream);
+  if (rc == kOk) rc = forward(E, B, B > 1);
+  if (rc == kOk) rc = sample(E, B, nullptr, nullptr, 0, 1.0f, E->next);
+  if (rc == kOk) rc = batch_advance(E->next, E->tokens, E->pos, E->batch_out, E->gen_cap, E->batch_step, B, E->stream);
+  cudaError_t ce = cudaStreamEndCapture(E->stream, &g);
+  if (rc != kOk) return rc;
+  E_CUDA(ce);
+  ce = cudaGraphInstantiate(out, g, 0);
+  cudaGraphDestroy(g);
+  E_CUDA(ce);
+  return kOk;
+}
+
 }  // namespace
 
 }  // namespace zc
@@ -311,7 +457,18 @@ using zc::Engine;
 
 extern "C" {
 
+int32_t zcu_tp_plan(const zcu_engine_config* cfg, int32_t tp_size, int32_t tp_rank, zcu_tp_shard* out) {
+  if (!cfg || !out) return zc::kBadArgument;
+  std::string err;
+  return zc::tp_plan(*cfg, tp_size, tp_rank, out, &err);
+}
+
 int32_t zcu_engine_create(const zcu_engine_config* cfg, void* stream, void** out) {
+  return zcu_engine_create_tp(cfg, 1, 0, nullptr, stream, out);
+}
+
+int32_t zcu_engine_create_tp(const zcu_engine_config* cfg, int32_t tp_size, int32_t tp_rank, const uint8_t* nccl_id,
+                             void* stream, void** out) {
   using namespace zc;
   if (!cfg || !out) return kBadArgument;
   const zcu_engine_config& c = *cfg;
@@ -321,12 +478,30 @@ int32_t zcu_engine_create(const zcu_engine_config* cfg, void* stream, void** out
     return kBadArgument;
   const int hd = c.dim / c.heads;
   if (hd % 8 || (hd & (hd - 1)) || hd > 256) return kUnsupported;  // attention kernel head sizes
+  zcu_tp_shard sh{};
+  {
+    std::string err;
+    const int prc = tp_plan(c, tp_size, tp_rank, &sh, &err);
+    if (prc != kOk) {
+      set_last_error("zcu_engine_create_tp: " + err);
+      return prc;
+    }
+  }
   Engine* E = new Engine();
   E->cfg = c;
+  E->tp_size = tp_size;
+  E->tp_rank = tp_rank;
+  E->shard = sh;
+  E->hq = sh.heads;
+  E->hkv = sh.kv_heads;
+  E->ffn = sh.ffn;
+  E->vocab = sh.vocab;
+  E->vocab_chunk = (c.vocab + tp_size - 1) / tp_size;
   E->hd = hd;
-  E->q_dim = c.heads * hd;
-  E->kv_dim = c.kv_heads * hd;
+  E->q_dim = E->hq * hd;
+  E->kv_dim = E->hkv * hd;
   E->qkv_dim = E->q_dim + 2 * E->kv_dim;
+  if (const char* t = std::getenv("ZCU_COLLECTIVE_TIMEOUT_MS")) E->timeout_ms = std::max(1, std::atoi(t));
   cudaGetDevice(&E->device);
   if (stream) {
     E->stream = reinterpret_cast<cudaStream_t>(stream);
@@ -341,9 +516,14 @@ int32_t zcu_engine_create(const zcu_engine_config* cfg, void* stream, void** out
   auto step = [&](int r) {
     if (rc == kOk) rc = r;
   };
+  {
+    std::string err;
+    step(comm_create(tp_size, tp_rank, nccl_id, &E->comm, &err));
+    if (rc != kOk) set_last_error("zcu_engine_create_tp: " + err);
+  }
   const int L = c.layers;
   step(alloc_weight(E, E->tok_emb, c.vocab, c.dim));
-  step(alloc_weight(E, E->lm_head, c.vocab, c.dim));
+  step(alloc_weight(E, E->lm_head, E->vocab, c.dim));
   E->wqkv.resize(L);
   E->wo.resize(L);
   E->wgu.resize(L);
@@ -351,8 +531,8 @@ int32_t zcu_engine_create(const zcu_engine_config* cfg, void* stream, void** out
   for (int l = 0; l < L && rc == kOk; ++l) {
     step(alloc_weight(E, E->wqkv[l], E->qkv_dim, c.dim));
     step(alloc_weight(E, E->wo[l], c.dim, E->q_dim));
-    step(alloc_weight(E, E->wgu[l], 2 * c.ffn, c.dim));
-    step(alloc_weight(E, E->wdown[l], c.dim, c.ffn));
+    step(alloc_weight(E, E->wgu[l], 2 * E->ffn, c.dim));
+    step(alloc_weight(E, E->wdown[l], c.dim, E->ffn));
   }
   step(dalloc(E, &E->final_norm, c.dim));
   step(dalloc(E, &E->attn_norm, (size_t)L * c.dim));
@@ -377,7 +557,7 @@ int32_t zcu_engine_create(const zcu_engine_config* cfg, void* stream, void** out
       cudaMemcpy(E->sin_t, st.data(), st.size() * 4, cudaMemcpyHostToDevice);
     }
   }
-  E->layer_pool_elems = (size_t)c.total_pages * c.kv_heads * c.page_size * hd;
+  E->layer_pool_elems = (size_t)c.total_pages * E->hkv * c.page_size * hd;
   step(dalloc(E, &E->kpool, E->layer_pool_elems * L));
   step(dalloc(E, &E->vpool, E->layer_pool_elems * L));
   step(dalloc(E, &E->page_table, (size_t)c.max_batch * c.max_pages_per_seq));
@@ -387,26 +567,31 @@ int32_t zcu_engine_create(const zcu_engine_config* cfg, void* stream, void** out
   step(dalloc(E, &E->xn, (size_t)R * c.dim));
   step(dalloc(E, &E->qkv, (size_t)R * E->qkv_dim));
   step(dalloc(E, &E->attn, (size_t)R * E->q_dim));
-  step(dalloc(E, &E->gu, (size_t)R * 2 * c.ffn));
-  step(dalloc(E, &E->sw, (size_t)R * c.ffn));
-  step(dalloc(E, &E->logits, (size_t)c.max_batch * c.vocab));
+  step(dalloc(E, &E->gu, (size_t)R * 2 * E->ffn));
+  step(dalloc(E, &E->sw, (size_t)R * E->ffn));
+  step(dalloc(E, &E->logits, (size_t)c.max_batch * E->vocab_chunk));
+  if (tp_size > 1) {
+    step(dalloc(E, &E->logits_all, (size_t)tp_size * c.max_batch * E->vocab_chunk));
+    step(dalloc(E, &E->pairs, (size_t)std::max(c.max_batch, 1)));
+    step(dalloc(E, &E->pairs_all, (size_t)tp_size * c.max_batch));
+  }
   step(dalloc(E, &E->tokens, R));
   step(dalloc(E, &E->pos, R));
   step(dalloc(E, &E->rows, R));
   step(dalloc(E, &E->ctx_ex, R));
   step(dalloc(E, &E->ctx_in, R));
   step(dalloc(E, &E->next, R));
-  E->attn_splits = paged_attention_choose_splits(c.max_batch, c.kv_heads, c.max_pages_per_seq * c.page_size,
-                                                 c.page_size);
-  step(dalloc(E, &E->attn_ws, std::max<size_t>(16, paged_attention_workspace_floats(c.max_batch, c.heads, hd,
+  E->attn_splits = paged_attention_choose_splits(c.max_batch, E->hkv, c.max_pages_per_seq * c.page_size, c.page_size);
+  step(dalloc(E, &E->attn_ws, std::max<size_t>(16, paged_attention_workspace_floats(c.max_batch, E->hq, hd,
                                                                                    E->attn_splits))));
-  step(dalloc(E, &E->attn_ctr, (size_t)R * c.heads));
+  step(dalloc(E, &E->attn_ctr, (size_t)R * E->hq));
   {  // the largest workspace any batched linear of this engine can ask for
-    const int shapes[5][2] = {{E->qkv_dim, c.dim}, {c.dim, E->q_dim}, {2 * c.ffn, c.dim}, {c.dim, c.ffn}, {c.vocab, c.dim}};
+    const int shapes[5][2] = {{E->qkv_dim, c.dim}, {c.dim, E->q_dim}, {2 * E->ffn, c.dim}, {c.dim, E->ffn},
+                              {E->vocab, c.dim}};
     size_t ws = 0;
-    for (auto& sh : shapes)
+    for (auto& sh2 : shapes)
       for (int rows_m : {R, c.max_batch, kGemmMinRows, std::min(R, 128)})
-        if (rows_m >= kGemmMinRows) ws = std::max(ws, gemm_q8_0_workspace_bytes(rows_m, sh[0], sh[1]));
+        if (rows_m >= kGemmMinRows) ws = std::max(ws, gemm_q8_0_workspace_bytes(rows_m, sh2[0], sh2[1]));
     E->gemm_ws_bytes = std::max<size_t>(ws, 256);
   }
   step(dalloc(E, reinterpret_cast<uint8_t**>(&E->gemm_ws), E->gemm_ws_bytes));
@@ -417,8 +602,10 @@ int32_t zcu_engine_create(const zcu_engine_config* cfg, void* stream, void** out
   step(dalloc(E, &E->gen_step, 1));
   step(dalloc(E, &E->gen_past_len, 1));
   step(dalloc(E, &E->gen_done, 1));
+  step(dalloc(E, &E->batch_out, (size_t)c.max_batch * E->gen_cap));
+  step(dalloc(E, &E->batch_step, 1));
   if (rc == kOk) {
-    cudaMemset(E->attn_ctr, 0, (size_t)R * c.heads * sizeof(int));
+    cudaMemset(E->attn_ctr, 0, (size_t)R * E->hq * sizeof(int));
     cudaMemset(E->status, 0, sizeof(int));
     cudaMemset(E->page_table, 0xff, (size_t)c.max_batch * c.max_pages_per_seq * sizeof(int32_t));  // -1: no page
     cudaMemset(E->kpool, 0, E->layer_pool_elems * L * 2);
@@ -431,6 +618,7 @@ int32_t zcu_engine_create(const zcu_engine_config* cfg, void* stream, void** out
   }
   if (rc != kOk) {
     for (void* p : E->allocs) cudaFree(p);
+    comm_destroy(E->comm);
     if (E->own_stream) cudaStreamDestroy(E->stream);
     delete E;
     cudaGetLastError();
@@ -445,9 +633,13 @@ int32_t zcu_engine_create(const zcu_engine_config* cfg, void* stream, void** out
 int32_t zcu_engine_destroy(void* engine) {
   Engine* E = static_cast<Engine*>(engine);
   if (!E) return zc::kBadArgument;
-  cudaStreamSynchronize(E->stream);
+  zc::wait(E);
+  // graphs that hold collectives go before the communicator
   for (auto& kv : E->step_graphs) cudaGraphExecDestroy(kv.second);
+  for (auto& kv : E->batch_graphs) cudaGraphExecDestroy(kv.second);
+  zc::comm_destroy(E->comm);
   for (void* p : E->allocs) cudaFree(p);
+  if (E->stage) cudaFree(E->stage);
   if (E->own_stream) cudaStreamDestroy(E->stream);
   delete E;
   return zc::kOk;
@@ -458,53 +650,57 @@ const char* zcu_engine_last_error(void* engine) {
   return E ? E->err.c_str() : "";
 }
 
-int32_t zcu_engine_set_weight(void* engine, int32_t kind, int32_t layer, const void* host, size_t bytes) {
+int32_t zcu_engine_set_weight(void* engine, int32_t kind, int32_t layer, const void* src, size_t bytes) {
   using namespace zc;
   Engine* E = static_cast<Engine*>(engine);
-  if (!E || !host) return kBadArgument;
+  if (!E || !src) return kBadArgument;
   E->err.clear();
+  // a device-memory source may still be being written by the caller's kernels on any stream
+  E_CUDA(cudaDeviceSynchronize());
   const zcu_engine_config& c = E->cfg;
   if (kind >= ZCU_W_ATTN_NORM && (layer < 0 || layer >= c.layers) && kind != ZCU_W_FINAL_NORM) return kBadArgument;
   auto q8bytes = [](size_t n, size_t k) { return n * (k / QK) * Q8_BLOCK_BYTES; };
   auto need = [&](size_t want) { return bytes == want; };
+  const zcu_tp_shard& sh = E->shard;
+  const int hd = E->hd, dblk = c.dim / QK, qd = c.heads * hd, kvd = c.kv_heads * hd;
   switch (kind) {
     case ZCU_W_TOK_EMB:
       if (!need(q8bytes(c.vocab, c.dim))) return kBadArgument;
-      return upload_q8(E, E->tok_emb, 0, host, c.vocab, c.dim);
+      return upload_q8(E, E->tok_emb, 0, src, dblk, 0, c.vocab, 0, dblk);
     case ZCU_W_LM_HEAD:
       if (!need(q8bytes(c.vocab, c.dim))) return kBadArgument;
-      return upload_q8(E, E->lm_head, 0, host, c.vocab, c.dim);
+      return upload_q8(E, E->lm_head, 0, src, dblk, sh.vocab_begin, E->vocab, 0, dblk);
     case ZCU_W_FINAL_NORM:
       if (!need((size_t)c.dim * 4)) return kBadArgument;
-      E_CUDA(cudaMemcpy(E->final_norm, host, bytes, cudaMemcpyHostToDevice));
+      E_CUDA(cudaMemcpy(E->final_norm, src, bytes, cudaMemcpyDefault));
       return kOk;
     case ZCU_W_ATTN_NORM:
     case ZCU_W_FFN_NORM:
       if (!need((size_t)c.dim * 4)) return kBadArgument;
-      E_CUDA(cudaMemcpy((kind == ZCU_W_ATTN_NORM ? E->attn_norm : E->ffn_norm) + (size_t)layer * c.dim, host, bytes,
-                        cudaMemcpyHostToDevice));
+      E_CUDA(cudaMemcpy((kind == ZCU_W_ATTN_NORM ? E->attn_norm : E->ffn_norm) + (size_t)layer * c.dim, src, bytes,
+                        cudaMemcpyDefault));
       return kOk;
     case ZCU_W_Q:
-      if (!need(q8bytes(E->q_dim, c.dim))) return kBadArgument;
-      return upload_q8(E, E->wqkv[layer], 0, host, E->q_dim, c.dim);
+      if (!need(q8bytes(qd, c.dim))) return kBadArgument;
+      return upload_q8(E, E->wqkv[layer], 0, src, dblk, sh.head_begin * hd, E->q_dim, 0, dblk);
     case ZCU_W_K:
-      if (!need(q8bytes(E->kv_dim, c.dim))) return kBadArgument;
-      return upload_q8(E, E->wqkv[layer], E->q_dim, host, E->kv_dim, c.dim);
+      if (!need(q8bytes(kvd, c.dim))) return kBadArgument;
+      return upload_q8(E, E->wqkv[layer], E->q_dim, src, dblk, sh.kv_head_begin * hd, E->kv_dim, 0, dblk);
     case ZCU_W_V:
-      if (!need(q8bytes(E->kv_dim, c.dim))) return kBadArgument;
-      return upload_q8(E, E->wqkv[layer], E->q_dim + E->kv_dim, host, E->kv_dim, c.dim);
+      if (!need(q8bytes(kvd, c.dim))) return kBadArgument;
+      return upload_q8(E, E->wqkv[layer], E->q_dim + E->kv_dim, src, dblk, sh.kv_head_begin * hd, E->kv_dim, 0, dblk);
     case ZCU_W_O:
-      if (!need(q8bytes(c.dim, E->q_dim))) return kBadArgument;
-      return upload_q8(E, E->wo[layer], 0, host, c.dim, E->q_dim);
+      if (!need(q8bytes(c.dim, qd))) return kBadArgument;
+      return upload_q8(E, E->wo[layer], 0, src, qd / QK, 0, c.dim, sh.head_begin * hd / QK, E->q_dim / QK);
     case ZCU_W_GATE:
       if (!need(q8bytes(c.ffn, c.dim))) return kBadArgument;
-      return upload_q8(E, E->wgu[layer], 0, host, c.ffn, c.dim);
+      return upload_q8(E, E->wgu[layer], 0, src, dblk, sh.ffn_begin, E->ffn, 0, dblk);
     case ZCU_W_UP:
       if (!need(q8bytes(c.ffn, c.dim))) return kBadArgument;
-      return upload_q8(E, E->wgu[layer], c.ffn, host, c.ffn, c.dim);
+      return upload_q8(E, E->wgu[layer], E->ffn, src, dblk, sh.ffn_begin, E->ffn, 0, dblk);
     case ZCU_W_DOWN:
       if (!need(q8bytes(c.dim, c.ffn))) return kBadArgument;
-      return upload_q8(E, E->wdown[layer], 0, host, c.dim, c.ffn);
+      return upload_q8(E, E->wdown[layer], 0, src, c.ffn / QK, 0, c.dim, sh.ffn_begin / QK, E->ffn / QK);
     default:
       return kBadArgument;
   }
@@ -530,9 +726,8 @@ int32_t zcu_engine_prefill(void* engine, int32_t seq_id, const int32_t* tokens, 
   E_CUDA(cudaMemcpyAsync(E->rows, rows.data(), n * 4, cudaMemcpyHostToDevice, E->stream));
   E_RC(embed_q8_0(E->tok_emb.qs, E->tok_emb.d, E->tokens, n, E->cfg.vocab, E->cfg.dim, E->x, E->stream));
   E_RC(forward(E, n, false));
-  if (logits)
-    E_CUDA(cudaMemcpyAsync(logits, E->logits, (size_t)E->cfg.vocab * 4, cudaMemcpyDeviceToHost, E->stream));
-  E_CUDA(cudaStreamSynchronize(E->stream));
+  if (logits) E_RC(logits_to_host(E, 1, logits));
+  E_RC(wait(E));
   s->len = std::max(s->len, start_pos + n);  // AppendTokenAt at the last layer (PagedKvCache.cs:311-314)
   return kOk;
 }
@@ -559,13 +754,13 @@ int32_t zcu_engine_decode(void* engine, const int32_t* seq_ids, const int32_t* t
   E_CUDA(cudaMemcpyAsync(E->rows, rows.data(), batch * 4, cudaMemcpyHostToDevice, E->stream));
   E_RC(embed_q8_0(E->tok_emb.qs, E->tok_emb.d, E->tokens, batch, E->cfg.vocab, E->cfg.dim, E->x, E->stream));
   E_RC(forward(E, batch, true));
+  // logits first: sampling may apply a penalty in place (not here: penalty 1), and both read E->logits
+  if (logits) E_RC(logits_to_host(E, batch, logits));
   if (next_tokens) {
-    E_RC(greedy_sample(E->logits, batch, E->cfg.vocab, nullptr, nullptr, 0, 1.0f, E->next, E->stream));
+    E_RC(sample(E, batch, nullptr, nullptr, 0, 1.0f, E->next));
     E_CUDA(cudaMemcpyAsync(next_tokens, E->next, batch * 4, cudaMemcpyDeviceToHost, E->stream));
   }
-  if (logits)
-    E_CUDA(cudaMemcpyAsync(logits, E->logits, (size_t)batch * E->cfg.vocab * 4, cudaMemcpyDeviceToHost, E->stream));
-  E_CUDA(cudaStreamSynchronize(E->stream));
+  E_RC(wait(E));
   for (int b = 0; b < batch; ++b) ss[b]->len = std::max(ss[b]->len, positions[b] + 1);
   return kOk;
 }
@@ -595,7 +790,7 @@ int32_t zcu_engine_generate(void* engine, int32_t seq_id, const int32_t* prompt,
   E_CUDA(cudaMemcpyAsync(E->pos, &n_prompt, 4, cudaMemcpyHostToDevice, E->stream));
   const int32_t row = s->row;
   E_CUDA(cudaMemcpyAsync(E->rows, &row, 4, cudaMemcpyHostToDevice, E->stream));
-  E_CUDA(cudaStreamSynchronize(E->stream));
+  E_RC(wait(E));
   E_CUDA(cudaEventRecord(ev[1], E->stream));
   if (n_new > 0) {
     // one graph per (penalty, eos) setting; the captured pointers are the engine's fixed buffers
@@ -611,7 +806,7 @@ int32_t zcu_engine_generate(void* engine, int32_t seq_id, const int32_t* prompt,
   E_CUDA(cudaEventRecord(ev[2], E->stream));
   int32_t produced = 0;
   E_CUDA(cudaMemcpyAsync(&produced, E->gen_step, 4, cudaMemcpyDeviceToHost, E->stream));
-  E_CUDA(cudaStreamSynchronize(E->stream));
+  E_RC(wait(E));
   E_CUDA(cudaMemcpy(out_tokens, E->gen_out, (size_t)std::max(produced, 0) * 4, cudaMemcpyDeviceToHost));
   if (timing_ms) {
     cudaEventElapsedTime(&timing_ms[0], ev[0], ev[1]);
@@ -679,13 +874,113 @@ int32_t zcu_engine_get_kv(void* engine, int32_t seq_id, int32_t layer, int32_t t
   cudaStreamSynchronize(E->stream);
   std::vector<__half> h((size_t)E->kv_dim);
   const __half* pool = (want_value ? E->vpool : E->kpool) + (size_t)layer * E->layer_pool_elems;
-  for (int kh = 0; kh < E->cfg.kv_heads; ++kh) {
-    const size_t off = (((size_t)page * E->cfg.kv_heads + kh) * P + token % P) * E->hd;
+  for (int kh = 0; kh < E->hkv; ++kh) {
+    const size_t off = (((size_t)page * E->hkv + kh) * P + token % P) * E->hd;
     if (cudaMemcpy(h.data() + (size_t)kh * E->hd, pool + off, E->hd * 2, cudaMemcpyDeviceToHost) != cudaSuccess)
       return kCudaError;
   }
-  for (int i = 0; i < E->kv_dim; ++i) out[i] = __half2float(h[i]);
+  float* dst = out + (size_t)E->shard.kv_head_begin * E->hd;
+  for (int i = 0; i < E->kv_dim; ++i) dst[i] = __half2float(h[i]);
   return kOk;
+}
+
+int32_t zcu_engine_append_kv(void* engine, int32_t seq_id, int32_t layer, int32_t start_pos, int32_t n_tokens,
+                             const void* k, const void* v, int32_t kv_dtype) {
+  using namespace zc;
+  Engine* E = static_cast<Engine*>(engine);
+  if (!E || !k || !v || layer < 0 || layer >= E->cfg.layers || start_pos < 0 || n_tokens < 0 ||
+      (kv_dtype != 0 && kv_dtype != 1))
+    return kBadArgument;
+  E->err.clear();
+  if (n_tokens == 0) return kOk;
+  E_CUDA(cudaDeviceSynchronize());  // k / v may be device memory written on another stream
+  Seq* s = nullptr;
+  E_RC(get_seq(E, seq_id, &s));
+  E_RC(ensure_pages(E, *s, start_pos + n_tokens));
+  // this rank's K/V heads of every token, staged contiguously [n][hkv][hd]
+  const size_t esz = kv_dtype ? 2 : 4;
+  const size_t full_row = (size_t)E->cfg.kv_heads * E->hd * esz, part = (size_t)E->kv_dim * esz;
+  const size_t off = (size_t)E->shard.kv_head_begin * E->hd * esz;
+  void* st = nullptr;
+  E_RC(stage(E, 2 * part * n_tokens, &st));
+  char* sk = static_cast<char*>(st);
+  char* sv = sk + part * n_tokens;
+  E_CUDA(cudaMemcpy2DAsync(sk, part, static_cast<const char*>(k) + off, full_row, part, n_tokens, cudaMemcpyDefault,
+                           E->stream));
+  E_CUDA(cudaMemcpy2DAsync(sv, part, static_cast<const char*>(v) + off, full_row, part, n_tokens, cudaMemcpyDefault,
+                           E->stream));
+  const size_t lo = (size_t)layer * E->layer_pool_elems;
+  E_RC(append_kv(sk, sv, kv_dtype, n_tokens, start_pos, E->hkv, E->hd,
+                 E->page_table + (size_t)s->row * E->cfg.max_pages_per_seq, E->cfg.max_pages_per_seq,
+                 E->cfg.page_size, E->kpool + lo, E->vpool + lo, E->stream));
+  E_CUDA(cudaStreamSynchronize(E->stream));
+  if (layer == E->cfg.layers - 1) s->len = std::max(s->len, start_pos + n_tokens);
+  return kOk;
+}
+
+int32_t zcu_engine_generate_batch(void* engine, int32_t batch, const int32_t* seq_ids, const int32_t* tokens,
+                                  int32_t n_new, int32_t* out_tokens, float* timing_ms) {
+  using namespace zc;
+  Engine* E = static_cast<Engine*>(engine);
+  if (!E || batch <= 0 || !seq_ids || !tokens || n_new < 0 || (n_new > 0 && !out_tokens)) return kBadArgument;
+  E->err.clear();
+  if (batch > E->cfg.max_batch) {
+    E->err = "batch larger than max_batch";
+    return kTooLarge;
+  }
+  if (n_new > E->gen_cap) {
+    E->err = "n_new exceeds the per-sequence token capacity";
+    return kTooLarge;
+  }
+  std::vector<int32_t> rows(batch), pos(batch);
+  std::vector<Seq*> ss(batch);
+  for (int b = 0; b < batch; ++b) {
+    E_RC(get_seq(E, seq_ids[b], &ss[b]));
+    for (int b2 = 0; b2 < b; ++b2)
+      if (ss[b2] == ss[b]) {
+        E->err = "a sequence appears twice in the batch";
+        return kBadArgument;
+      }
+    pos[b] = ss[b]->len;
+    E_RC(ensure_pages(E, *ss[b], pos[b] + n_new));  // every page up front: no host work between steps
+    rows[b] = ss[b]->row;
+  }
+  const int32_t zero = 0;
+  E_CUDA(cudaMemcpyAsync(E->tokens, tokens, batch * 4, cudaMemcpyHostToDevice, E->stream));
+  E_CUDA(cudaMemcpyAsync(E->pos, pos.data(), batch * 4, cudaMemcpyHostToDevice, E->stream));
+  E_CUDA(cudaMemcpyAsync(E->rows, rows.data(), batch * 4, cudaMemcpyHostToDevice, E->stream));
+  E_CUDA(cudaMemcpyAsync(E->batch_step, &zero, 4, cudaMemcpyHostToDevice, E->stream));
+  auto it = E->batch_graphs.find(batch);
+  if (n_new > 0 && it == E->batch_graphs.end()) {
+    cudaGraphExec_t ge;
+    E_RC(capture_batch_step(E, batch, &ge));
+    it = E->batch_graphs.emplace(batch, ge).first;
+  }
+  cudaEvent_t ev[2];
+  for (auto& e : ev) E_CUDA(cudaEventCreate(&e));
+  E_CUDA(cudaEventRecord(ev[0], E->stream));
+  for (int i = 0; i < n_new; ++i) E_CUDA(cudaGraphLaunch(it->second, E->stream));
+  E_CUDA(cudaEventRecord(ev[1], E->stream));
+  std::vector<int32_t> all;
+  if (n_new > 0) {
+    all.resize((size_t)batch * E->gen_cap);
+    E_CUDA(cudaMemcpyAsync(all.data(), E->batch_out, all.size() * 4, cudaMemcpyDeviceToHost, E->stream));
+  }
+  const int wrc = wait(E);
+  if (wrc == kOk && timing_ms) cudaEventElapsedTime(&timing_ms[0], ev[0], ev[1]);
+  for (auto& e : ev) cudaEventDestroy(e);
+  if (wrc != kOk) return wrc;
+  for (int b = 0; b < batch; ++b) {
+    for (int i = 0; i < n_new; ++i) out_tokens[(size_t)b * n_new + i] = all[(size_t)b * E->gen_cap + i];
+    ss[b]->len = pos[b] + n_new;
+  }
+  int st = 0;
+  cudaMemcpy(&st, E->status, 4, cudaMemcpyDeviceToHost);
+  if (st) {
+    E->err = "a kernel's bounded wait expired";
+    return kCudaError;
+  }
+  return n_new;
 }
 
 }  // extern "C"

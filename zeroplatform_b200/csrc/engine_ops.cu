@@ -74,17 +74,20 @@ __global__ void swiglu_rows_kernel(const float* __restrict__ gu, float* __restri
 
 // One CTA per row.  The penalty is applied occurrence by occurrence, in order, as the reference loops over
 // pastTokens (a token seen c times is divided c times); only thread 0 touches the penalised logits.
+// With a vocabulary split over ranks (vocab_offset = first token id of this rank's logits), the penalty
+// touches the past tokens that fall in this rank's range, and `pairs` receives (best value, global index) per
+// row for greedy_merge instead of a token in `out`.
 __global__ void greedy_kernel(float* __restrict__ logits, int vocab, const int32_t* __restrict__ past,
                               const int32_t* __restrict__ past_len, int past_cap, float penalty,
-                              int32_t* __restrict__ out) {
+                              int32_t* __restrict__ out, int vocab_offset, int2* __restrict__ pairs) {
   float* lg = logits + (size_t)blockIdx.x * vocab;
   if (penalty > 1.0f && past && past_len) {
     if (threadIdx.x == 0) {
       const int n = min(past_len[blockIdx.x], past_cap);
       const int32_t* pt = past + (size_t)blockIdx.x * past_cap;
       for (int i = 0; i < n; ++i) {
-        const unsigned tok = (unsigned)pt[i];
-        if (tok < (unsigned)vocab) lg[tok] = lg[tok] > 0 ? lg[tok] / penalty : lg[tok] * penalty;
+        const unsigned tok = (unsigned)(pt[i] - vocab_offset);
+        if (pt[i] >= vocab_offset && tok < (unsigned)vocab) lg[tok] = lg[tok] > 0 ? lg[tok] / penalty : lg[tok] * penalty;
       }
     }
     __syncthreads();
@@ -122,8 +125,66 @@ __global__ void greedy_kernel(float* __restrict__ logits, int vocab, const int32
         b = sb[w];
         bi = si[w];
       }
-    // all-NaN rows keep index 0, as the reference's scan does
-    out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
+    if (pairs) {
+      pairs[blockIdx.x] = make_int2(__float_as_int(b), bi == 0x7fffffff ? bi : bi + vocab_offset);
+    } else {
+      // all-NaN rows keep index 0, as the reference's scan does
+      out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
+    }
+  }
+}
+
+// pairs [ranks][rows] of (value bits, global index) -> the row's token: largest value, lowest index on ties.
+__global__ void greedy_merge_kernel(const int2* __restrict__ pairs, int ranks, int rows, int32_t* __restrict__ out) {
+  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
+    float best = -INFINITY;
+    int idx = 0x7fffffff;
+    for (int k = 0; k < ranks; ++k) {
+      const int2 p = pairs[(size_t)k * rows + r];
+      const float v = __int_as_float(p.x);
+      if (p.y == 0x7fffffff) continue;
+      if (v > best || (v == best && p.y < idx)) {
+        best = v;
+        idx = p.y;
+      }
+    }
+    out[r] = idx == 0x7fffffff ? 0 : idx;
+  }
+}
+
+// Batched generation bookkeeping: every sequence's sampled token becomes its next input and is recorded.
+__global__ void batch_advance_kernel(const int32_t* __restrict__ next, int32_t* __restrict__ tokens,
+                                     int32_t* __restrict__ pos, int32_t* __restrict__ out, int out_stride,
+                                     int32_t* __restrict__ step, int B) {
+  const int st = *step;
+  for (int b = threadIdx.x; b < B; b += blockDim.x) {
+    const int t = next[b];
+    if (st < out_stride) out[(size_t)b * out_stride + st] = t;
+    tokens[b] = t;
+    pos[b] += 1;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *step = st + 1;
+}
+
+// PagedKvCache.AppendTokenAt for a run of tokens: src rows [n][kvh][hd] (fp32 or fp16) to the fp16 pools.
+template <class T>
+__global__ void append_kv_kernel(const T* __restrict__ k, const T* __restrict__ v, int n, int start, int kvh, int hd,
+                                 const int32_t* __restrict__ pt_row, int max_pages, int page_size,
+                                 __half* __restrict__ k_pool, __half* __restrict__ v_pool) {
+  const size_t total = (size_t)n * kvh * hd;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int e = (int)(i % hd);
+    const int h = (int)((i / hd) % kvh);
+    const int t = (int)(i / ((size_t)hd * kvh));
+    const int p = start + t;
+    const int lp = p / page_size;
+    if (lp >= max_pages) continue;
+    const int page = pt_row[lp];
+    if (page < 0) continue;
+    const size_t off = (((size_t)page * kvh + h) * page_size + (p % page_size)) * hd + e;
+    k_pool[off] = __float2half_rn((float)k[i]);
+    v_pool[off] = __float2half_rn((float)v[i]);
   }
 }
 
@@ -183,7 +244,43 @@ int swiglu_rows(const float* gu, float* out, int T, int ffn, cudaStream_t s) {
 int greedy_sample(float* logits, int rows, int vocab, const int32_t* past, const int32_t* past_len, int past_cap,
                   float penalty, int32_t* out, cudaStream_t s) {
   if (!logits || !out || rows <= 0 || vocab <= 0) return kBadArgument;
-  greedy_kernel<<<rows, 1024, 0, s>>>(logits, vocab, past, past_len, past_cap, penalty, out);
+  greedy_kernel<<<rows, 1024, 0, s>>>(logits, vocab, past, past_len, past_cap, penalty, out, 0, nullptr);
+  return launched();
+}
+
+int greedy_partial(float* logits, int rows, int vocab, int vocab_offset, const int32_t* past, const int32_t* past_len,
+                   int past_cap, float penalty, int2* pairs, cudaStream_t s) {
+  if (!logits || !pairs || rows <= 0 || vocab <= 0) return kBadArgument;
+  greedy_kernel<<<rows, 1024, 0, s>>>(logits, vocab, past, past_len, past_cap, penalty, nullptr, vocab_offset, pairs);
+  return launched();
+}
+
+int greedy_merge(const int2* pairs, int ranks, int rows, int32_t* out, cudaStream_t s) {
+  if (!pairs || !out || ranks <= 0 || rows <= 0) return kBadArgument;
+  greedy_merge_kernel<<<(rows + 255) / 256, 256, 0, s>>>(pairs, ranks, rows, out);
+  return launched();
+}
+
+int batch_advance(const int32_t* next, int32_t* tokens, int32_t* pos, int32_t* out, int out_stride, int32_t* step,
+                  int B, cudaStream_t s) {
+  if (!next || !tokens || !pos || !out || !step || B <= 0) return kBadArgument;
+  batch_advance_kernel<<<1, 1024, 0, s>>>(next, tokens, pos, out, out_stride, step, B);
+  return launched();
+}
+
+int append_kv(const void* k, const void* v, int half_input, int n, int start, int kvh, int hd, const int32_t* pt_row,
+              int max_pages, int page_size, __half* k_pool, __half* v_pool, cudaStream_t s) {
+  if (!k || !v || !pt_row || !k_pool || !v_pool || n < 0 || start < 0) return kBadArgument;
+  if (n == 0) return kOk;
+  const size_t total = (size_t)n * kvh * hd;
+  if (half_input)
+    append_kv_kernel<__half><<<grid_for(total, 256), 256, 0, s>>>(static_cast<const __half*>(k),
+                                                                 static_cast<const __half*>(v), n, start, kvh, hd,
+                                                                 pt_row, max_pages, page_size, k_pool, v_pool);
+  else
+    append_kv_kernel<float><<<grid_for(total, 256), 256, 0, s>>>(static_cast<const float*>(k),
+                                                                static_cast<const float*>(v), n, start, kvh, hd,
+                                                                pt_row, max_pages, page_size, k_pool, v_pool);
   return launched();
 }
 

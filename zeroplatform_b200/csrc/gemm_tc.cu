@@ -28,6 +28,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "sync.cuh"
 
 namespace zc {
 
@@ -46,8 +47,6 @@ constexpr int W_SUB = 4;                    // k-stages per int8 weight tile (on
 constexpr int W_TILE_BYTES = BM * BK * W_SUB;     // 32 KB of int8 W per weight stage
 constexpr int S_TILE_BYTES = BM * BK * W_SUB / QK * 2;  // + 2 KB of its fp16 block scales (8 per row)
 constexpr int W_STAGE_BYTES = W_TILE_BYTES + S_TILE_BYTES;
-constexpr uint32_t WAIT_LIMIT = 1u << 24;    // try_wait polls before a wait is declared hung
-constexpr uint64_t WAIT_NS = 2000000000ull;  // ... or two seconds
 
 struct GemmParams {
   const uint16_t* d;
@@ -64,60 +63,6 @@ struct GemmParams {
   int kb_per_split;  // a multiple of W_SUB
   int scale_tma;     // 1: block scales arrive by TMA with their weight tile (K % 256 == 0), 0: loaded per item
 };
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
-
-// Bounded wait: gives up after WAIT_LIMIT polls or WAIT_NS nanoseconds, whichever comes first, raising
-// the CTA abort flag and recording `code` in the device status word.  Returns false when it gave up or
-// when another role of the CTA already aborted.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status,
-                                          int code) {
-  uint64_t t0 = 0;
-  for (uint32_t i = 0; i < WAIT_LIMIT; ++i) {
-    if (mbar_try(bar, parity)) return true;
-    if ((i & 255) == 255) {
-      if (*abort_flag) return false;
-      const uint64_t now = global_ns();
-      if (t0 == 0) t0 = now;
-      else if (now - t0 > WAIT_NS) break;
-    }
-  }
-  *abort_flag = 1;
-  atomicExch(status, code);
-  return false;
-}
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint32_t bar) {
   asm volatile(

@@ -11,12 +11,15 @@
 // so every row of quantized values is 16-byte aligned and streams with 128-bit loads; the reference's
 // 34/18-byte array-of-structs blocks are not 16-byte aligned.
 //
-// Kernel shape: one warp owns R rows; each lane streams 16-byte chunks of those rows with
-// L1-bypassing 128-bit loads (all of a row's chunks in flight at once), the activation vector is
-// staged once per CTA in shared memory (XOR-swizzled so that the 128-bit shared loads of a warp are
-// bank-conflict free), int8/nibble -> fp32 conversion is exact (PRMT + FADD), per-chunk sums are
-// scaled by the block scale, and a warp-shuffle reduction finishes each row.
+// Kernel shape: one warp owns R rows; each lane keeps 8 L1-bypassing 128-bit weight loads in flight (U
+// chunks of each of the R rows), the activation vector is staged once per CTA in shared memory
+// (XOR-swizzled so that the 128-bit shared loads of a warp are bank-conflict free), int8/nibble -> fp32
+// conversion is exact (PRMT + packed FADD), products accumulate in packed fp32x2 FMAs, per-chunk sums are
+// scaled by the block scale, and a warp-shuffle reduction finishes each row.  At most 64 registers a
+// thread: four CTAs share an SM, so consecutive GEMVs overlap under programmatic dependent launch.
 // The HBM roofline: bytes = N*K (Q8) or N*K/2 (Q4) + N*K/32*2 (scales) + 4K + 4N.
+
+#include <algorithm>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -59,6 +62,11 @@ struct XPlain {  // x as given
   const float* x;
   __device__ __forceinline__ void prepare(float*) const {}
   __device__ __forceinline__ float get(int i, const float*) const { return x[i]; }
+  // values i .. i+3 (i a multiple of 4); one 128-bit load when x is 16-byte aligned
+  __device__ __forceinline__ float4 get4(int i, const float*) const {
+    if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) return __ldg(reinterpret_cast<const float4*>(x + i));
+    return make_float4(x[i], x[i + 1], x[i + 2], x[i + 3]);
+  }
 };
 
 // x = RmsNorm(x_raw) * w, fused: RmsNorm.Forward (Layers/RmsNorm.cs:14-59) computed per CTA -- mean of
@@ -84,6 +92,9 @@ struct XRmsNorm {
   __device__ __forceinline__ float get(int i, const float* red) const {
     return __fmul_rn(__fmul_rn(x[i], red[blockDim.x >> 5]), w[i]);
   }
+  __device__ __forceinline__ float4 get4(int i, const float* red) const {
+    return make_float4(get(i, red), get(i + 1, red), get(i + 2, red), get(i + 3, red));
+  }
 };
 
 // x = SwiGLU(gate, up) with gate = gu[0:ffn], up = gu[ffn:2ffn] (SwiGLU.Forward, Layers/SwiGLU.cs:13-51).
@@ -96,36 +107,189 @@ struct XSwiGLU {
     const float sg = 1.0f / (1.0f + expf(-g));
     return __fmul_rn(__fmul_rn(g, sg), gu[ffn + i]);
   }
+  __device__ __forceinline__ float4 get4(int i, const float* red) const {
+    return make_float4(get(i, red), get(i + 1, red), get(i + 2, red), get(i + 3, red));
+  }
 };
 
-// Chunk geometry: Q8 chunks hold 16 values (4 float4), Q4 chunks hold 32 values (8 float4).
+// ------------------------------------------------------------------------------------------
+// Activations as int16 per 32-value block.
+//
+// Each CTA stages its K-segment of x once: block b gets the scale s_b = max|x| / 32767 and the values
+// q = rint(x / s_b) in [-32767, 32767] (|x - s_b q| <= s_b / 2: a relative error of at most 2^-16 of the
+// block's largest value).  A block's 32 int8 (or nibble) weights then meet their activations in DP2A
+// instructions -- two int16 x int8 products summed into an int32 each -- so a 16-value chunk costs 8 integer
+// dot-product instructions instead of 16 conversions and 16 FMAs, and the int32 block sums are exact.  One
+// int -> float conversion and the two scales finish a chunk:  y += d_w * s_b * sum_i q_i w_i.
+//
+// Shared layout: the int16 values in 16-byte units, chunk by chunk (a Q8_0 chunk = 16 values = 2 units, a
+// Q4_0 chunk = one 32-value block = 4 units), with the units of chunk c XOR-swizzled so that the 8 lanes of
+// a 128-bit load phase (chunks c .. c+7) hit distinct banks; then the block scales (fp32) and, for Q4_0, the
+// block sums of q (int32, for the -8 nibble offset).
+// ------------------------------------------------------------------------------------------
+template <int UPC>  // 16-byte units per chunk: 2 (Q8_0) or 4 (Q4_0)
+__device__ __forceinline__ int xunit(int chunk, int u) {
+  if (UPC == 2) return chunk * 2 + (u ^ ((chunk >> 2) & 1));
+  return chunk * 4 + (u ^ ((chunk >> 1) & 3));
+}
+
+// Stages x[k0, k0 + len) as int16 blocks in two steps: (A) global -> shared fp32 with 128-bit loads, one
+// pass; (B) shared fp32 -> shared int16, one thread per half block (16 values).  The two halves of a block are
+// adjacent lanes and agree on the block maximum with one shuffle.  Rounding uses the magic number
+// 1.5 * 2^23: v * inv + 1.5 * 2^23 (one packed FMA for two values, a single round-to-nearest-even) leaves
+// rint(v * inv) in the low bits of the float's encoding, and one PRMT packs two of those 16-bit integers.
+template <int UPC, class XP>
+__device__ __forceinline__ void stage_xq(float4* xf, int4* xq, float* xs, int* xsum, const XP& xp, int k0, int len,
+                                         float* red) {
+  xp.prepare(red);
+  for (int f = threadIdx.x; f < len / 4; f += blockDim.x) xf[f] = xp.get4(k0 + 4 * f, red);
+  __syncthreads();
+  const float magic = 12582912.0f;  // 1.5 * 2^23
+  const int halves = len / 16;
+  for (int h = threadIdx.x; h < halves; h += blockDim.x) {  // halves is even: partners iterate together
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {  // pass 1 over shared memory: the block maximum
+      const float4 v = xf[4 * h + i];
+      amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+    amax = fmaxf(amax, __shfl_xor_sync(__activemask(), amax, 1));
+    const float inv = amax > 0.f ? 32767.0f / amax : 0.f;
+    const float2 inv2 = make_float2(inv, inv), mg2 = make_float2(magic, magic);
+    const int c = UPC == 2 ? h : h >> 1;  // chunk and first unit of this half block
+    const int u0 = UPC == 2 ? 0 : 2 * (h & 1);
+    float part = 0.f;  // sum of the 16 integers, exact in fp32
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {  // pass 2: 8 values -> one 16-byte unit of int16
+      int wv[4];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const float4 v = xf[4 * h + 2 * half + i];
+        const float2 a = __ffma2_rn(make_float2(v.x, v.y), inv2, mg2);
+        const float2 b = __ffma2_rn(make_float2(v.z, v.w), inv2, mg2);
+        wv[2 * i] = (int)__byte_perm(__float_as_uint(a.x), __float_as_uint(a.y), 0x5410);
+        wv[2 * i + 1] = (int)__byte_perm(__float_as_uint(b.x), __float_as_uint(b.y), 0x5410);
+        if (xsum) part += ((a.x - magic) + (a.y - magic)) + ((b.x - magic) + (b.y - magic));
+      }
+      xq[xunit<UPC>(c, u0 + half)] = make_int4(wv[0], wv[1], wv[2], wv[3]);
+    }
+    if (xsum) part += __shfl_xor_sync(__activemask(), part, 1);
+    if ((h & 1) == 0) {
+      xs[h >> 1] = amax * (1.0f / 32767.0f);
+      if (xsum) xsum[h >> 1] = (int)part;
+    }
+  }
+}
+
+__device__ __forceinline__ int dp2a_lo(int x2, int w4, int c) { return __dp2a_lo(x2, w4, c); }
+__device__ __forceinline__ int dp2a_hi(int x2, int w4, int c) { return __dp2a_hi(x2, w4, c); }
+
+// sum over the 16 values of a Q8_0 chunk: w = 16 int8, x0 / x1 = the chunk's 16 int16 (logical units 0, 1).
+__device__ __forceinline__ int dot16_q8(const int4& w, const int4& x0, const int4& x1) {
+  int s = dp2a_lo(x0.x, w.x, 0);
+  s = dp2a_hi(x0.y, w.x, s);
+  s = dp2a_lo(x0.z, w.y, s);
+  s = dp2a_hi(x0.w, w.y, s);
+  s = dp2a_lo(x1.x, w.z, s);
+  s = dp2a_hi(x1.y, w.z, s);
+  s = dp2a_lo(x1.z, w.w, s);
+  return dp2a_hi(x1.w, w.w, s);
+}
+
+// sum over the 32 nibbles u of a Q4_0 block (byte j = value j | value j+16 << 4) with x0..x3 = values 0..31.
+__device__ __forceinline__ int dot32_q4(const int4& w, const int4& x0, const int4& x1, const int4& x2,
+                                        const int4& x3) {
+  const int m = 0x0F0F0F0F;
+  const int l0 = w.x & m, l1 = w.y & m, l2 = w.z & m, l3 = w.w & m;                      // values 0..15
+  const int h0 = (w.x >> 4) & m, h1 = (w.y >> 4) & m, h2 = (w.z >> 4) & m, h3 = (w.w >> 4) & m;  // 16..31
+  int s = dp2a_lo(x0.x, l0, 0);
+  s = dp2a_hi(x0.y, l0, s);
+  s = dp2a_lo(x0.z, l1, s);
+  s = dp2a_hi(x0.w, l1, s);
+  s = dp2a_lo(x1.x, l2, s);
+  s = dp2a_hi(x1.y, l2, s);
+  s = dp2a_lo(x1.z, l3, s);
+  s = dp2a_hi(x1.w, l3, s);
+  s = dp2a_lo(x2.x, h0, s);
+  s = dp2a_hi(x2.y, h0, s);
+  s = dp2a_lo(x2.z, h1, s);
+  s = dp2a_hi(x2.w, h1, s);
+  s = dp2a_lo(x3.x, h2, s);
+  s = dp2a_hi(x3.y, h2, s);
+  s = dp2a_lo(x3.z, h3, s);
+  return dp2a_hi(x3.w, h3, s);
+}
+
+// fp32 activations (the decode-chain form): staged in a swizzled float4 layout, products accumulate in packed
+// fp32x2 FMAs after an exact int8 / nibble -> fp32 conversion (PRMT + packed FADD).
 template <int F4_PER_CHUNK>
 __device__ __forceinline__ int swz(int chunk, int j) {
-  // Logical float4 j of chunk `chunk` -> physical float4 slot (conflict-free for 8-lane phases).
+  // logical float4 j of chunk `chunk` -> physical float4 slot (conflict-free for 8-lane phases)
   if (F4_PER_CHUNK == 4) return chunk * 4 + (j ^ ((chunk >> 1) & 3));
   return chunk * 8 + (j ^ (chunk & 7));
 }
 
-template <int F4_PER_CHUNK, class XP>
-__device__ __forceinline__ void stage_x(float4* sx, const XP& xp, int k0, int len, float* red) {
-  xp.prepare(red);
-  const int nf4 = len / 4;
-  for (int f = threadIdx.x; f < nf4; f += blockDim.x) {
-    int chunk = f / F4_PER_CHUNK, j = f % F4_PER_CHUNK;
-    int e = k0 + 4 * f;
-    sx[swz<F4_PER_CHUNK>(chunk, j)] = make_float4(xp.get(e, red), xp.get(e + 1, red), xp.get(e + 2, red),
-                                                  xp.get(e + 3, red));
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+
+__device__ __forceinline__ void bytes_to_f2(uint32_t b, float2 bias, float2& p01, float2& p23) {
+  p01 = __fadd2_rn(f2(__uint_as_float(__byte_perm(b, 0x4B000000u, 0x7650)),
+                      __uint_as_float(__byte_perm(b, 0x4B000000u, 0x7651))), bias);
+  p23 = __fadd2_rn(f2(__uint_as_float(__byte_perm(b, 0x4B000000u, 0x7652)),
+                      __uint_as_float(__byte_perm(b, 0x4B000000u, 0x7653))), bias);
+}
+
+// sum over a Q8_0 chunk (16 values) with x in fp32: chunk c of the swizzled layout
+__device__ __forceinline__ float dotf_q8(const int4& w, const float4* sx, int c) {
+  const float2 bias = f2(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
+  const uint32_t* wv = reinterpret_cast<const uint32_t*>(&w);
+  float2 s = f2(0.f, 0.f);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float4 xv = sx[swz<4>(c, j)];
+    float2 p01, p23;
+    bytes_to_f2(wv[j] ^ 0x80808080u, bias, p01, p23);
+    s = __ffma2_rn(p01, f2(xv.x, xv.y), s);
+    s = __ffma2_rn(p23, f2(xv.z, xv.w), s);
   }
+  return s.x + s.y;
+}
+
+// sum over a Q4_0 block (32 values) with x in fp32
+__device__ __forceinline__ float dotf_q4(const int4& w, const float4* sx, int c) {
+  const float2 bias = f2(-8388616.0f, -8388616.0f);  // -(2^23 + 8)
+  const uint32_t* wv = reinterpret_cast<const uint32_t*>(&w);
+  float2 s = f2(0.f, 0.f);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float4 xl = sx[swz<8>(c, j)], xh = sx[swz<8>(c, 4 + j)];
+    float2 l01, l23, h01, h23;
+    bytes_to_f2(wv[j] & 0x0F0F0F0Fu, bias, l01, l23);
+    bytes_to_f2((wv[j] >> 4) & 0x0F0F0F0Fu, bias, h01, h23);
+    s = __ffma2_rn(l01, f2(xl.x, xl.y), s);
+    s = __ffma2_rn(l23, f2(xl.z, xl.w), s);
+    s = __ffma2_rn(h01, f2(xh.x, xh.y), s);
+    s = __ffma2_rn(h23, f2(xh.z, xh.w), s);
+  }
+  return s.x + s.y;
 }
 
 constexpr int GEMV_THREADS = 256;
 constexpr int GEMV_WARPS = GEMV_THREADS / 32;
-constexpr int SEG_Q8 = 8192;   // activations staged per K segment (32 KB of shared memory)
-constexpr int SEG_Q4 = 8192;
-constexpr int UNROLL = 8;      // chunks in flight per lane per row (Q4_0)
+// Four CTAs of 256 threads per SM (at most 64 registers a thread): the CTAs of the next GEMV in the stream fit
+// beside this one's and issue their weight loads -- before griddepcontrol.wait, weights never depend on the
+// previous kernel -- while this one finishes.
+constexpr int GEMV_MIN_CTAS = 4;
+constexpr int GEMV_STREAM_CTAS_PER_SM = 4;          // grid of the streaming form (contiguous row ranges)
+constexpr size_t GEMV_STREAM_BYTES = 64ull << 20;  // weights from which a GEMV uses the streaming form
+constexpr int SEG = 8192;   // activations staged per K segment: 32 KB fp32 + 16 KB int16 + 2 KB scales / sums
+// 16-byte weight chunks in flight per lane (R rows x U chunks): 8 for Q8_0 (16 values each), 4 for Q4_0
+// (32 values each: twice the arithmetic per byte, and the registers the nibble unpacking needs)
+__host__ __device__ constexpr int loads_per_lane(int qt) { return qt == 8 ? 8 : 4; }
 
-// Loads one batch of UNROLL chunks per row (and the block scales they need) for lane `lane`.
-template <int R, int U, int CHUNK_BYTES, int CHUNKS_PER_BLOCK>
+__host__ __device__ constexpr int seg_smem_bytes(int len) { return len * 4 + len * 2 + (len / QK) * 8; }
+
+// Loads one batch of U chunks per row (and the block scales they need) for lane `lane`.
+template <int R, int U, int CHUNKS_PER_BLOCK>
 __device__ __forceinline__ void load_batch(int4 (&w)[R][U], float (&sc)[R][U], const uint8_t* __restrict__ qs,
                                            const uint16_t* __restrict__ dsc, size_t row_bytes, int kb,
                                            int row0, int N, int seg_chunk0, int seg_blk0, int cb, int nch,
@@ -137,137 +301,197 @@ __device__ __forceinline__ void load_batch(int4 (&w)[R][U], float (&sc)[R][U], c
       const int c = cb + lane + 32 * u;
       const int row = row0 + r;
       const bool ok = c < nch && row < N;
-      w[r][u] = ok ? ld_stream_v4(qs + (size_t)row * row_bytes + (size_t)(seg_chunk0 + c) * CHUNK_BYTES)
+      w[r][u] = ok ? ld_stream_v4(qs + (size_t)row * row_bytes + (size_t)(seg_chunk0 + c) * 16)
                    : make_int4(0, 0, 0, 0);
       sc[r][u] = ok ? h2f(__ldg(dsc + (size_t)row * kb + seg_blk0 + c / CHUNKS_PER_BLOCK)) : 0.f;
     }
 }
 
-template <int R, int U, class XP>
-__global__ void __launch_bounds__(GEMV_THREADS) gemv_q8_0_kernel(const int8_t* __restrict__ qs,
-                                                                 const uint16_t* __restrict__ dsc, XP xp,
-                                                                 float* __restrict__ y, int N, int K,
-                                                                 int accumulate) {
-  extern __shared__ float4 sx[];
+// Bulk prefetch of the 16-byte units wholly inside [p, p + bytes) into L2 (a hint: nothing outside the range is
+// touched, no completion is awaited).
+__device__ __forceinline__ void prefetch_l2(const void* p, size_t bytes) {
+  const uintptr_t a = (reinterpret_cast<uintptr_t>(p) + 15) & ~(uintptr_t)15;
+  const uintptr_t e = (reinterpret_cast<uintptr_t>(p) + bytes) & ~(uintptr_t)15;
+  for (uintptr_t o = a; o < e; o += 0x40000000u) {
+    const uint32_t n = (uint32_t)((e - o) < 0x40000000u ? (e - o) : 0x40000000u);
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(o), "r"(n) : "memory");
+  }
+}
+
+// acc[r] += d_w * s_x * (chunk c of row r . x) for the int16 activation layout (the u-th loaded chunk).
+template <int QT, int R, int U>
+__device__ __forceinline__ void chunk_dot(float (&acc)[R], const int4 (&w)[R][U], const float (&sc)[R][U], int u,
+                                          int c, const int4* xq, const float* xs, const int* xsum) {
+  const int b = QT == 8 ? c >> 1 : c;
+  const float s_x = xs[b];
+  if (QT == 8) {
+    const int4 x0 = xq[xunit<2>(c, 0)], x1 = xq[xunit<2>(c, 1)];
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] = fmaf(sc[r][u] * s_x, (float)dot16_q8(w[r][u], x0, x1), acc[r]);
+  } else {
+    const int4 x0 = xq[xunit<4>(c, 0)], x1 = xq[xunit<4>(c, 1)], x2 = xq[xunit<4>(c, 2)], x3 = xq[xunit<4>(c, 3)];
+    const int off = 8 * xsum[b];  // the nibbles carry +8
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+      acc[r] = fmaf(sc[r][u] * s_x, (float)(dot32_q4(w[r][u], x0, x1, x2, x3) - off), acc[r]);
+  }
+}
+
+template <int F4_PER_CHUNK, class XP>
+__device__ __forceinline__ void stage_xf_scalar(float4* sx, const XP& xp, int k0, int len, float* red) {
+  xp.prepare(red);
+  for (int f = threadIdx.x; f < len / 4; f += blockDim.x) {
+    const int e = k0 + 4 * f;
+    sx[swz<F4_PER_CHUNK>(f / F4_PER_CHUNK, f % F4_PER_CHUNK)] =
+        make_float4(xp.get(e, red), xp.get(e + 1, red), xp.get(e + 2, red), xp.get(e + 3, red));
+  }
+}
+
+// Decode-chain form: one batch of R rows per warp (the grid covers every row), so a CTA issues all of its
+// weight loads before griddepcontrol.wait; fp32 activations staged per K segment of SEG values.
+template <int QT, int R, int U, class XP>
+__global__ void __launch_bounds__(GEMV_THREADS, R == 1 ? GEMV_MIN_CTAS : GEMV_MIN_CTAS - 1)
+    gemv_direct_kernel(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, XP xp,
+                       float* __restrict__ y, int N, int K, int accumulate) {
+  constexpr int VPC = QT == 8 ? 16 : 32;
+  constexpr int CPB = QT == 8 ? 2 : 1;
+  static_assert(R * U == loads_per_lane(QT), "R rows x U chunks = the loads in flight per lane");
+  extern __shared__ float4 sxf[];
   __shared__ float red[GEMV_WARPS + 1];
-  static_assert(GEMV_THREADS / 32 == GEMV_WARPS, "red[] holds one partial per warp plus the result");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = (blockIdx.x * GEMV_WARPS + warp) * R;
   const int kb = K / QK;
-  const uint8_t* q = reinterpret_cast<const uint8_t*>(qs);
+  const size_t row_bytes = QT == 8 ? (size_t)K : (size_t)K / 2;
   float acc[R];
 #pragma unroll
   for (int r = 0; r < R; ++r) acc[r] = 0.f;
   int4 w[R][U];
   float sc[R][U];
-
-  for (int k0 = 0; k0 < K; k0 += SEG_Q8) {
-    const int len = min(SEG_Q8, K - k0);
-    const int nch = len / 16;  // 16-value chunks (half a block)
-    // The first batch of weight loads is issued before x is staged so both are in flight together; the
-    // weights do not depend on the previous kernel, so they are issued before the dependency wait.
+  for (int k0 = 0; k0 < K; k0 += SEG) {
+    const int len = min(SEG, K - k0);
+    const int nch = len / VPC;
     if (k0 == 0) pdl_trigger();
-    load_batch<R, U, 16, 2>(w, sc, q, dsc, (size_t)K, kb, row0, N, k0 / 16, k0 / QK, 0, nch, lane);
-    if (k0 == 0) pdl_wait();
+    load_batch<R, U, CPB>(w, sc, qs, dsc, row_bytes, kb, row0, N, k0 / VPC, k0 / QK, 0, nch, lane);
+    if (k0 == 0) pdl_wait();  // x (and y when accumulating) may come from the previous kernel
     if (k0 > 0) __syncthreads();
-    stage_x<4>(sx, xp, k0, len, red);
+    stage_xf_scalar<QT == 8 ? 4 : 8>(sxf, xp, k0, len, red);
     __syncthreads();
     for (int cb = 0; cb < nch; cb += 32 * U) {
-      if (cb > 0) load_batch<R, U, 16, 2>(w, sc, q, dsc, (size_t)K, kb, row0, N, k0 / 16, k0 / QK, cb, nch, lane);
+      if (cb > 0) load_batch<R, U, CPB>(w, sc, qs, dsc, row_bytes, kb, row0, N, k0 / VPC, k0 / QK, cb, nch, lane);
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int c = cb + lane + 32 * u;
         if (c >= nch) break;
-        float4 xv[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) xv[j] = sx[swz<4>(c, j)];
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-          const uint32_t* wv = reinterpret_cast<const uint32_t*>(&w[r][u]);
-          float s = 0.f;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            float f0, f1, f2, f3;
-            s8x4_to_f32(wv[j], f0, f1, f2, f3);
-            s = fmaf(f0, xv[j].x, s);
-            s = fmaf(f1, xv[j].y, s);
-            s = fmaf(f2, xv[j].z, s);
-            s = fmaf(f3, xv[j].w, s);
-          }
-          acc[r] = fmaf(sc[r][u], s, acc[r]);
-        }
+        for (int r = 0; r < R; ++r)
+          acc[r] = fmaf(sc[r][u], QT == 8 ? dotf_q8(w[r][u], sxf, c) : dotf_q4(w[r][u], sxf, c), acc[r]);
       }
     }
   }
 #pragma unroll
   for (int r = 0; r < R; ++r) {
-    float v = warp_sum(acc[r]);
+    const float v = warp_sum(acc[r]);
     if (lane == 0 && row0 + r < N) y[row0 + r] = accumulate ? y[row0 + r] + v : v;
   }
 }
 
-template <int R, class XP>
-__global__ void __launch_bounds__(GEMV_THREADS) gemv_q4_0_kernel(const uint8_t* __restrict__ qs,
-                                                                 const uint16_t* __restrict__ dsc, XP xp,
-                                                                 float* __restrict__ y, int N, int K,
-                                                                 int accumulate) {
-  extern __shared__ float4 sx[];
+// QT = 8: Q8_0 rows (K bytes, 16-value chunks); QT = 4: Q4_0 rows (K / 2 bytes, one 32-value block per chunk).
+// CTA c owns the contiguous rows [c * N / G, (c + 1) * N / G) (G = grid size).  When K fits one staged
+// segment each warp walks the CTA's rows in batches of R rows, x is staged once, and the first batch is
+// loaded before griddepcontrol.wait -- with a grid of one batch per warp that is every weight byte of the
+// CTA; with the small streaming grid (`prefetch` set) the CTA also asks L2 for its whole row range at once.
+// Longer rows are split into K segments and the grid has one batch per warp.
+template <int QT, int R, int U, class XP>
+__global__ void __launch_bounds__(GEMV_THREADS, R == 1 ? GEMV_MIN_CTAS : GEMV_MIN_CTAS - 1)
+    gemv_kernel(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, XP xp, float* __restrict__ y, int N,
+                int K, int accumulate, int prefetch) {
+  constexpr int VPC = QT == 8 ? 16 : 32;  // values per chunk
+  constexpr int UPC = VPC / 8;            // 16-byte int16 units per chunk
+  constexpr int CPB = QT == 8 ? 2 : 1;    // chunks per block
+  static_assert(R * U == loads_per_lane(QT), "R rows x U chunks = the loads in flight per lane");
+  extern __shared__ int4 smem_x[];
   __shared__ float red[GEMV_WARPS + 1];
-  constexpr int U = UNROLL / 2;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row0 = (blockIdx.x * GEMV_WARPS + warp) * R;
+  // rows of this CTA: a balanced share of N (K <= SEG, warps loop over it) or exactly one batch per warp
+  const bool looped = K <= SEG;
+  const int r0 = looped ? (int)((long long)blockIdx.x * N / gridDim.x) : blockIdx.x * GEMV_WARPS * R;
+  const int nrows = looped ? (int)((long long)(blockIdx.x + 1) * N / gridDim.x) - r0 : min(GEMV_WARPS * R, N - r0);
   const int kb = K / QK;
+  const size_t row_bytes = QT == 8 ? (size_t)K : (size_t)K / 2;
+  int4 w[R][U];
+  float sc[R][U];
+  pdl_trigger();
+  if (looped) {
+    const int nch = K / VPC;
+    if (prefetch && threadIdx.x == 0) {
+      prefetch_l2(qs + (size_t)r0 * row_bytes, (size_t)nrows * row_bytes);
+      prefetch_l2(dsc + (size_t)r0 * kb, (size_t)nrows * kb * 2);
+    }
+    int rb = warp * R;  // first row (relative to r0) of this warp's current batch
+    load_batch<R, U, CPB>(w, sc, qs, dsc, row_bytes, kb, r0 + rb, r0 + nrows, 0, 0, 0, nch, lane);
+    float4* xf = reinterpret_cast<float4*>(smem_x);
+    int4* xq = smem_x + K / 4;
+    float* xs = reinterpret_cast<float*>(xq + K / 8);
+    int* xsum = QT == 4 ? reinterpret_cast<int*>(xs + kb) : nullptr;
+    pdl_wait();  // x (and y when accumulating) may come from the previous kernel
+    stage_xq<UPC>(xf, xq, xs, xsum, xp, 0, K, red);
+    __syncthreads();
+    for (; rb < nrows; rb += GEMV_WARPS * R) {
+      float acc[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) acc[r] = 0.f;
+      for (int cb = 0; cb < nch; cb += 32 * U) {
+        if (cb > 0) load_batch<R, U, CPB>(w, sc, qs, dsc, row_bytes, kb, r0 + rb, r0 + nrows, 0, 0, cb, nch, lane);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int c = cb + lane + 32 * u;
+          if (c >= nch) break;
+          chunk_dot<QT, R, U>(acc, w, sc, u, c, xq, xs, xsum);
+        }
+      }
+      // next batch of this warp: issue its loads before reducing this one
+      const int nb = rb + GEMV_WARPS * R;
+      if (nb < nrows) load_batch<R, U, CPB>(w, sc, qs, dsc, row_bytes, kb, r0 + nb, r0 + nrows, 0, 0, 0, nch, lane);
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const float v = warp_sum(acc[r]);
+        const int row = r0 + rb + r;
+        if (lane == 0 && rb + r < nrows) y[row] = accumulate ? y[row] + v : v;
+      }
+    }
+    return;
+  }
+  // K > SEG: one batch of R rows per warp, K in segments (x staged per segment)
+  const int row0 = r0 + warp * R;
   float acc[R];
 #pragma unroll
   for (int r = 0; r < R; ++r) acc[r] = 0.f;
-  int4 w[R][U];
-  float sc[R][U];
-
-  for (int k0 = 0; k0 < K; k0 += SEG_Q4) {
-    const int len = min(SEG_Q4, K - k0);
-    const int nch = len / QK;  // one chunk = one 32-value block = 16 bytes
-    if (k0 == 0) pdl_trigger();
-    load_batch<R, U, 16, 1>(w, sc, qs, dsc, (size_t)K / 2, kb, row0, N, k0 / QK, k0 / QK, 0, nch, lane);
+  for (int k0 = 0; k0 < K; k0 += SEG) {
+    const int len = min(SEG, K - k0);
+    const int nch = len / VPC;
+    float4* xf = reinterpret_cast<float4*>(smem_x);
+    int4* xq = smem_x + len / 4;
+    float* xs = reinterpret_cast<float*>(xq + len / 8);
+    int* xsum = QT == 4 ? reinterpret_cast<int*>(xs + len / QK) : nullptr;
+    load_batch<R, U, CPB>(w, sc, qs, dsc, row_bytes, kb, row0, r0 + nrows, k0 / VPC, k0 / QK, 0, nch, lane);
     if (k0 == 0) pdl_wait();
     if (k0 > 0) __syncthreads();
-    stage_x<8>(sx, xp, k0, len, red);
+    stage_xq<UPC>(xf, xq, xs, xsum, xp, k0, len, red);
     __syncthreads();
     for (int cb = 0; cb < nch; cb += 32 * U) {
-      if (cb > 0) load_batch<R, U, 16, 1>(w, sc, qs, dsc, (size_t)K / 2, kb, row0, N, k0 / QK, k0 / QK, cb, nch, lane);
+      if (cb > 0) load_batch<R, U, CPB>(w, sc, qs, dsc, row_bytes, kb, row0, r0 + nrows, k0 / VPC, k0 / QK, cb, nch, lane);
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int c = cb + lane + 32 * u;
         if (c >= nch) break;
-        float4 xv[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) xv[j] = sx[swz<8>(c, j)];
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-          const uint32_t* wv = reinterpret_cast<const uint32_t*>(&w[r][u]);
-          float s = 0.f;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            float f0, f1, f2, f3;
-            u4x4_to_f32(wv[j] & 0x0F0F0F0Fu, f0, f1, f2, f3);  // elements 4j..4j+3
-            s = fmaf(f0, xv[j].x, s);
-            s = fmaf(f1, xv[j].y, s);
-            s = fmaf(f2, xv[j].z, s);
-            s = fmaf(f3, xv[j].w, s);
-            u4x4_to_f32((wv[j] >> 4) & 0x0F0F0F0Fu, f0, f1, f2, f3);  // elements 16+4j..16+4j+3
-            s = fmaf(f0, xv[4 + j].x, s);
-            s = fmaf(f1, xv[4 + j].y, s);
-            s = fmaf(f2, xv[4 + j].z, s);
-            s = fmaf(f3, xv[4 + j].w, s);
-          }
-          acc[r] = fmaf(sc[r][u], s, acc[r]);
-        }
+        chunk_dot<QT, R, U>(acc, w, sc, u, c, xq, xs, xsum);
       }
     }
   }
 #pragma unroll
   for (int r = 0; r < R; ++r) {
-    float v = warp_sum(acc[r]);
-    if (lane == 0 && row0 + r < N) y[row0 + r] = accumulate ? y[row0 + r] + v : v;
+    const float v = warp_sum(acc[r]);
+    if (lane == 0 && row0 + r < r0 + nrows) y[row0 + r] = accumulate ? y[row0 + r] + v : v;
   }
 }
 
@@ -299,28 +523,80 @@ static int set_smem(Kern k, int bytes) {
   return kOk;
 }
 
-constexpr int Q4_R = 4;
+static int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
 
-// Rows per warp (R) and 16-byte chunks per lane per row (U) for a row of K int8 values: R * U stays at 16
-// loads in flight per lane, so short rows (K = 768: 48 chunks) still keep ~8 KB per warp in flight.
-template <class XP>
-static int launch_q8(const int8_t* qs, const uint16_t* d, const XP& xp, float* y, int n, int k, int accumulate,
-                     cudaStream_t s) {
+// Shape of the per-lane load batch: U chunks of each of R rows, R * U = loads_per_lane.  A row of nch chunks
+// takes U = loads_per_lane when it spans a whole warp pass; shorter rows give each warp more rows, so every
+// lane keeps the same number of loads in flight (Q8_0, K = 768: 48 chunks, U = 2, R = 4).
+template <int QT, class XP>
+static int launch_gemv(const uint8_t* qs, const uint16_t* d, const XP& xp, float* y, int n, int k, int accumulate,
+                       cudaStream_t s) {
   if (!qs || !d || !y || n < 0 || k <= 0 || k % QK) return kBadArgument;
   if (n == 0) return kOk;
-  const int smem = min(k, SEG_Q8) * 4;
-  const int chunks = min(k, SEG_Q8) / 16;
-  auto go = [&](auto kern, int r) -> int {
-    if (set_smem(kern, smem) != kOk) return kCudaError;
+  const int len = min(k, SEG);
+  const int nch = len / (QT == 8 ? 16 : 32);
+  const int smem = seg_smem_bytes(len);
+  // Streaming shapes (at least 64 MB of weights, K in one segment): int16 activations + DP2A, a grid of
+  // GEMV_STREAM_CTAS_PER_SM CTAs per SM walking contiguous row ranges that are prefetched into L2.  Smaller
+  // weights (the decode chain's GEMVs, whose time is set by the dependency on the previous kernel): fp32
+  // activations, one batch per warp, every weight load issued before griddepcontrol.wait, no prefetch.
+  const size_t weight_bytes = (QT == 8 ? (size_t)n * k : (size_t)n * k / 2) + (size_t)n * (k / QK) * 2;
+  const bool stream = k <= SEG && weight_bytes >= GEMV_STREAM_BYTES;
+  auto go = [&](auto kern, int r, int sm_bytes) -> int {  // streaming form (looped, prefetching)
+    if (set_smem(kern, sm_bytes) != kOk) return kCudaError;
     const int rows_per_cta = GEMV_WARPS * r;
-    const int grid = (n + rows_per_cta - 1) / rows_per_cta;
-    return launch_pdl(kern, dim3(grid), dim3(GEMV_THREADS), smem, s, qs, d, xp, y, n, k, accumulate) == cudaSuccess
+    const int grid = std::min((n + rows_per_cta - 1) / rows_per_cta, GEMV_STREAM_CTAS_PER_SM * sm_count());
+    return launch_pdl(kern, dim3(grid), dim3(GEMV_THREADS), sm_bytes, s, qs, d, xp, y, n, k, accumulate, 1) ==
+                   cudaSuccess
                ? kOk
                : kCudaError;
   };
-  if (chunks > 64) return go(gemv_q8_0_kernel<2, 8, XP>, 2);  // K >= 1056
-  if (chunks > 32) return go(gemv_q8_0_kernel<8, 2, XP>, 8);  // K in (512, 1024]
-  return go(gemv_q8_0_kernel<16, 1, XP>, 16);                 // K <= 512
+  auto go_direct = [&](auto kern, int r, int sm_bytes) -> int {  // decode-chain form
+    if (set_smem(kern, sm_bytes) != kOk) return kCudaError;
+    const int rows_per_cta = GEMV_WARPS * r;
+    const int grid = (n + rows_per_cta - 1) / rows_per_cta;
+    return launch_pdl(kern, dim3(grid), dim3(GEMV_THREADS), sm_bytes, s, qs, d, xp, y, n, k, accumulate) ==
+                   cudaSuccess
+               ? kOk
+               : kCudaError;
+  };
+  const int fsmem = len * 4;
+  if constexpr (QT == 8) {
+    if (stream) {
+      if (nch > 128) return go(gemv_kernel<QT, 1, 8, XP>, 1, smem);
+      if (nch > 64) return go(gemv_kernel<QT, 2, 4, XP>, 2, smem);
+      if (nch > 32) return go(gemv_kernel<QT, 4, 2, XP>, 4, smem);
+      return go(gemv_kernel<QT, 8, 1, XP>, 8, smem);
+    }
+    if (nch > 128) return go_direct(gemv_direct_kernel<QT, 1, 8, XP>, 1, fsmem);
+    if (nch > 64) return go_direct(gemv_direct_kernel<QT, 2, 4, XP>, 2, fsmem);
+    if (nch > 32) return go_direct(gemv_direct_kernel<QT, 4, 2, XP>, 4, fsmem);
+    return go_direct(gemv_direct_kernel<QT, 8, 1, XP>, 8, fsmem);
+  } else {
+  if (stream) {
+    if (nch > 64) return go(gemv_kernel<QT, 1, 4, XP>, 1, smem);
+    if (nch > 32) return go(gemv_kernel<QT, 2, 2, XP>, 2, smem);
+    return go(gemv_kernel<QT, 4, 1, XP>, 4, smem);
+  }
+  if (nch > 64) return go_direct(gemv_direct_kernel<QT, 1, 4, XP>, 1, fsmem);
+  if (nch > 32) return go_direct(gemv_direct_kernel<QT, 2, 2, XP>, 2, fsmem);
+  return go_direct(gemv_direct_kernel<QT, 4, 1, XP>, 4, fsmem);
+  }
+}
+
+template <class XP>
+static int launch_q8(const int8_t* qs, const uint16_t* d, const XP& xp, float* y, int n, int k, int accumulate,
+                     cudaStream_t s) {
+  return launch_gemv<8>(reinterpret_cast<const uint8_t*>(qs), d, xp, y, n, k, accumulate, s);
 }
 
 int gemv_q8_0(const int8_t* qs, const uint16_t* d, const float* x, float* y, int n, int k, int accumulate,
@@ -343,16 +619,8 @@ int gemv_q8_0_swiglu(const int8_t* qs, const uint16_t* d, const float* gate_up, 
 
 int gemv_q4_0(const uint8_t* qs, const uint16_t* d, const float* x, float* y, int n, int k, int accumulate,
               cudaStream_t s) {
-  if (!qs || !d || !x || !y || n < 0 || k <= 0 || k % QK) return kBadArgument;
-  if (n == 0) return kOk;
-  const int rows_per_cta = GEMV_WARPS * Q4_R;
-  const int grid = (n + rows_per_cta - 1) / rows_per_cta;
-  const int smem = min(k, SEG_Q4) * 4;
-  auto kern = gemv_q4_0_kernel<Q4_R, XPlain>;
-  if (set_smem(kern, smem) != kOk) return kCudaError;
-  return launch_pdl(kern, dim3(grid), dim3(GEMV_THREADS), smem, s, qs, d, XPlain{x}, y, n, k, accumulate) == cudaSuccess
-             ? kOk
-             : kCudaError;
+  if (!x) return kBadArgument;
+  return launch_gemv<4>(qs, d, XPlain{x}, y, n, k, accumulate, s);
 }
 
 }  // namespace zc

@@ -85,6 +85,18 @@ int swiglu_rows(const float* gu, float* out, int T, int ffn, cudaStream_t s);
 // (first index wins ties).  penalty <= 1 disables the penalty.  out[row] = token.
 int greedy_sample(float* logits, int rows, int vocab, const int32_t* past, const int32_t* past_len, int past_cap,
                   float penalty, int32_t* out, cudaStream_t s);
+// The same over a vocabulary slice [vocab_offset, vocab_offset + vocab): pairs[row] = (best value bits, global
+// index), INT_MAX index when nothing compares (all NaN); greedy_merge picks over [ranks][rows] pairs.
+int greedy_partial(float* logits, int rows, int vocab, int vocab_offset, const int32_t* past, const int32_t* past_len,
+                   int past_cap, float penalty, int2* pairs, cudaStream_t s);
+int greedy_merge(const int2* pairs, int ranks, int rows, int32_t* out, cudaStream_t s);
+// Batched generation: out[b][*step] = tokens[b] = next[b]; pos[b]++ for b < B; then (*step)++.
+int batch_advance(const int32_t* next, int32_t* tokens, int32_t* pos, int32_t* out, int out_stride, int32_t* step,
+                  int B, cudaStream_t s);
+// K/V rows [n][kvh][hd] (fp16 when half_input, else fp32) of positions start.. into the fp16 pools
+// [page][kvh][slot][hd] through one page-table row.
+int append_kv(const void* k, const void* v, int half_input, int n, int start, int kvh, int hd, const int32_t* pt_row,
+              int max_pages, int page_size, __half* k_pool, __half* v_pool, cudaStream_t s);
 // ctx_excl[b] = pos[b], ctx_incl[b] = pos[b] + 1 (the reference's per-layer causal lengths).
 int causal_lengths(const int32_t* pos, int B, int32_t* ctx_excl, int32_t* ctx_incl, cudaStream_t s);
 // Generation bookkeeping after a sampled step (B = 1): out[*step] = tok[0]; past[past_len] = tok[0];
