@@ -122,7 +122,7 @@ def _tp_worker(rank, world, port, out_dir):
         from zeroplatform_b200.engine import LlmEngine, broadcast_unique_id
         m = O.make_model(**TP_MODEL)
         uid = broadcast_unique_id(rank)
-        e = LlmEngine(m, max_batch=12, total_pages=128, tp_size=world, tp_rank=rank, nccl_id=uid)
+        e = LlmEngine(m, max_batch=16, total_pages=160, tp_size=world, tp_rank=rank, nccl_id=uid)
         rng = np.random.default_rng(31)
         lens = list(range(3, 27, 2))
         res = {"prefill": [], "shard": e.shard()}

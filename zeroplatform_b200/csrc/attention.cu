@@ -29,35 +29,44 @@ namespace {
 constexpr int ATT_WARPS = 4;
 constexpr int ATT_THREADS = ATT_WARPS * 32;
 constexpr int ATT_UNROLL = 4;
+// Resident CTAs per SM the register budget is sized for: the q and accumulator registers grow with the query
+// heads a CTA serves (GT), so one head (GQA group 1) gets 8 CTAs = 32 warps (<= 64 registers a thread).
+// fp32 pools hold twice the raw bytes per token in flight.
+__host__ __device__ constexpr int att_min_ctas(int gt, bool half_kv) {
+  return half_kv ? (gt == 1 ? 8 : gt == 2 ? 4 : gt == 4 ? 3 : 2) : (gt == 1 ? 4 : gt == 2 ? 3 : 2);
+}
 constexpr float LOG2E = 1.4426950408889634f;
 
+// Raw K/V words of one lane's 8 dimensions (one 16-byte load for fp16 pools, two for fp32), kept unconverted
+// while in flight and converted at use.
 template <typename KV>
-__device__ __forceinline__ void load8(const KV* p, float (&f)[8]);
-
+struct Raw8;
 template <>
-__device__ __forceinline__ void load8<__half>(const __half* p, float (&f)[8]) {
-  int4 r = ld_stream_v4(p);
-  const __half2* h = reinterpret_cast<const __half2*>(&r);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    float2 v = __half22float2(h[i]);
-    f[2 * i] = v.x;
-    f[2 * i + 1] = v.y;
-  }
+struct Raw8<__half> {
+  int4 v;
+};
+template <>
+struct Raw8<float> {
+  int4 a, b;
+};
+
+__device__ __forceinline__ void ld_raw(const __half* p, Raw8<__half>& r) { r.v = ld_stream_v4(p); }
+__device__ __forceinline__ void ld_raw(const float* p, Raw8<float>& r) {
+  r.a = ld_stream_v4(p);
+  r.b = ld_stream_v4(p + 4);
 }
+__device__ __forceinline__ void zero_raw(Raw8<__half>& r) { r.v = make_int4(0, 0, 0, 0); }
+__device__ __forceinline__ void zero_raw(Raw8<float>& r) { r.a = r.b = make_int4(0, 0, 0, 0); }
 
-template <>
-__device__ __forceinline__ void load8<float>(const float* p, float (&f)[8]) {
-  int4 a = ld_stream_v4(p);
-  int4 b = ld_stream_v4(p + 4);
-  f[0] = __int_as_float(a.x);
-  f[1] = __int_as_float(a.y);
-  f[2] = __int_as_float(a.z);
-  f[3] = __int_as_float(a.w);
-  f[4] = __int_as_float(b.x);
-  f[5] = __int_as_float(b.y);
-  f[6] = __int_as_float(b.z);
-  f[7] = __int_as_float(b.w);
+// element pair j (dims 2j, 2j+1) as fp32
+__device__ __forceinline__ float2 pair(const Raw8<__half>& r, int j) {
+  const int w = j == 0 ? r.v.x : j == 1 ? r.v.y : j == 2 ? r.v.z : r.v.w;
+  return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+__device__ __forceinline__ float2 pair(const Raw8<float>& r, int j) {
+  const int4& q = j < 2 ? r.a : r.b;
+  const int jj = j & 1;
+  return make_float2(__int_as_float(jj ? q.z : q.x), __int_as_float(jj ? q.w : q.y));
 }
 
 struct AttnDev {
@@ -77,7 +86,7 @@ struct AttnDev {
 };
 
 template <int HD, typename KV, int GT>
-__global__ void __launch_bounds__(ATT_THREADS) paged_attn_kernel(AttnDev a) {
+__global__ void __launch_bounds__(ATT_THREADS, att_min_ctas(GT, sizeof(KV) == 2)) paged_attn_kernel(AttnDev a) {
   constexpr int LPT = HD / 8;        // lanes per token
   constexpr int TPW = 32 / LPT;      // tokens per warp pass
   constexpr int NG = ATT_WARPS * TPW;  // token groups per CTA
@@ -102,57 +111,72 @@ __global__ void __launch_bounds__(ATT_THREADS) paged_attn_kernel(AttnDev a) {
   const KV* kp = reinterpret_cast<const KV*>(a.k_pool);
   const KV* vp = reinterpret_cast<const KV*>(a.v_pool);
 
-  float q[GT][8], m[GT], l[GT], acc[GT][8];
+  float2 q[GT][4], acc[GT][4];
+  float m[GT], l[GT];
 #pragma unroll
   for (int g = 0; g < GT; ++g) {
     const float* qg = a.q + (size_t)b * a.q_stride + (size_t)(qh0 + g) * HD + 8 * sub;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      q[g][e] = qg[e] * a.scale_log2;
-      acc[g][e] = 0.f;
+    for (int j = 0; j < 4; ++j) {
+      q[g][j] = make_float2(qg[2 * j] * a.scale_log2, qg[2 * j + 1] * a.scale_log2);
+      acc[g][j] = make_float2(0.f, 0.f);
     }
     m[g] = -INFINITY;
     l[g] = 0.f;
   }
 
+  // Each pass: ATT_UNROLL tokens per token group; the online softmax is updated once per pass (the block's
+  // maximum first, then one rescale of the running state and the block's exp2 weights).
   for (int t0 = t_begin + warp * TPW * ATT_UNROLL; t0 < t_end; t0 += ATT_WARPS * TPW * ATT_UNROLL) {
-    float kf[ATT_UNROLL][8], vf[ATT_UNROLL][8];
+    Raw8<KV> kr[ATT_UNROLL], vr[ATT_UNROLL];
     bool valid[ATT_UNROLL];
 #pragma unroll
     for (int u = 0; u < ATT_UNROLL; ++u) {
       const int t = t0 + u * TPW + tg;
       const int lp = t / P;
-      int page = (t < t_end && lp < a.max_pages) ? pt[lp] : -1;
+      const int page = (t < t_end && lp < a.max_pages) ? pt[lp] : -1;
       valid[u] = page >= 0 && page < a.num_pages;  // out-of-range page ids are never dereferenced
       if (valid[u]) {
         const long long off = page * a.page_stride + (long long)(t % P) * a.slot_stride +
                               (long long)kvh * a.head_stride + 8 * sub;
-        load8<KV>(kp + off, kf[u]);
-        load8<KV>(vp + off, vf[u]);
+        ld_raw(kp + off, kr[u]);
+        ld_raw(vp + off, vr[u]);
       } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) kf[u][e] = vf[u][e] = 0.f;
+        zero_raw(kr[u]);
+        zero_raw(vr[u]);
       }
     }
 #pragma unroll
-    for (int u = 0; u < ATT_UNROLL; ++u) {
+    for (int g = 0; g < GT; ++g) {
+      float sc[ATT_UNROLL];
+      float mb = -INFINITY;
 #pragma unroll
-      for (int g = 0; g < GT; ++g) {
-        float s = 0.f;
+      for (int u = 0; u < ATT_UNROLL; ++u) {
+        float2 s2 = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) s = fmaf(q[g][e], kf[u][e], s);
+        for (int j = 0; j < 4; ++j) s2 = __ffma2_rn(q[g][j], pair(kr[u], j), s2);
+        float s = s2.x + s2.y;
 #pragma unroll
         for (int o = LPT / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (valid[u]) {
-          const float mn = fmaxf(m[g], s);
-          const float alpha = exp2f(m[g] - mn);
-          const float p = exp2f(s - mn);
-          l[g] = l[g] * alpha + p;
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc[g][e] = fmaf(p, vf[u][e], acc[g][e] * alpha);
-          m[g] = mn;
-        }
+        sc[u] = valid[u] ? s : -INFINITY;
+        mb = fmaxf(mb, sc[u]);
       }
+      const float mn = fmaxf(m[g], mb);
+      if (mn == -INFINITY) continue;  // nothing valid yet for this token group
+      const float alpha = exp2f(m[g] - mn);
+      const float2 a2 = make_float2(alpha, alpha);
+      l[g] *= alpha;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[g][j] = __fmul2_rn(acc[g][j], a2);
+#pragma unroll
+      for (int u = 0; u < ATT_UNROLL; ++u) {
+        const float p = exp2f(sc[u] - mn);  // 0 for invalid tokens
+        l[g] += p;
+        const float2 p2 = make_float2(p, p);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[g][j] = __ffma2_rn(p2, pair(vr[u], j), acc[g][j]);
+      }
+      m[g] = mn;
     }
   }
 
@@ -164,7 +188,10 @@ __global__ void __launch_bounds__(ATT_THREADS) paged_attn_kernel(AttnDev a) {
       sm_l[gi][g] = l[g];
     }
 #pragma unroll
-    for (int e = 0; e < 8; ++e) sm_acc[gi][g][8 * sub + e] = acc[g][e];
+    for (int j = 0; j < 4; ++j) {
+      sm_acc[gi][g][8 * sub + 2 * j] = acc[g][j].x;
+      sm_acc[gi][g][8 * sub + 2 * j + 1] = acc[g][j].y;
+    }
   }
   __syncthreads();
 
