@@ -83,7 +83,15 @@ struct AttnDev {
   long long q_stride, out_stride, pt_stride;
   const int32_t* pt_rows;
   float scale_log2;
+  int out_half;  // out is __half instead of float
 };
+
+__device__ __forceinline__ void store_out(const AttnDev& a, size_t i, float v) {
+  if (a.out_half)
+    reinterpret_cast<__half*>(a.out)[i] = __float2half_rn(v);
+  else
+    a.out[i] = v;
+}
 
 template <int HD, typename KV, int GT>
 __global__ void __launch_bounds__(ATT_THREADS, att_min_ctas(GT, sizeof(KV) == 2)) paged_attn_kernel(AttnDev a) {
@@ -94,6 +102,8 @@ __global__ void __launch_bounds__(ATT_THREADS, att_min_ctas(GT, sizeof(KV) == 2)
   __shared__ float sm_l[NG][GT];
   __shared__ float sm_acc[NG][GT][HD];
   __shared__ int s_last;
+  pdl_trigger();
+  pdl_wait();  // q and the pages come from the previous kernels
 
   const int split = blockIdx.x, tile = blockIdx.y, b = blockIdx.z;
   const int splits = gridDim.x, tiles = gridDim.y;
@@ -211,7 +221,7 @@ __global__ void __launch_bounds__(ATT_THREADS, att_min_ctas(GT, sizeof(KV) == 2)
     }
     const size_t head = (size_t)b * a.hq + qh0 + g;
     if (splits == 1) {
-      a.out[(size_t)b * a.out_stride + (size_t)(qh0 + g) * HD + e] = L > 0.f ? O / L : 0.f;
+      store_out(a, (size_t)b * a.out_stride + (size_t)(qh0 + g) * HD + e, L > 0.f ? O / L : 0.f);
     } else {
       float* ws = a.ws + (head * splits + split) * (HD + 2);
       ws[e] = O;
@@ -249,7 +259,7 @@ __global__ void __launch_bounds__(ATT_THREADS, att_min_ctas(GT, sizeof(KV) == 2)
         O = fmaf(__ldcg(ws + s * (HD + 2) + e), w, O);
       }
     }
-    a.out[(size_t)b * a.out_stride + (size_t)(qh0 + g) * HD + e] = L > 0.f ? O / L : 0.f;
+    store_out(a, (size_t)b * a.out_stride + (size_t)(qh0 + g) * HD + e, L > 0.f ? O / L : 0.f);
   }
   if (threadIdx.x == 0) a.counters[(size_t)b * tiles + tile] = 0;  // ready for the next call
 }
@@ -257,14 +267,15 @@ __global__ void __launch_bounds__(ATT_THREADS, att_min_ctas(GT, sizeof(KV) == 2)
 template <int HD, typename KV>
 int launch_hd(const AttnDev& d, int batch, int tiles_gt, int gt, int splits, cudaStream_t s) {
   dim3 grid(splits, tiles_gt, batch);
+  cudaError_t e;
   switch (gt) {
-    case 1: paged_attn_kernel<HD, KV, 1><<<grid, ATT_THREADS, 0, s>>>(d); break;
-    case 2: paged_attn_kernel<HD, KV, 2><<<grid, ATT_THREADS, 0, s>>>(d); break;
-    case 4: paged_attn_kernel<HD, KV, 4><<<grid, ATT_THREADS, 0, s>>>(d); break;
-    case 8: paged_attn_kernel<HD, KV, 8><<<grid, ATT_THREADS, 0, s>>>(d); break;
+    case 1: e = launch_pdl(paged_attn_kernel<HD, KV, 1>, grid, dim3(ATT_THREADS), 0, s, d); break;
+    case 2: e = launch_pdl(paged_attn_kernel<HD, KV, 2>, grid, dim3(ATT_THREADS), 0, s, d); break;
+    case 4: e = launch_pdl(paged_attn_kernel<HD, KV, 4>, grid, dim3(ATT_THREADS), 0, s, d); break;
+    case 8: e = launch_pdl(paged_attn_kernel<HD, KV, 8>, grid, dim3(ATT_THREADS), 0, s, d); break;
     default: return kUnsupported;
   }
-  return cudaPeekAtLastError() == cudaSuccess ? kOk : kCudaError;
+  return e == cudaSuccess ? kOk : kCudaError;
 }
 
 template <typename KV>
@@ -336,6 +347,7 @@ int paged_attention(const PagedAttnArgs& a, cudaStream_t s) {
   d.out_stride = a.out_stride > 0 ? a.out_stride : (long long)a.hq * a.hd;
   d.pt_stride = a.pt_stride >= 0 ? a.pt_stride : (long long)a.max_pages;
   d.pt_rows = a.pt_rows;
+  d.out_half = a.out_half;
   const int tiles = a.hq / gt;
   return a.kv_half ? launch_kv<__half>(d, a.hd, a.batch, tiles, gt, splits, s)
                    : launch_kv<float>(d, a.hd, a.batch, tiles, gt, splits, s);

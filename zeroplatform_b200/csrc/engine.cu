@@ -130,6 +130,7 @@ struct Engine {
   int32_t* page_table = nullptr;  // [max_batch][max_pages_per_seq]
   int max_rows = 0;               // activation rows: max(max_batch, max_prefill_tokens)
   float *x = nullptr, *xn = nullptr, *qkv = nullptr, *attn = nullptr, *gu = nullptr, *sw = nullptr;
+  __half* xh = nullptr;  // fp16 activations feeding the tensor-core GEMM: [R][max(dim, q_dim, ffn)]
   float* logits = nullptr;      // [max_batch][vocab] (this rank's vocabulary slice)
   float* logits_all = nullptr;  // [tp][max_batch * vocab_chunk] gathered slices (tp > 1)
   int2* pairs = nullptr;        // [max_batch] arg-max of this rank's slice (tp > 1)
@@ -215,15 +216,22 @@ int linear(Engine* E, const DevW& w, const float* x, float* y, int rows, int acc
                       E->stream);
 }
 
-int attention(Engine* E, int layer, int T, const int32_t* ctx) {
+// The same on fp16 activations written by the previous kernel (rows >= kGemmMinRows: the tensor-core GEMM).
+int linear_h(Engine* E, const DevW& w, const __half* xh, float* y, int rows, int accumulate) {
+  return gemm_q8_0_tc_h(w.qs, w.d, xh, y, rows, w.n, w.k, accumulate, E->gemm_ws, E->gemm_ws_bytes, E->status,
+                        E->stream);
+}
+
+int attention(Engine* E, int layer, int T, const int32_t* ctx, bool half_out) {
   PagedAttnArgs a{};
+  a.out_half = half_out ? 1 : 0;
   a.q = E->qkv;
   a.k_pool = E->kpool + (size_t)layer * E->layer_pool_elems;
   a.v_pool = E->vpool + (size_t)layer * E->layer_pool_elems;
   a.page_table = E->page_table;
   a.pt_rows = E->rows;
   a.ctx_len = ctx;
-  a.out = E->attn;
+  a.out = half_out ? reinterpret_cast<float*>(E->xh) : E->attn;
   a.batch = T;
   a.hq = E->hq;
   a.hkv = E->hkv;
@@ -260,11 +268,18 @@ int forward(Engine* E, int T, bool all_logits) {
   const int L = c.layers;
   const int acc = residual_mode(E);
   E_RC(causal_lengths(E->pos, T, E->ctx_ex, E->ctx_in, E->stream));
+  // T >= kGemmMinRows: every projection runs on the tensor cores and its input is written in fp16 by the
+  // kernel before it (RmsNorm, attention, SwiGLU); 1 < T < kGemmMinRows: fp32 GEMVs per row; T == 1: the
+  // fused GEMVs.
+  const bool tc = T >= kGemmMinRows;
   for (int l = 0; l < L; ++l) {
     const float* an = E->attn_norm + (size_t)l * c.dim;
     const float* fn = E->ffn_norm + (size_t)l * c.dim;
     if (T == 1) {
       E_RC(gemv_q8_0_rmsnorm(E->wqkv[l].qs, E->wqkv[l].d, E->x, an, c.eps, E->qkv, E->qkv_dim, c.dim, 0, E->stream));
+    } else if (tc) {
+      E_RC(rmsnorm_h(E->x, an, E->xh, T, c.dim, c.eps, E->stream));
+      E_RC(linear_h(E, E->wqkv[l], E->xh, E->qkv, T, 0));
     } else {
       E_RC(rmsnorm(E->x, an, E->xn, T, c.dim, c.eps, E->stream));
       E_RC(linear(E, E->wqkv[l], E->xn, E->qkv, T, 0));
@@ -273,12 +288,20 @@ int forward(Engine* E, int T, bool all_logits) {
                         c.page_size, E->cos_t, E->sin_t, E->max_pos, E->kpool + (size_t)l * E->layer_pool_elems,
                         E->vpool + (size_t)l * E->layer_pool_elems, E->stream));
     const int32_t* ctx = (c.reference_causal_quirk && l != L - 1) ? E->ctx_ex : E->ctx_in;
-    E_RC(attention(E, l, T, ctx));
-    E_RC(linear(E, E->wo[l], E->attn, E->x, T, acc));  // x += Wo . attn (MatVecAddQ8_0)
+    E_RC(attention(E, l, T, ctx, tc));
+    if (tc)
+      E_RC(linear_h(E, E->wo[l], E->xh, E->x, T, acc));  // x += Wo . attn (MatVecAddQ8_0)
+    else
+      E_RC(linear(E, E->wo[l], E->attn, E->x, T, acc));
     E_RC(allreduce_x(E, T));
     if (T == 1) {
       E_RC(gemv_q8_0_rmsnorm(E->wgu[l].qs, E->wgu[l].d, E->x, fn, c.eps, E->gu, 2 * E->ffn, c.dim, 0, E->stream));
       E_RC(gemv_q8_0_swiglu(E->wdown[l].qs, E->wdown[l].d, E->gu, E->x, c.dim, E->ffn, acc, E->stream));
+    } else if (tc) {
+      E_RC(rmsnorm_h(E->x, fn, E->xh, T, c.dim, c.eps, E->stream));
+      E_RC(linear_h(E, E->wgu[l], E->xh, E->gu, T, 0));
+      E_RC(swiglu_rows_h(E->gu, E->xh, T, E->ffn, E->stream));
+      E_RC(linear_h(E, E->wdown[l], E->xh, E->x, T, acc));
     } else {
       E_RC(rmsnorm(E->x, fn, E->xn, T, c.dim, c.eps, E->stream));
       E_RC(linear(E, E->wgu[l], E->xn, E->gu, T, 0));
@@ -288,8 +311,13 @@ int forward(Engine* E, int T, bool all_logits) {
     E_RC(allreduce_x(E, T));
   }
   if (all_logits && T > 1) {
-    E_RC(rmsnorm(E->x, E->final_norm, E->xn, T, c.dim, c.eps, E->stream));
-    E_RC(linear(E, E->lm_head, E->xn, E->logits, T, 0));
+    if (tc) {
+      E_RC(rmsnorm_h(E->x, E->final_norm, E->xh, T, c.dim, c.eps, E->stream));
+      E_RC(linear_h(E, E->lm_head, E->xh, E->logits, T, 0));
+    } else {
+      E_RC(rmsnorm(E->x, E->final_norm, E->xn, T, c.dim, c.eps, E->stream));
+      E_RC(linear(E, E->lm_head, E->xn, E->logits, T, 0));
+    }
   } else {  // LM head only for the last row (PrefillPrompt, LlmEngine.cs:307-314)
     const float* xl = E->x + (size_t)(T - 1) * c.dim;
     E_RC(gemv_q8_0_rmsnorm(E->lm_head.qs, E->lm_head.d, xl, E->final_norm, c.eps, E->logits, E->vocab, c.dim, 0,
@@ -569,6 +597,7 @@ int32_t zcu_engine_create_tp(const zcu_engine_config* cfg, int32_t tp_size, int3
   step(dalloc(E, &E->attn, (size_t)R * E->q_dim));
   step(dalloc(E, &E->gu, (size_t)R * 2 * E->ffn));
   step(dalloc(E, &E->sw, (size_t)R * E->ffn));
+  step(dalloc(E, &E->xh, (size_t)R * std::max(std::max(c.dim, E->q_dim), E->ffn)));
   step(dalloc(E, &E->logits, (size_t)c.max_batch * E->vocab_chunk));
   if (tp_size > 1) {
     step(dalloc(E, &E->logits_all, (size_t)tp_size * c.max_batch * E->vocab_chunk));

@@ -19,6 +19,8 @@ __global__ void rope_append_kernel(float* __restrict__ qkv, int T, int hq, int h
                                    const int32_t* __restrict__ page_table, int max_pages, int page_size,
                                    const float* __restrict__ cos_t, const float* __restrict__ sin_t, int max_pos,
                                    __half* __restrict__ k_pool, __half* __restrict__ v_pool) {
+  pdl_trigger();
+  pdl_wait();
   const int half = hd / 2;
   const int q_dim = hq * hd, kv_dim = hkv * hd;
   const int row_len = q_dim + 2 * kv_dim;
@@ -61,14 +63,17 @@ __global__ void rope_append_kernel(float* __restrict__ qkv, int T, int hq, int h
   }
 }
 
-__global__ void swiglu_rows_kernel(const float* __restrict__ gu, float* __restrict__ out, int T, int ffn) {
+template <typename OutT>
+__global__ void swiglu_rows_kernel(const float* __restrict__ gu, OutT* __restrict__ out, int T, int ffn) {
+  pdl_trigger();
+  pdl_wait();
   const size_t total = (size_t)T * ffn;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const int t = (int)(i / ffn), j = (int)(i % ffn);
     const float g = gu[(size_t)t * 2 * ffn + j];
     const float u = gu[(size_t)t * 2 * ffn + ffn + j];
     const float sg = 1.0f / (1.0f + expf(-g));
-    out[i] = __fmul_rn(__fmul_rn(g, sg), u);
+    out[i] = (OutT)__fmul_rn(__fmul_rn(g, sg), u);
   }
 }
 
@@ -80,6 +85,8 @@ __global__ void swiglu_rows_kernel(const float* __restrict__ gu, float* __restri
 __global__ void greedy_kernel(float* __restrict__ logits, int vocab, const int32_t* __restrict__ past,
                               const int32_t* __restrict__ past_len, int past_cap, float penalty,
                               int32_t* __restrict__ out, int vocab_offset, int2* __restrict__ pairs) {
+  pdl_trigger();
+  pdl_wait();
   float* lg = logits + (size_t)blockIdx.x * vocab;
   if (penalty > 1.0f && past && past_len) {
     if (threadIdx.x == 0) {
@@ -136,6 +143,8 @@ __global__ void greedy_kernel(float* __restrict__ logits, int vocab, const int32
 
 // pairs [ranks][rows] of (value bits, global index) -> the row's token: largest value, lowest index on ties.
 __global__ void greedy_merge_kernel(const int2* __restrict__ pairs, int ranks, int rows, int32_t* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
     float best = -INFINITY;
     int idx = 0x7fffffff;
@@ -156,6 +165,8 @@ __global__ void greedy_merge_kernel(const int2* __restrict__ pairs, int ranks, i
 __global__ void batch_advance_kernel(const int32_t* __restrict__ next, int32_t* __restrict__ tokens,
                                      int32_t* __restrict__ pos, int32_t* __restrict__ out, int out_stride,
                                      int32_t* __restrict__ step, int B) {
+  pdl_trigger();
+  pdl_wait();
   const int st = *step;
   for (int b = threadIdx.x; b < B; b += blockDim.x) {
     const int t = next[b];
@@ -190,6 +201,8 @@ __global__ void append_kv_kernel(const T* __restrict__ k, const T* __restrict__ 
 
 __global__ void causal_kernel(const int32_t* __restrict__ pos, int B, int32_t* __restrict__ ex,
                               int32_t* __restrict__ in) {
+  pdl_trigger();
+  pdl_wait();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b < B) {
     ex[b] = pos[b];
@@ -200,6 +213,8 @@ __global__ void causal_kernel(const int32_t* __restrict__ pos, int B, int32_t* _
 __global__ void advance_kernel(const int32_t* __restrict__ tok, int32_t* __restrict__ pos, int32_t* __restrict__ out,
                                int32_t* __restrict__ step, int32_t* __restrict__ past, int32_t* __restrict__ past_len,
                                int past_cap, int eos, int32_t* __restrict__ done) {
+  pdl_trigger();
+  pdl_wait();
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
   if (*done) return;
   const int t = tok[0];
@@ -229,43 +244,63 @@ int rope_append_kv(float* qkv, int T, int hq, int hkv, int hd, const int32_t* po
   if (!qkv || !pos || !rows || !page_table || !cos_t || !sin_t || !k_pool || !v_pool || (hd & 1)) return kBadArgument;
   if (T <= 0) return kOk;
   const size_t n = (size_t)T * (hq + 2 * hkv) * (hd / 2);
-  rope_append_kernel<<<grid_for(n, 256), 256, 0, s>>>(qkv, T, hq, hkv, hd, pos, rows, page_table, max_pages,
-                                                       page_size, cos_t, sin_t, max_pos, k_pool, v_pool);
-  return launched();
+  return launch_pdl(rope_append_kernel, dim3(grid_for(n, 256)), dim3(256), 0, s, qkv, T, hq, hkv, hd, pos, rows,
+                    page_table, max_pages, page_size, cos_t, sin_t, max_pos, k_pool, v_pool) == cudaSuccess
+             ? kOk
+             : kCudaError;
 }
 
 int swiglu_rows(const float* gu, float* out, int T, int ffn, cudaStream_t s) {
   if (!gu || !out) return kBadArgument;
   if (T <= 0) return kOk;
-  swiglu_rows_kernel<<<grid_for((size_t)T * ffn, 256), 256, 0, s>>>(gu, out, T, ffn);
-  return launched();
+  return launch_pdl(swiglu_rows_kernel<float>, dim3(grid_for((size_t)T * ffn, 256)), dim3(256), 0, s, gu, out, T,
+                    ffn) == cudaSuccess
+             ? kOk
+             : kCudaError;
+}
+
+int swiglu_rows_h(const float* gu, __half* out, int T, int ffn, cudaStream_t s) {
+  if (!gu || !out) return kBadArgument;
+  if (T <= 0) return kOk;
+  return launch_pdl(swiglu_rows_kernel<__half>, dim3(grid_for((size_t)T * ffn, 256)), dim3(256), 0, s, gu, out, T,
+                    ffn) == cudaSuccess
+             ? kOk
+             : kCudaError;
 }
 
 int greedy_sample(float* logits, int rows, int vocab, const int32_t* past, const int32_t* past_len, int past_cap,
                   float penalty, int32_t* out, cudaStream_t s) {
   if (!logits || !out || rows <= 0 || vocab <= 0) return kBadArgument;
-  greedy_kernel<<<rows, 1024, 0, s>>>(logits, vocab, past, past_len, past_cap, penalty, out, 0, nullptr);
-  return launched();
+  return launch_pdl(greedy_kernel, dim3(rows), dim3(1024), 0, s, logits, vocab, past, past_len, past_cap, penalty, out,
+                    0, (int2*)nullptr) == cudaSuccess
+             ? kOk
+             : kCudaError;
 }
 
 int greedy_partial(float* logits, int rows, int vocab, int vocab_offset, const int32_t* past, const int32_t* past_len,
                    int past_cap, float penalty, int2* pairs, cudaStream_t s) {
   if (!logits || !pairs || rows <= 0 || vocab <= 0) return kBadArgument;
-  greedy_kernel<<<rows, 1024, 0, s>>>(logits, vocab, past, past_len, past_cap, penalty, nullptr, vocab_offset, pairs);
-  return launched();
+  return launch_pdl(greedy_kernel, dim3(rows), dim3(1024), 0, s, logits, vocab, past, past_len, past_cap, penalty,
+                    (int32_t*)nullptr, vocab_offset, pairs) == cudaSuccess
+             ? kOk
+             : kCudaError;
 }
 
 int greedy_merge(const int2* pairs, int ranks, int rows, int32_t* out, cudaStream_t s) {
   if (!pairs || !out || ranks <= 0 || rows <= 0) return kBadArgument;
-  greedy_merge_kernel<<<(rows + 255) / 256, 256, 0, s>>>(pairs, ranks, rows, out);
-  return launched();
+  return launch_pdl(greedy_merge_kernel, dim3((rows + 255) / 256), dim3(256), 0, s, pairs, ranks, rows, out) ==
+                 cudaSuccess
+             ? kOk
+             : kCudaError;
 }
 
 int batch_advance(const int32_t* next, int32_t* tokens, int32_t* pos, int32_t* out, int out_stride, int32_t* step,
                   int B, cudaStream_t s) {
   if (!next || !tokens || !pos || !out || !step || B <= 0) return kBadArgument;
-  batch_advance_kernel<<<1, 1024, 0, s>>>(next, tokens, pos, out, out_stride, step, B);
-  return launched();
+  return launch_pdl(batch_advance_kernel, dim3(1), dim3(1024), 0, s, next, tokens, pos, out, out_stride, step, B) ==
+                 cudaSuccess
+             ? kOk
+             : kCudaError;
 }
 
 int append_kv(const void* k, const void* v, int half_input, int n, int start, int kvh, int hd, const int32_t* pt_row,
@@ -287,14 +322,17 @@ int append_kv(const void* k, const void* v, int half_input, int n, int start, in
 int causal_lengths(const int32_t* pos, int B, int32_t* ctx_excl, int32_t* ctx_incl, cudaStream_t s) {
   if (!pos || !ctx_excl || !ctx_incl) return kBadArgument;
   if (B <= 0) return kOk;
-  causal_kernel<<<(B + 255) / 256, 256, 0, s>>>(pos, B, ctx_excl, ctx_incl);
-  return launched();
+  return launch_pdl(causal_kernel, dim3((B + 255) / 256), dim3(256), 0, s, pos, B, ctx_excl, ctx_incl) == cudaSuccess
+             ? kOk
+             : kCudaError;
 }
 
 int advance_generation(const int32_t* tok, int32_t* pos, int32_t* out, int32_t* step, int32_t* past,
                        int32_t* past_len, int past_cap, int eos, int32_t* done, cudaStream_t s) {
-  advance_kernel<<<1, 32, 0, s>>>(tok, pos, out, step, past, past_len, past_cap, eos, done);
-  return launched();
+  return launch_pdl(advance_kernel, dim3(1), dim3(32), 0, s, tok, pos, out, step, past, past_len, past_cap, eos,
+                    done) == cudaSuccess
+             ? kOk
+             : kCudaError;
 }
 
 }  // namespace zc

@@ -17,7 +17,7 @@
 //   warps 4-11  dequantizers: int8 W tile (shared memory) x fp16 block scales -> fp16 q*d in the UMMA
 //               K-major 128B-swizzled layout (fence.proxy.async before signalling the MMA warp)
 //   warps 12-15 epilogue: tcgen05.ld 32 TMEM columns at a time, coalesced fp32 stores of Y (or of the
-//               split-K partials, reduced afterwards in a fixed order)
+//               split-K partials, summed afterwards in split order by splitk_reduce_kernel)
 // The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue of one tile overlaps the
 // MMAs of the next.  Every mbarrier wait is bounded: on time-out the CTA records an error code in
 // `status`, stops issuing work, drains what it issued and frees its TMEM before returning.
@@ -47,10 +47,12 @@ constexpr int W_SUB = 4;                    // k-stages per int8 weight tile (on
 constexpr int W_TILE_BYTES = BM * BK * W_SUB;     // 32 KB of int8 W per weight stage
 constexpr int S_TILE_BYTES = BM * BK * W_SUB / QK * 2;  // + 2 KB of its fp16 block scales (8 per row)
 constexpr int W_STAGE_BYTES = W_TILE_BYTES + S_TILE_BYTES;
+constexpr int MAX_SPLITS = 8;               // split-K ranges per output tile at most
 
 struct GemmParams {
   const uint16_t* d;
-  float* y;         // output, or split partials [splits][M][N] when splits > 1
+  float* y;         // output [M][N]
+  float* part;      // split partials [splits][M][N] (splits > 1)
   int* status;
   int M, N, K;
   int accumulate;
@@ -194,6 +196,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Programmatic dependent launch: the next kernel may be scheduled now.  Weights never depend on the
+  // previous kernel, so the weight producer and the dequantizers start at once; the activation producer and
+  // the epilogue wait for the previous kernel (its X is read, and Y may still be read by it) first.
+  pdl_trigger();
 
   // Work unit u -> output tile u / splits (weight tile major), K range (u % splits).
   auto unit_tile = [&](int u) { return u / p.splits; };
@@ -225,6 +231,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   } else if (warp == 2) {
     // ---------------- TMA producer: fp16 activation tiles [bn tokens x 64 k] ----------------
     if (lane == 0) {
+      pdl_wait();
       int s = 0;
       uint32_t ph = 0;
       for (int u = blockIdx.x; u < n_units && !*abort_flag; u += gridDim.x) {
@@ -348,6 +355,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
   } else if (warp >= EPI_WARP0) {
     // ---------------- epilogue (4 warps -> TMEM lane quadrants warp % 4) ----------------
+    pdl_wait();
     const int quad = warp & 3;
     const int row_in_tile = quad * 32 + lane;
     int it = 0;
@@ -359,7 +367,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const int t = unit_tile(u);
       const int row = (t / p.n_tok_tiles) * BM + row_in_tile;
       const int tok0 = (t % p.n_tok_tiles) * bn;
-      float* out = p.splits > 1 ? p.y + (size_t)(u % p.splits) * p.M * p.N : p.y;
+      const size_t mn = (size_t)p.M * p.N;
+      float* out = p.splits > 1 ? p.part + (size_t)(u % p.splits) * mn : p.y;
       const bool acc_mode = p.splits == 1 && p.accumulate;
       for (int c0 = 0; c0 < bn; c0 += 32) {
         uint32_t r[32];
@@ -393,6 +402,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 // Split-K reduction in a fixed order (deterministic): y (=|+=) sum_s part[s].
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, float* __restrict__ y, size_t mn, int splits,
                                      int accumulate) {
+  pdl_trigger();
+  pdl_wait();
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < mn; i += (size_t)gridDim.x * blockDim.x) {
     float v = part[i];
     for (int s = 1; s < splits; ++s) v += part[(size_t)s * mn + i];
@@ -401,6 +412,8 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ part, float* __re
 }
 
 __global__ void f32_to_f16_kernel(const float* __restrict__ x, __half* __restrict__ y, size_t n) {
+  pdl_trigger();
+  pdl_wait();
   const size_t n4 = n / 4;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
     const float4 v = reinterpret_cast<const float4*>(x)[i];
@@ -469,7 +482,7 @@ static GemmConfig choose_config(int m, int n, int k) {
     if (bn > 32 && m <= bn / 2) continue;  // a narrower tile already covers every token
     const int tok_tiles = (m + bn - 1) / bn;
     const int tiles = ((n + BM - 1) / BM) * tok_tiles;
-    const int max_s = m <= 128 ? 8 : 1;
+    const int max_s = m <= 128 ? MAX_SPLITS : 1;
     for (int sp = 1; sp <= max_s; ++sp) {
       const int kb_per = ((nk + sp - 1) / sp + W_SUB - 1) / W_SUB * W_SUB;  // whole weight tiles per split
       if (sp > 1 && kb_per < 8) break;
@@ -490,6 +503,8 @@ static GemmConfig choose_config(int m, int n, int k) {
 
 static size_t align256(size_t b) { return (b + 255) & ~size_t(255); }
 
+// Workspace: [fp16 X][split partials].
+
 }  // namespace
 
 size_t gemm_q8_0_workspace_bytes(int m, int n, int k) {
@@ -499,30 +514,20 @@ size_t gemm_q8_0_workspace_bytes(int m, int n, int k) {
   return b;
 }
 
-int gemm_q8_0_tc(const int8_t* qs, const uint16_t* d, const float* x, float* y, int m, int n, int k, int accumulate,
-                 void* workspace, size_t workspace_bytes, int* status, cudaStream_t s) {
-  if (!qs || !d || !x || !y || !status || m <= 0 || n <= 0 || k <= 0 || k % QK) return kBadArgument;
-  if (k % 16) return kUnsupported;  // TMA row pitches (fp16 activations, int8 weights) must be 16-byte multiples
-  if (!workspace || workspace_bytes < gemm_q8_0_workspace_bytes(m, n, k)) return kBadArgument;
-  if (reinterpret_cast<uintptr_t>(workspace) & 255 || reinterpret_cast<uintptr_t>(x) & 15 ||
-      reinterpret_cast<uintptr_t>(qs) & 15 || reinterpret_cast<uintptr_t>(d) & 15)
-    return kUnsupported;
+// Core launcher on fp16 activations x16 [m][k] (16-byte aligned rows).
+static int launch_gemm(const int8_t* qs, const uint16_t* d, const __half* x16, float* y, int m, int n, int k,
+                       int accumulate, char* ws, int* status, cudaStream_t s) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return kCudaError;
   const GemmConfig c = choose_config(m, n, k);
-  __half* x16 = reinterpret_cast<__half*>(workspace);
-  float* part = reinterpret_cast<float*>(static_cast<char*>(workspace) + align256((size_t)m * k * 2));
-  const size_t nx = (size_t)m * k;
-  f32_to_f16_kernel<<<(unsigned)std::min<size_t>((nx / 4 + 255) / 256, 148 * 8), 256, 0, s>>>(x, x16, nx);
-  if (cudaPeekAtLastError() != cudaSuccess) return kCudaError;
-
+  float* part = reinterpret_cast<float*>(ws + align256((size_t)m * k * 2));
   CUtensorMap xmap, wmap;
   {
     cuuint64_t gdim[2] = {(cuuint64_t)k, (cuuint64_t)m};
     cuuint64_t gstride[1] = {(cuuint64_t)k * 2};
     cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)c.bn};
     cuuint32_t estride[2] = {1, 1};
-    if (enc(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x16, gdim, gstride, box, estride,
+    if (enc(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(x16), gdim, gstride, box, estride,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return kCudaError;
@@ -555,7 +560,8 @@ int gemm_q8_0_tc(const int8_t* qs, const uint16_t* d, const float* x, float* y, 
   GemmParams p;
   p.d = d;
   p.scale_tma = scale_tma;
-  p.y = c.splits > 1 ? part : y;
+  p.y = y;
+  p.part = part;
   p.status = status;
   p.M = m;
   p.N = n;
@@ -572,15 +578,47 @@ int gemm_q8_0_tc(const int8_t* qs, const uint16_t* d, const float* x, float* y, 
   if (cudaFuncSetAttribute(gemm_q8_0_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return kCudaError;
   const int grid = std::min(c.n_tiles * c.splits, num_sms());
-  gemm_q8_0_tc_kernel<<<grid, GEMM_THREADS, smem, s>>>(xmap, wmap, smap, p);
-  if (cudaPeekAtLastError() != cudaSuccess) return kCudaError;
+  if (launch_pdl(gemm_q8_0_tc_kernel, dim3(grid), dim3(GEMM_THREADS), (size_t)smem, s, xmap, wmap, smap, p) !=
+      cudaSuccess)
+    return kCudaError;
   if (c.splits > 1) {
     const size_t mn = (size_t)m * n;
-    splitk_reduce_kernel<<<(unsigned)std::min<size_t>((mn + 255) / 256, 148 * 8), 256, 0, s>>>(part, y, mn, c.splits,
-                                                                                               accumulate);
-    if (cudaPeekAtLastError() != cudaSuccess) return kCudaError;
+    if (launch_pdl(splitk_reduce_kernel, dim3((unsigned)std::min<size_t>((mn + 255) / 256, 148 * 8)), dim3(256), 0,
+                   s, (const float*)part, y, mn, c.splits, accumulate) != cudaSuccess)
+      return kCudaError;
   }
   return kOk;
+}
+
+static int check_gemm_args(const void* qs, const void* d, const void* x, const void* y, int m, int n, int k,
+                           const void* workspace, size_t workspace_bytes, const int* status) {
+  if (!qs || !d || !x || !y || !status || m <= 0 || n <= 0 || k <= 0 || k % QK) return kBadArgument;
+  if (k % 16) return kUnsupported;  // TMA row pitches (fp16 activations, int8 weights) must be 16-byte multiples
+  if (!workspace || workspace_bytes < gemm_q8_0_workspace_bytes(m, n, k)) return kBadArgument;
+  if (reinterpret_cast<uintptr_t>(workspace) & 255 || reinterpret_cast<uintptr_t>(x) & 15 ||
+      reinterpret_cast<uintptr_t>(qs) & 15 || reinterpret_cast<uintptr_t>(d) & 15)
+    return kUnsupported;
+  return kOk;
+}
+
+int gemm_q8_0_tc(const int8_t* qs, const uint16_t* d, const float* x, float* y, int m, int n, int k, int accumulate,
+                 void* workspace, size_t workspace_bytes, int* status, cudaStream_t s) {
+  const int rc = check_gemm_args(qs, d, x, y, m, n, k, workspace, workspace_bytes, status);
+  if (rc != kOk) return rc;
+  char* ws = static_cast<char*>(workspace);
+  __half* x16 = reinterpret_cast<__half*>(ws);
+  const size_t nx = (size_t)m * k;
+  if (launch_pdl(f32_to_f16_kernel, dim3((unsigned)std::min<size_t>((nx / 4 + 255) / 256, 148 * 8)), dim3(256), 0, s,
+                 x, x16, nx) != cudaSuccess)
+    return kCudaError;
+  return launch_gemm(qs, d, x16, y, m, n, k, accumulate, ws, status, s);
+}
+
+int gemm_q8_0_tc_h(const int8_t* qs, const uint16_t* d, const __half* x16, float* y, int m, int n, int k,
+                   int accumulate, void* workspace, size_t workspace_bytes, int* status, cudaStream_t s) {
+  const int rc = check_gemm_args(qs, d, x16, y, m, n, k, workspace, workspace_bytes, status);
+  if (rc != kOk) return rc;
+  return launch_gemm(qs, d, x16, y, m, n, k, accumulate, static_cast<char*>(workspace), status, s);
 }
 
 }  // namespace zc

@@ -17,11 +17,16 @@ namespace zc {
 
 namespace {
 
-__global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ out,
+// One CTA per row.  OutT = float, or __half when the row feeds the tensor-core GEMM directly.  Launched with
+// programmatic dependent launch: it waits for the previous kernel before reading x.
+template <typename OutT>
+__global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w, OutT* __restrict__ out,
                                int n, float eps) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red[32];
   const float* xr = x + (size_t)blockIdx.x * n;
-  float* orow = out + (size_t)blockIdx.x * n;
+  OutT* orow = out + (size_t)blockIdx.x * n;
   float ss = 0.f;
   for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
   ss = warp_sum(ss);
@@ -35,7 +40,7 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
   __syncthreads();
   const float mean_sq = red[0] / (float)n;
   const float inv = 1.0f / (float)sqrt((double)(mean_sq + eps));
-  for (int i = threadIdx.x; i < n; i += blockDim.x) orow[i] = xr[i] * inv * w[i];
+  for (int i = threadIdx.x; i < n; i += blockDim.x) orow[i] = (OutT)(xr[i] * inv * w[i]);
 }
 
 __global__ void swiglu_kernel(const float* __restrict__ g, const float* __restrict__ u, float* __restrict__ out,
@@ -76,6 +81,8 @@ __global__ void rope_kernel(float* __restrict__ x, int rows, int heads, int hd, 
 
 __global__ void embed_q8_0_kernel(const int8_t* __restrict__ qs, const uint16_t* __restrict__ d,
                                   const int32_t* __restrict__ tokens, int vocab, int dim, float* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   int tok = tokens[blockIdx.x];
   if (tok < 0 || tok >= vocab) tok = 0;  // unknown ids map to 0 (LlmEngine.cs:321)
   const int8_t* row = qs + (size_t)tok * dim;
@@ -172,8 +179,18 @@ int rmsnorm(const float* x, const float* w, float* out, int rows, int n, float e
   if (!x || !w || !out || rows < 0 || n <= 0) return kBadArgument;
   if (rows == 0) return kOk;
   int threads = n >= 1024 ? 512 : (n >= 256 ? 256 : 128);
-  rmsnorm_kernel<<<rows, threads, 0, s>>>(x, w, out, n, eps);
-  return launched();
+  return launch_pdl(rmsnorm_kernel<float>, dim3(rows), dim3(threads), 0, s, x, w, out, n, eps) == cudaSuccess
+             ? kOk
+             : kCudaError;
+}
+
+int rmsnorm_h(const float* x, const float* w, __half* out, int rows, int n, float eps, cudaStream_t s) {
+  if (!x || !w || !out || rows < 0 || n <= 0) return kBadArgument;
+  if (rows == 0) return kOk;
+  int threads = n >= 1024 ? 512 : (n >= 256 ? 256 : 128);
+  return launch_pdl(rmsnorm_kernel<__half>, dim3(rows), dim3(threads), 0, s, x, w, out, n, eps) == cudaSuccess
+             ? kOk
+             : kCudaError;
 }
 
 int swiglu(const float* gate, const float* up, float* out, size_t n, cudaStream_t s) {
@@ -203,8 +220,9 @@ int embed_q8_0(const int8_t* qs, const uint16_t* d, const int32_t* tokens, int n
                float* out, cudaStream_t s) {
   if (!qs || !d || !tokens || !out || n_tokens < 0 || vocab <= 0 || dim <= 0 || dim % QK) return kBadArgument;
   if (n_tokens == 0) return kOk;
-  embed_q8_0_kernel<<<n_tokens, 256, 0, s>>>(qs, d, tokens, vocab, dim, out);
-  return launched();
+  return launch_pdl(embed_q8_0_kernel, dim3(n_tokens), dim3(256), 0, s, qs, d, tokens, vocab, dim, out) == cudaSuccess
+             ? kOk
+             : kCudaError;
 }
 
 int rope_tensorops(float* x, int heads, int seq, int hd, int pos0, float theta, cudaStream_t s) {
