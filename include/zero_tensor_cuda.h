@@ -62,6 +62,10 @@ ZC_API int32_t zcu_gemv_q4_0(const uint8_t* qs, const uint16_t* d, const float* 
  * k_cols must be a multiple of 32; the fp16 copy of X lives in the library's per-(device, stream) workspace. */
 ZC_API int32_t zcu_gemm_q8_0(const int8_t* qs, const uint16_t* d, const float* x, float* y, size_t m, size_t n_rows,
                              size_t k_cols, int32_t accumulate, void* stream);
+/* The same for Q4_0 weights (SoA nibbles [n_rows][k_cols/32][16] + fp16 scales, zcu_q4_0_repack): the batched
+ * MatVecMulQ4_0 / MatVecAddQ4_0 (QuantizedKernels.cs:231-267,313-349) on the tensor cores; k_cols % 32 == 0. */
+ZC_API int32_t zcu_gemm_q4_0(const uint8_t* qs, const uint16_t* d, const float* x, float* y, size_t m, size_t n_rows,
+                             size_t k_cols, int32_t accumulate, void* stream);
 
 /* Synchronises the device and returns its status word: 0 = healthy, otherwise the code a kernel recorded
  * when one of its bounded waits expired (the kernel then stopped, drained and released its resources).
@@ -214,6 +218,35 @@ ZC_API int32_t zcu_engine_free_pages(void* engine);
 ZC_API int32_t zcu_engine_page_table(void* engine, int32_t seq_id, int32_t* out, int32_t cap);
 ZC_API int32_t zcu_engine_get_kv(void* engine, int32_t seq_id, int32_t layer, int32_t token, int32_t want_value,
                                  float* out);
+
+/* ---------------------------------------------------------------------------------------------------------
+ * Sparse mixture-of-experts FFN layer: SparseMoeLayer.Forward (ZeroLlm/src/ZeroLlm.Core/Layers/SparseMoeLayer.cs:
+ * 32-125) for T tokens at once -- router logits (given, or an fp32 router [n_experts][dim] . xnorm), top-k
+ * selection (ties keep the lowest expert index), softmax over the k selected, each selected expert's SwiGLU FFN
+ * with Q4_0 (qtype 4) or Q8_0 (qtype 8) weights on the tensor cores, and residual += weight * expert output in
+ * selection order.  Expert parallelism: ep_size ranks (one process per GPU, same calls on every rank), expert e
+ * on rank e / (n_experts / ep_size); every rank passes its own tokens, rows travel to the experts' ranks and back
+ * by NCCL all-to-all.  dim and ffn must be multiples of 256.  No shared experts.
+ * ------------------------------------------------------------------------------------------------------- */
+typedef struct {
+  int32_t n_experts, top_k, dim, ffn; /* ExpertCount, ExpertUsedCount, EmbeddingDim, FeedForwardDim */
+  int32_t qtype;                      /* 4 = Q4_0 experts, 8 = Q8_0 experts */
+  int32_t max_tokens;                 /* largest T of a forward call on this rank */
+} zcu_moe_config;
+ZC_API int32_t zcu_moe_create(const zcu_moe_config* cfg, int32_t ep_size, int32_t ep_rank, const uint8_t* nccl_id,
+                              void* stream, void** moe);
+ZC_API int32_t zcu_moe_destroy(void* moe);
+ZC_API const char* zcu_moe_last_error(void* moe);
+/* Expert `expert`'s gate (which 0, [ffn][dim]), up (1, [ffn][dim]) or down (2, [dim][ffn]) projection as the
+ * reference's packed blocks (host or device memory); ranks that do not own the expert ignore it. */
+ZC_API int32_t zcu_moe_set_expert(void* moe, int32_t expert, int32_t which, const void* src, size_t bytes);
+/* Optional fp32 router weights [n_experts][dim] (host or device); without them forward needs router_logits. */
+ZC_API int32_t zcu_moe_set_router(void* moe, const float* w, size_t bytes);
+/* xnorm [T][dim], router_logits [T][n_experts] (or NULL: router weights, else uniform) and residual [T][dim]
+ * (updated in place) are device memory; sel_idx / sel_w [T][top_k] (host or device, may be NULL) receive the
+ * routing.  Synchronous. */
+ZC_API int32_t zcu_moe_forward(void* moe, const float* xnorm, const float* router_logits, float* residual, int32_t T,
+                               int32_t* sel_idx, float* sel_w);
 
 #ifdef __cplusplus
 }

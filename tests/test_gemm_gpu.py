@@ -20,8 +20,9 @@ def _lib():
 
 
 def _run(qw, x, y, accumulate=False):
-    rc = _lib().zcu_gemm_q8_0(qw.qs.data_ptr(), qw.d.data_ptr(), x.data_ptr(), y.data_ptr(), x.shape[0], qw.rows,
-                              qw.cols, int(accumulate), torch.cuda.current_stream().cuda_stream)
+    fn = _lib().zcu_gemm_q8_0 if qw.qtype == 8 else _lib().zcu_gemm_q4_0
+    rc = fn(qw.qs.data_ptr(), qw.d.data_ptr(), x.data_ptr(), y.data_ptr(), x.shape[0], qw.rows, qw.cols,
+            int(accumulate), torch.cuda.current_stream().cuda_stream)
     assert rc == 0
     assert _lib().zcu_device_status(1) == 0  # no bounded wait expired
 
@@ -81,3 +82,26 @@ def test_gemm_matches_fp16_rounded_reference_tightly():
     y = torch.empty((m, n), device="cuda")
     _run(qw, torch.from_numpy(x).cuda(), y)
     assert rel_err(y.cpu().numpy(), ref) <= 1e-5
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 128, 64), (64, 256, 768), (130, 1000, 4096), (64, 28672, 4096),
+                                   (64, 4096, 14336), (9, 2304, 96)])
+def test_gemm_q4_0_matches_oracle(m, n, k):
+    """Q4_0 weights (the MoE experts' format) on the tensor cores vs the oracle's token-parallel MatVecMulQ4_0."""
+    from zeroplatform_b200.ops import QuantizedWeight
+    rng = np.random.default_rng(m * 13 + n + k)
+    w = rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02)
+    x = rng.standard_normal((m, k), dtype=np.float32)
+    blocks = O.quantize_q4_0(w)
+    ref = O.matmul(4, blocks, x, n, k)
+    qw = QuantizedWeight.upload(4, blocks, n, k)
+    xd = torch.from_numpy(x).cuda()
+    y = torch.full((m, n), float("nan"), device="cuda")
+    _run(qw, xd, y)
+    err = rel_err(y.cpu().numpy(), ref)
+    print(f"gemm q4_0 {m}x{n}x{k}: max-rel err {err:.3e}")
+    assert err <= TOL
+    y0 = rng.standard_normal((m, n), dtype=np.float32)
+    yt = torch.from_numpy(y0.copy()).cuda()
+    _run(qw, xd, yt, accumulate=True)
+    assert rel_err(yt.cpu().numpy() - y0, ref) <= TOL

@@ -45,6 +45,7 @@ SIGNATURES = {
     "zcu_gemv_q8_0": (i32, [vp, vp, vp, vp, sz, sz, i32, vp]),
     "zcu_gemv_q4_0": (i32, [vp, vp, vp, vp, sz, sz, i32, vp]),
     "zcu_gemm_q8_0": (i32, [vp, vp, vp, vp, sz, sz, sz, i32, vp]),
+    "zcu_gemm_q4_0": (i32, [vp, vp, vp, vp, sz, sz, sz, i32, vp]),
     "zcu_device_status": (i32, [i32]),
     "zcu_paged_attention": (i32, [vp, vp, vp, i32, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, i64, i64, i64,
                                   f32, i32, vp]),
@@ -98,6 +99,22 @@ class TpShard(C.Structure):
 SIGNATURES.update({
     "zcu_tp_plan": (i32, [C.POINTER(EngineConfig), i32, i32, C.POINTER(TpShard)]),
     "zcu_engine_create_tp": (i32, [C.POINTER(EngineConfig), i32, i32, vp, vp, C.POINTER(vp)]),
+})
+
+
+class MoeConfig(C.Structure):
+    """zcu_moe_config (include/zero_tensor_cuda.h)."""
+
+    _fields_ = [(n, C.c_int32) for n in ("n_experts", "top_k", "dim", "ffn", "qtype", "max_tokens")]
+
+
+SIGNATURES.update({
+    "zcu_moe_create": (i32, [C.POINTER(MoeConfig), i32, i32, vp, vp, C.POINTER(vp)]),
+    "zcu_moe_destroy": (i32, [vp]),
+    "zcu_moe_last_error": (C.c_char_p, [vp]),
+    "zcu_moe_set_expert": (i32, [vp, i32, i32, vp, sz]),
+    "zcu_moe_set_router": (i32, [vp, vp, sz]),
+    "zcu_moe_forward": (i32, [vp, vp, vp, vp, i32, vp, vp]),
 })
 
 

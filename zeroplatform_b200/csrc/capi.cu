@@ -597,6 +597,20 @@ int32_t zcu_gemm_q8_0(const int8_t* qs, const uint16_t* d, const float* x, float
   return gemm_q8_0_tc(qs, d, x, y, (int)m, (int)n_rows, (int)k_cols, accumulate, ws, bytes, status, s);
 }
 
+int32_t zcu_gemm_q4_0(const uint8_t* qs, const uint16_t* d, const float* x, float* y, size_t m, size_t n_rows,
+                      size_t k_cols, int32_t accumulate, void* stream) {
+  t_last_error.clear();
+  if (m > 0x7fffffff || n_rows > 0x7fffffff || k_cols > 0x7fffffff) return fail(kUnsupported, "dimension too large");
+  if (m == 0 || n_rows == 0) return kOk;
+  cudaStream_t s = as_stream(stream);
+  void* ws;
+  int* status;
+  const size_t bytes = gemm_q8_0_workspace_bytes((int)m, (int)n_rows, (int)k_cols);
+  ZC_RC(stream_scratch(s, 2, bytes, false, &ws));
+  ZC_RC(device_status_ptr(&status));
+  return gemm_q4_0_tc(qs, d, x, y, (int)m, (int)n_rows, (int)k_cols, accumulate, ws, bytes, status, s);
+}
+
 int32_t zcu_device_status(int32_t reset) {
   int* p = nullptr;
   if (device_status_ptr(&p) != kOk) return kCudaError;

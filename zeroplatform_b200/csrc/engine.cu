@@ -618,9 +618,7 @@ int32_t zcu_engine_create_tp(const zcu_engine_config* cfg, int32_t tp_size, int3
     const int shapes[5][2] = {{E->qkv_dim, c.dim}, {c.dim, E->q_dim}, {2 * E->ffn, c.dim}, {c.dim, E->ffn},
                               {E->vocab, c.dim}};
     size_t ws = 0;
-    for (auto& sh2 : shapes)
-      for (int rows_m : {R, c.max_batch, kGemmMinRows, std::min(R, 128)})
-        if (rows_m >= kGemmMinRows) ws = std::max(ws, gemm_q8_0_workspace_bytes(rows_m, sh2[0], sh2[1]));
+    for (auto& sh2 : shapes) ws = std::max(ws, gemm_workspace_max(R, sh2[0], sh2[1]));
     E->gemm_ws_bytes = std::max<size_t>(ws, 256);
   }
   step(dalloc(E, reinterpret_cast<uint8_t**>(&E->gemm_ws), E->gemm_ws_bytes));

@@ -1,7 +1,7 @@
 // gemm_tc.cu -- batched / prefill quantized GEMM on the 5th-generation tensor cores (tcgen05, sm_100a).
 //
 // Y[m, n] (=|+=) sum_k X[m, k] * dequant(W)[n, k] for X fp32 [M][K], W Q8_0 (SoA: int8 [N][K] + fp16
-// scales [N][K/32]), Y fp32 [M][N].  This is LlmEngine.PrefillPrompt's token-parallel loop of
+// scales [N][K/32]) or Q4_0 (SoA: nibbles [N][K/32][16] + fp16 scales), Y fp32 [M][N].  This is LlmEngine.PrefillPrompt's token-parallel loop of
 // QuantizedKernels.MatVecMulQ8_0 / MatVecAddQ8_0 (ZeroLlm/src/ZeroLlm.Core/Engine/LlmEngine.cs:208-304,
 // Quantization/QuantizedKernels.cs:190-308) executed as one contraction.
 //
@@ -44,9 +44,11 @@ constexpr int EPI_WARP0 = 4 + DQ_WARPS;       // first of the four epilogue warp
 constexpr int GEMM_THREADS = (EPI_WARP0 + 4) * 32;
 constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KB of fp16 A per stage
 constexpr int W_SUB = 4;                    // k-stages per int8 weight tile (one TMA box of 256 bytes x 128 rows)
-constexpr int W_TILE_BYTES = BM * BK * W_SUB;     // 32 KB of int8 W per weight stage
-constexpr int S_TILE_BYTES = BM * BK * W_SUB / QK * 2;  // + 2 KB of its fp16 block scales (8 per row)
-constexpr int W_STAGE_BYTES = W_TILE_BYTES + S_TILE_BYTES;
+constexpr int S_TILE_BYTES = BM * BK * W_SUB / QK * 2;  // fp16 block scales of a weight tile (8 per row)
+// Quantized bytes of a weight tile [128 rows x 256 k]: 32 KB of int8 (Q8_0) or 16 KB of nibbles (Q4_0).
+__host__ __device__ constexpr int w_tile_bytes(int qt) { return qt == 8 ? BM * BK * W_SUB : BM * BK * W_SUB / 2; }
+__host__ __device__ constexpr int w_stage_bytes(int qt) { return w_tile_bytes(qt) + S_TILE_BYTES; }
+__host__ __device__ constexpr int w_row_bytes(int qt) { return w_tile_bytes(qt) / BM; }  // 256 or 128
 constexpr int MAX_SPLITS = 8;               // split-K ranges per output tile at most
 
 struct GemmParams {
@@ -141,9 +143,39 @@ __device__ __forceinline__ void dequant16(int4 w, __half2 d2, uint4& lo, uint4& 
   hi = make_uint4(out[4], out[5], out[6], out[7]);
 }
 
+// Four nibbles (one per byte, 0..15) -> two half2 of (u - 8) * d.
+__device__ __forceinline__ void nib4(uint32_t u, __half2 d2, uint32_t& p0, uint32_t& p1) {
+  const __half2 bias = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));  // 1024 + 8
+  const uint32_t a = __byte_perm(u, 0x64646464u, 0x5140);
+  const uint32_t b = __byte_perm(u, 0x64646464u, 0x7362);
+  __half2 h0 = __hmul2_rn(__hsub2(*reinterpret_cast<const __half2*>(&a), bias), d2);  // exact u - 8, then * d
+  __half2 h1 = __hmul2_rn(__hsub2(*reinterpret_cast<const __half2*>(&b), bias), d2);
+  p0 = *reinterpret_cast<uint32_t*>(&h0);
+  p1 = *reinterpret_cast<uint32_t*>(&h1);
+}
+
+// One Q4_0 block (16 bytes: byte j = value j | value j+16 << 4) times its scale -> 32 fp16 values as four
+// 16-byte chunks (values 0-7, 8-15, 16-23, 24-31).
+__device__ __forceinline__ void dequant32_q4(int4 w, __half2 d2, uint4 (&c)[4]) {
+  const uint32_t m = 0x0F0F0F0Fu;
+  const uint32_t wv[4] = {(uint32_t)w.x, (uint32_t)w.y, (uint32_t)w.z, (uint32_t)w.w};
+  uint32_t o[16];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    nib4(wv[j] & m, d2, o[2 * j], o[2 * j + 1]);             // values 4j .. 4j+3
+    nib4((wv[j] >> 4) & m, d2, o[8 + 2 * j], o[8 + 2 * j + 1]);  // values 16+4j .. 16+4j+3
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) c[q] = make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+}
+
+// QT = 8: Q8_0 weights (int8 tiles); QT = 4: Q4_0 weights (nibble tiles, one 32-value block per dequant item).
+template <int QT>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_q8_0_tc_kernel(const __grid_constant__ CUtensorMap x_map, const __grid_constant__ CUtensorMap w_map,
                         const __grid_constant__ CUtensorMap s_map, GemmParams p) {
+  constexpr int W_STAGE_BYTES = w_stage_bytes(QT);
+  constexpr int W_TILE_BYTES = w_tile_bytes(QT);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int bn = p.bn;
@@ -216,7 +248,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         for (int kb = unit_kb0(u); kb < unit_kb1(u); kb += W_SUB) {  // one box covers W_SUB k-stages
           if (!mbar_wait(smem_u32(&w_empty[s]), ph ^ 1, abort_flag, p.status, 1)) break;
           mbar_arrive_tx(smem_u32(&w_full[s]), (uint32_t)(p.scale_tma ? W_STAGE_BYTES : W_TILE_BYTES));
-          tma_load_2d(smem_u32(w_st + s * W_STAGE_BYTES), &w_map, kb * BK, row0, smem_u32(&w_full[s]));
+          tma_load_2d(smem_u32(w_st + s * W_STAGE_BYTES), &w_map, QT == 8 ? kb * BK : kb * BK / 2, row0,
+                      smem_u32(&w_full[s]));
           if (p.scale_tma)  // the 8 scales per row of these 256 k (x = kb * 2, a multiple of 8 scales = 16 bytes)
             tma_load_2d(smem_u32(w_st + s * W_STAGE_BYTES + W_TILE_BYTES), &s_map, kb * (BK / QK), row0,
                         smem_u32(&w_full[s]));
@@ -303,20 +336,25 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       for (int kb = kb0; kb < kb1 && !stop; ++kb) {
         const int sub = (kb - kb0) % W_SUB;  // which 64-byte column block of the current weight tile
         if (sub == 0 && !mbar_wait(smem_u32(&w_full[ws]), wph, abort_flag, p.status, 4)) break;
-        int4 cw[DQ_ITEMS];
-        __half2 cd[DQ_ITEMS];
-        const uint8_t* wsrc = w_st + ws * W_STAGE_BYTES + sub * BK;
+        // Q8_0: DQ_ITEMS items of 16 values (row r, 16-value chunk c); Q4_0: one item of one 32-value block
+        // (row r, block b of the stage) per thread.
+        constexpr int ITEMS = QT == 8 ? DQ_ITEMS : BM * BK / 32 / DQ_THREADS;
+        int4 cw[ITEMS];
+        __half2 cd[ITEMS];
+        const uint8_t* wsrc = w_st + ws * W_STAGE_BYTES + sub * (QT == 8 ? BK : BK / 2);
         const uint16_t* ssrc = reinterpret_cast<const uint16_t*>(w_st + ws * W_STAGE_BYTES + W_TILE_BYTES);
 #pragma unroll
-        for (int j = 0; j < DQ_ITEMS; ++j) {
+        for (int j = 0; j < ITEMS; ++j) {
           const int item = tid + DQ_THREADS * j;
-          const int r = item >> 2, c = item & 3;
-          cw[j] = *reinterpret_cast<const int4*>(wsrc + r * (BK * W_SUB) + c * 16);
+          const int r = QT == 8 ? item >> 2 : item >> 1;
+          const int c = QT == 8 ? item & 3 : item & 1;  // 16-value chunk (Q8_0) or block (Q4_0) of the stage
+          cw[j] = *reinterpret_cast<const int4*>(wsrc + r * w_row_bytes(QT) + c * 16);
+          const int blk = QT == 8 ? c >> 1 : c;  // block of this k-stage (two per stage)
           __half h;
           if (p.scale_tma) {
-            h = __ushort_as_half(ssrc[r * (W_SUB * BK / QK) + sub * (BK / QK) + (c >> 1)]);
+            h = __ushort_as_half(ssrc[r * (W_SUB * BK / QK) + sub * (BK / QK) + blk]);
           } else {  // K not a multiple of 256: scales straight from global memory
-            const int row = row0 + r, k = kb * BK + c * 16;
+            const int row = row0 + r, k = kb * BK + blk * QK;
             h = __ushort_as_half((row < p.N && k < p.K) ? __ldg(p.d + (size_t)row * (p.K / QK) + (k >> 5))
                                                         : (unsigned short)0);
           }
@@ -335,15 +373,24 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
         uint8_t* a = a_st + as * A_STAGE_BYTES;
 #pragma unroll
-        for (int j = 0; j < DQ_ITEMS; ++j) {
+        for (int j = 0; j < ITEMS; ++j) {
           const int item = tid + DQ_THREADS * j;
-          const int r = item >> 2, c = item & 3;
-          uint4 lo, hi;
-          dequant16(cw[j], cd[j], lo, hi);
+          const int r = QT == 8 ? item >> 2 : item >> 1;
           // row r of the tile: 128-byte line in its 1024-byte group, 16-byte chunks XOR-swizzled by r % 8
           uint8_t* line = a + (r >> 3) * 1024 + (r & 7) * 128;
-          *reinterpret_cast<uint4*>(line + (((2 * c) ^ (r & 7)) << 4)) = lo;
-          *reinterpret_cast<uint4*>(line + (((2 * c + 1) ^ (r & 7)) << 4)) = hi;
+          if (QT == 8) {
+            const int c = item & 3;
+            uint4 lo, hi;
+            dequant16(cw[j], cd[j], lo, hi);
+            *reinterpret_cast<uint4*>(line + (((2 * c) ^ (r & 7)) << 4)) = lo;
+            *reinterpret_cast<uint4*>(line + (((2 * c + 1) ^ (r & 7)) << 4)) = hi;
+          } else {
+            const int b = item & 1;
+            uint4 q4[4];
+            dequant32_q4(cw[j], cd[j], q4);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) *reinterpret_cast<uint4*>(line + (((4 * b + q) ^ (r & 7)) << 4)) = q4[q];
+          }
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         mbar_arrive(smem_u32(&ab_full[as]));
@@ -462,9 +509,10 @@ constexpr int SMEM_FIXED = 1024 + 512;  // alignment slack + barriers, TMEM slot
 // Ring depths from the shared-memory budget: the A/B ring (fp16 A + fp16 X per stage) as deep as fits after
 // the int8 weight ring, at most MAX_STAGES.  Deep rings keep several stages in flight across the
 // dequantize -> MMA -> commit round trip.
-static void ring_depths(int bn, int& ab, int& w) {
+static void ring_depths(int qt, int bn, int& ab, int& w) {
   w = bn <= 64 ? 3 : 2;
-  ab = (SMEM_LIMIT - SMEM_FIXED - w * W_STAGE_BYTES) / (A_STAGE_BYTES + bn * BK * 2);
+  if (qt == 4) ++w;  // nibble tiles are half the size
+  ab = (SMEM_LIMIT - SMEM_FIXED - w * w_stage_bytes(qt)) / (A_STAGE_BYTES + bn * BK * 2);
   if (ab > MAX_STAGES) ab = MAX_STAGES;
 }
 
@@ -472,7 +520,7 @@ static void ring_depths(int bn, int& ab, int& w) {
 // costing (its k-stages) x (bn + 64) (the 64 stands for the A-operand traffic every stage pays whatever bn
 // is), plus a small charge per extra split for the partial-sum traffic.  Split-K only when M <= 128 (small
 // decode batches), where the partials are small.
-static GemmConfig choose_config(int m, int n, int k) {
+static GemmConfig choose_config(int m, int n, int k, int qt = 8) {
   const int sms = num_sms();
   const int nk = (k + BK - 1) / BK;
   GemmConfig best{};
@@ -493,7 +541,7 @@ static GemmConfig choose_config(int m, int n, int k) {
       if (cost < best_cost - 1e-9) {
         best_cost = cost;
         int ab, w;
-        ring_depths(bn, ab, w);
+        ring_depths(qt, bn, ab, w);
         best = GemmConfig{bn, real_sp, kb_per, ab, w, tok_tiles, tiles};
       }
     }
@@ -514,12 +562,20 @@ size_t gemm_q8_0_workspace_bytes(int m, int n, int k) {
   return b;
 }
 
-// Core launcher on fp16 activations x16 [m][k] (16-byte aligned rows).
-static int launch_gemm(const int8_t* qs, const uint16_t* d, const __half* x16, float* y, int m, int n, int k,
+size_t gemm_workspace_max(int m_max, int n, int k) {
+  // split-K is chosen only up to M = 128 (and the partials grow with M there), beyond it the size grows with M
+  size_t b = gemm_q8_0_workspace_bytes(std::max(m_max, 1), n, k);
+  for (int m = 1; m <= std::min(m_max, 129); ++m) b = std::max(b, gemm_q8_0_workspace_bytes(m, n, k));
+  return b;
+}
+
+// Core launcher on fp16 activations x16 [m][k] (16-byte aligned rows); QT = 8 (Q8_0) or 4 (Q4_0) weights.
+template <int QT>
+static int launch_gemm(const void* qs, const uint16_t* d, const __half* x16, float* y, int m, int n, int k,
                        int accumulate, char* ws, int* status, cudaStream_t s) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return kCudaError;
-  const GemmConfig c = choose_config(m, n, k);
+  const GemmConfig c = choose_config(m, n, k, QT);
   float* part = reinterpret_cast<float*>(ws + align256((size_t)m * k * 2));
   CUtensorMap xmap, wmap;
   {
@@ -533,11 +589,12 @@ static int launch_gemm(const int8_t* qs, const uint16_t* d, const __half* x16, f
       return kCudaError;
   }
   {
-    cuuint64_t gdim[2] = {(cuuint64_t)k, (cuuint64_t)n};
-    cuuint64_t gstride[1] = {(cuuint64_t)k};
-    cuuint32_t box[2] = {(cuuint32_t)(BK * W_SUB), (cuuint32_t)BM};
+    const cuuint64_t row_bytes = QT == 8 ? (cuuint64_t)k : (cuuint64_t)k / 2;
+    cuuint64_t gdim[2] = {row_bytes, (cuuint64_t)n};
+    cuuint64_t gstride[1] = {row_bytes};
+    cuuint32_t box[2] = {(cuuint32_t)w_row_bytes(QT), (cuuint32_t)BM};
     cuuint32_t estride[2] = {1, 1};
-    if (enc(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(qs), gdim, gstride, box, estride,
+    if (enc(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(qs), gdim, gstride, box, estride,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return kCudaError;
@@ -574,11 +631,11 @@ static int launch_gemm(const int8_t* qs, const uint16_t* d, const __half* x16, f
   p.n_tiles = c.n_tiles;
   p.splits = c.splits;
   p.kb_per_split = c.kb_per;
-  const int smem = SMEM_FIXED + c.ab_stages * (A_STAGE_BYTES + c.bn * BK * 2) + c.w_stages * W_STAGE_BYTES;
-  if (cudaFuncSetAttribute(gemm_q8_0_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+  const int smem = SMEM_FIXED + c.ab_stages * (A_STAGE_BYTES + c.bn * BK * 2) + c.w_stages * w_stage_bytes(QT);
+  if (cudaFuncSetAttribute(gemm_q8_0_tc_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return kCudaError;
   const int grid = std::min(c.n_tiles * c.splits, num_sms());
-  if (launch_pdl(gemm_q8_0_tc_kernel, dim3(grid), dim3(GEMM_THREADS), (size_t)smem, s, xmap, wmap, smap, p) !=
+  if (launch_pdl(gemm_q8_0_tc_kernel<QT>, dim3(grid), dim3(GEMM_THREADS), (size_t)smem, s, xmap, wmap, smap, p) !=
       cudaSuccess)
     return kCudaError;
   if (c.splits > 1) {
@@ -611,14 +668,35 @@ int gemm_q8_0_tc(const int8_t* qs, const uint16_t* d, const float* x, float* y, 
   if (launch_pdl(f32_to_f16_kernel, dim3((unsigned)std::min<size_t>((nx / 4 + 255) / 256, 148 * 8)), dim3(256), 0, s,
                  x, x16, nx) != cudaSuccess)
     return kCudaError;
-  return launch_gemm(qs, d, x16, y, m, n, k, accumulate, ws, status, s);
+  return launch_gemm<8>(qs, d, x16, y, m, n, k, accumulate, ws, status, s);
 }
 
 int gemm_q8_0_tc_h(const int8_t* qs, const uint16_t* d, const __half* x16, float* y, int m, int n, int k,
                    int accumulate, void* workspace, size_t workspace_bytes, int* status, cudaStream_t s) {
   const int rc = check_gemm_args(qs, d, x16, y, m, n, k, workspace, workspace_bytes, status);
   if (rc != kOk) return rc;
-  return launch_gemm(qs, d, x16, y, m, n, k, accumulate, static_cast<char*>(workspace), status, s);
+  return launch_gemm<8>(qs, d, x16, y, m, n, k, accumulate, static_cast<char*>(workspace), status, s);
+}
+
+int gemm_q4_0_tc(const uint8_t* qs, const uint16_t* d, const float* x, float* y, int m, int n, int k, int accumulate,
+                 void* workspace, size_t workspace_bytes, int* status, cudaStream_t s) {
+  const int rc = check_gemm_args(qs, d, x, y, m, n, k, workspace, workspace_bytes, status);
+  if (rc != kOk) return rc;
+  if (k % 32) return kUnsupported;  // nibble rows (K / 2 bytes) must be 16-byte multiples
+  char* ws = static_cast<char*>(workspace);
+  __half* x16 = reinterpret_cast<__half*>(ws);
+  const size_t nx = (size_t)m * k;
+  if (launch_pdl(f32_to_f16_kernel, dim3((unsigned)std::min<size_t>((nx / 4 + 255) / 256, 148 * 8)), dim3(256), 0, s,
+                 x, x16, nx) != cudaSuccess)
+    return kCudaError;
+  return launch_gemm<4>(qs, d, x16, y, m, n, k, accumulate, ws, status, s);
+}
+
+int gemm_q4_0_tc_h(const uint8_t* qs, const uint16_t* d, const __half* x16, float* y, int m, int n, int k,
+                   int accumulate, void* workspace, size_t workspace_bytes, int* status, cudaStream_t s) {
+  const int rc = check_gemm_args(qs, d, x16, y, m, n, k, workspace, workspace_bytes, status);
+  if (rc != kOk) return rc;
+  return launch_gemm<4>(qs, d, x16, y, m, n, k, accumulate, static_cast<char*>(workspace), status, s);
 }
 
 }  // namespace zc

@@ -29,10 +29,16 @@ int gemv_q8_0_swiglu(const int8_t* qs, const uint16_t* d, const float* gate_up, 
 
 // ---- prefill / batched GEMM on tcgen05 (gemm_tc.cu): Y[m][n] (=|+=) X[m][:] . dequant(W)[n][:] ----
 size_t gemm_q8_0_workspace_bytes(int m, int n, int k);  // fp16 activations + split-K partials
+size_t gemm_workspace_max(int m_max, int n, int k);       // the largest of the above over 1 <= m <= m_max
 int gemm_q8_0_tc(const int8_t* qs, const uint16_t* d, const float* x, float* y, int m, int n, int k, int accumulate,
                  void* workspace, size_t workspace_bytes, int* status, cudaStream_t s);
 // The same on fp16 activations [m][k] (a producer that writes fp16 saves the conversion kernel).
 int gemm_q8_0_tc_h(const int8_t* qs, const uint16_t* d, const __half* x16, float* y, int m, int n, int k,
+                   int accumulate, void* workspace, size_t workspace_bytes, int* status, cudaStream_t s);
+// Q4_0 weights (SoA nibbles [N][K/32][16] + fp16 scales), same workspace size rule.
+int gemm_q4_0_tc(const uint8_t* qs, const uint16_t* d, const float* x, float* y, int m, int n, int k, int accumulate,
+                 void* workspace, size_t workspace_bytes, int* status, cudaStream_t s);
+int gemm_q4_0_tc_h(const uint8_t* qs, const uint16_t* d, const __half* x16, float* y, int m, int n, int k,
                    int accumulate, void* workspace, size_t workspace_bytes, int* status, cudaStream_t s);
 
 // ---- paged decode attention (attention.cu) ----
