@@ -358,6 +358,68 @@ def decode_7b_leg(dev, rank, world, batch=32, n_ctx=2048, n_new=128, n_warm=3, l
                       "max over ranks"}
 
 
+def moe_leg(dev, rank, world, iters=10, tokens=256, n_experts=8, top_k=2, dim=4096, ffn=14336):
+    """MoE FFN layer, 8 experts x SwiGLU FFN 14336 at d_model 4096, Q4_0 (group 32, fp16 scales)
+    from N(0,0.02); 256 tokens of N(0,1) activations, router logits N(0,1), softmax over the top 2.  Expert
+    parallel over the `world` GPUs of this job: each rank holds n_experts / world experts and 256 / world of the
+    tokens; rows travel to the experts' ranks and back by NCCL all-to-all.  Timing: device events around the
+    layer's forward (routing, dispatch, experts, return, combine), max over ranks."""
+    import torch
+    import torch.distributed as dist
+    from zeroplatform_b200.engine import nccl_unique_id
+    from zeroplatform_b200.moe import SparseMoeLayer
+    from zeroplatform_b200.ops import quantize
+    uid = None
+    if world > 1:
+        t = torch.zeros(128, dtype=torch.uint8, device=dev)
+        if rank == 0:
+            t.copy_(torch.frombuffer(bytearray(nccl_unique_id()), dtype=torch.uint8))
+        dist.broadcast(t, 0)
+        uid = bytes(t.cpu().numpy().tobytes())
+    t_local = tokens // world
+    s = torch.cuda.current_stream()
+    m = SparseMoeLayer(n_experts, top_k, dim, ffn, qtype=4, max_tokens=t_local, ep_size=world, ep_rank=rank,
+                       nccl_id=uid, stream=s.cuda_stream)
+    g = torch.Generator(device=dev)
+    per = n_experts // world
+    for e in range(rank * per, (rank + 1) * per):  # other ranks' experts are ignored by set_expert anyway
+        for j, (name, (r, c)) in enumerate((("gate", (ffn, dim)), ("up", (ffn, dim)), ("down", (dim, ffn)))):
+            g.manual_seed(7000 + 10 * e + j)
+            m.set_expert(e, name, quantize(4, torch.randn((r, c), generator=g, device=dev) * 0.02))
+    g.manual_seed(99 + rank)
+    x = torch.randn((t_local, dim), generator=g, device=dev)
+    logits = torch.randn((t_local, n_experts), generator=g, device=dev)
+    res = torch.zeros((t_local, dim), device=dev)
+    for _ in range(3):
+        m.forward(x, res, logits)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(iters):
+        m.forward(x, res, logits)
+    e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / iters
+    if world > 1:
+        tt = torch.tensor([ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    m.close()
+    w_bytes = n_experts * 3 * dim * ffn * 18 // 32  # Q4_0 weight bytes of all experts (each rank reads its share)
+    peak, src = _peaks()
+    gbs_rank = (w_bytes / world) / (ms * 1e-3) / 1e9
+    flops = 2.0 * tokens * top_k * 3 * dim * ffn
+    return {"ms": round(ms, 4), "tokens_per_s": round(tokens / (ms * 1e-3), 1), "n_gpus": world,
+            "parallelism": f"ep{world}", "tokens": tokens, "experts": n_experts, "top_k": top_k, "dim": dim,
+            "ffn": ffn, "weight_bytes": w_bytes, "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
+            "roofline": {"bound": "hbm", "achieved": round(gbs_rank, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs_rank / peak, 3), "peak_source": src,
+                         "what": "Q4_0 expert weight bytes one rank streams per forward / device time"},
+            "data": "synthetic: experts N(0,0.02) -> Q4_0 on device, x and router logits N(0,1)"}
+
+
 # ----------------------------------------------------------------------------------------------------------
 # GPU arm
 # ----------------------------------------------------------------------------------------------------------
@@ -513,6 +575,10 @@ def run_ours(args):
                                                               n_new=args.new_tokens)
         except Exception as ex:
             extra[f"decode_7b_b32_tp{world}"] = {"error": str(ex)[:300]}
+        try:
+            extra[f"moe_8x14336_top2_ep{world}"] = moe_leg(dev, rank, world)
+        except Exception as ex:
+            extra[f"moe_8x14336_top2_ep{world}"] = {"error": str(ex)[:300]}
     cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu) else None
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -536,8 +602,8 @@ def run_ours(args):
 
 
 def run_leg(args):
-    """`--leg decode_7b`: only the 7B-shaped tensor-parallel decode, printed as its own JSON line (rank 0).
-    --layers / --new-tokens shrink it for profiler captures."""
+    """`--leg decode_7b` / `--leg moe`: one extra leg alone, printed as its own JSON line (rank 0).
+    --layers / --new-tokens shrink the decode leg for profiler captures."""
     import torch
     import torch.distributed as dist
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -548,9 +614,14 @@ def run_leg(args):
     if world > 1:
         import datetime
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
-    res = decode_7b_leg(dev, rank, world, n_new=args.new_tokens, layers=args.layers)
+    if args.leg == "moe":
+        res = moe_leg(dev, rank, world)
+        name = f"moe_8x14336_top2_ep{world}"
+    else:
+        res = decode_7b_leg(dev, rank, world, n_new=args.new_tokens, layers=args.layers)
+        name = f"decode_7b_b32_tp{world}"
     if rank == 0:
-        print(json.dumps({"leg": f"decode_7b_b32_tp{world}", **res}), flush=True)
+        print(json.dumps({"leg": name, **res}), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -558,8 +629,9 @@ def run_leg(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--leg", choices=["all", "decode_7b"], default="all",
-                    help="all: the headline and every extra leg; decode_7b: only the 7B tensor-parallel decode")
+    ap.add_argument("--leg", choices=["all", "decode_7b", "moe"], default="all",
+                    help="all: the headline and every extra leg; decode_7b: only the 7B tensor-parallel decode; "
+                         "moe: only the expert-parallel MoE layer")
     ap.add_argument("--layers", type=int, default=32, help="decode_7b: decoder layers (32 = the 7B shape)")
     ap.add_argument("--new-tokens", type=int, default=128, help="decode_7b: generated tokens per sequence")
     ap.add_argument("--gpus", type=int, default=1)
@@ -575,7 +647,7 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
-    elif args.leg == "decode_7b":
+    elif args.leg in ("decode_7b", "moe"):
         run_leg(args)
     else:
         run_ours(args)

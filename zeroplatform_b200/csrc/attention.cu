@@ -83,12 +83,13 @@ struct AttnDev {
   long long q_stride, out_stride, pt_stride;
   const int32_t* pt_rows;
   float scale_log2;
-  int out_half;  // out is __half instead of float
+  int out_half;  // out is __half hi / lo pairs (lo out_lo_offset elements after hi) instead of float
+  long long out_lo_offset;
 };
 
 __device__ __forceinline__ void store_out(const AttnDev& a, size_t i, float v) {
   if (a.out_half)
-    reinterpret_cast<__half*>(a.out)[i] = __float2half_rn(v);
+    store_hl(reinterpret_cast<__half*>(a.out) + i, (size_t)a.out_lo_offset, v);
   else
     a.out[i] = v;
 }
@@ -348,6 +349,7 @@ int paged_attention(const PagedAttnArgs& a, cudaStream_t s) {
   d.pt_stride = a.pt_stride >= 0 ? a.pt_stride : (long long)a.max_pages;
   d.pt_rows = a.pt_rows;
   d.out_half = a.out_half;
+  d.out_lo_offset = a.out_lo_offset;
   const int tiles = a.hq / gt;
   return a.kv_half ? launch_kv<__half>(d, a.hd, a.batch, tiles, gt, splits, s)
                    : launch_kv<float>(d, a.hd, a.batch, tiles, gt, splits, s);

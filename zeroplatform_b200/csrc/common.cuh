@@ -59,6 +59,17 @@ __device__ __forceinline__ float4 ld_f4(const float* p) { return __ldg(reinterpr
 
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 
+// v as the pair of fp16 values the tensor-core GEMM takes for an activation: hi = fp16(v) at p[0] and
+// lo = fp16(v - hi) at p[lo_off] (v - hi is exact in fp32; hi + lo holds v to about 2^-22 relative).
+__device__ __forceinline__ void store_hl(__half* p, size_t lo_off, float v) {
+  const __half h = __float2half_rn(v);
+  p[0] = h;
+  p[lo_off] = __float2half_rn(v - __half2float(h));
+}
+
+__device__ __forceinline__ void store_act(float* p, size_t, float v) { *p = v; }
+__device__ __forceinline__ void store_act(__half* p, size_t lo_off, float v) { store_hl(p, lo_off, v); }
+
 // Exact int8 -> fp32 for the four signed bytes of w: byte i becomes the float 2^23 + (q_i + 128),
 // from which one subtraction recovers q_i exactly (PRMT + FADD instead of a conversion unit op).
 __device__ __forceinline__ void s8x4_to_f32(uint32_t w, float& f0, float& f1, float& f2, float& f3) {

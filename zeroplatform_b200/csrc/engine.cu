@@ -38,6 +38,7 @@
 #include <vector>
 
 #include "../../include/zero_tensor_cuda.h"
+#include "allreduce_p2p.h"
 #include "collective.h"
 #include "common.cuh"
 #include "kernels.h"
@@ -107,6 +108,8 @@ struct Engine {
   int tp_rank = 0, tp_size = 1;
   zcu_tp_shard shard{};
   Comm* comm = nullptr;
+  P2pAllReduce* arp = nullptr;  // NVLink peer-memory all-reduce of the residual stream (tp > 1); NCCL otherwise
+  float* barrier_buf = nullptr;  // one float for rank_barrier
   int timeout_ms = 120000;
   int hq = 0, hkv = 0, ffn = 0, vocab = 0, vocab_chunk = 0;
   int hd = 0, q_dim = 0, kv_dim = 0, qkv_dim = 0;
@@ -130,7 +133,7 @@ struct Engine {
   int32_t* page_table = nullptr;  // [max_batch][max_pages_per_seq]
   int max_rows = 0;               // activation rows: max(max_batch, max_prefill_tokens)
   float *x = nullptr, *xn = nullptr, *qkv = nullptr, *attn = nullptr, *gu = nullptr, *sw = nullptr;
-  __half* xh = nullptr;  // fp16 activations feeding the tensor-core GEMM: [R][max(dim, q_dim, ffn)]
+  __half* xh = nullptr;  // fp16 activations feeding the tensor-core GEMM: [R][2 * max(dim, q_dim, ffn)] (hi | lo)
   float* logits = nullptr;      // [max_batch][vocab] (this rank's vocabulary slice)
   float* logits_all = nullptr;  // [tp][max_batch * vocab_chunk] gathered slices (tp > 1)
   int2* pairs = nullptr;        // [max_batch] arg-max of this rank's slice (tp > 1)
@@ -217,9 +220,10 @@ int linear(Engine* E, const DevW& w, const float* x, float* y, int rows, int acc
 }
 
 // The same on fp16 activations written by the previous kernel (rows >= kGemmMinRows: the tensor-core GEMM).
+// xh rows are [hi k | lo k] as the fp16 producers write them.
 int linear_h(Engine* E, const DevW& w, const __half* xh, float* y, int rows, int accumulate) {
-  return gemm_q8_0_tc_h(w.qs, w.d, xh, y, rows, w.n, w.k, accumulate, E->gemm_ws, E->gemm_ws_bytes, E->status,
-                        E->stream);
+  return gemm_q8_0_tc_h(w.qs, w.d, xh, xh + w.k, 2 * w.k, y, rows, w.n, w.k, accumulate, E->gemm_ws,
+                        E->gemm_ws_bytes, E->status, E->stream);
 }
 
 int attention(Engine* E, int layer, int T, const int32_t* ctx, bool half_out) {
@@ -246,7 +250,8 @@ int attention(Engine* E, int layer, int T, const int32_t* ctx, bool half_out) {
   a.kv_half = 1;
   a.max_ctx = E->cfg.max_pages_per_seq * E->cfg.page_size;
   a.q_stride = E->qkv_dim;
-  a.out_stride = E->q_dim;
+  a.out_stride = half_out ? 2 * E->q_dim : E->q_dim;  // fp16 rows are [hi q_dim | lo q_dim]
+  a.out_lo_offset = E->q_dim;
   a.workspace = E->attn_ws;
   a.counters = E->attn_ctr;
   a.splits = (T <= E->cfg.max_batch) ? E->attn_splits : 1;
@@ -257,7 +262,9 @@ int attention(Engine* E, int layer, int T, const int32_t* ctx, bool half_out) {
 inline int residual_mode(const Engine* E) { return E->tp_rank == 0 ? 1 : 0; }
 
 int allreduce_x(Engine* E, int T) {
-  return comm_allreduce_sum_f32(E->comm, E->x, (size_t)T * E->cfg.dim, E->stream, &E->err);
+  const size_t n = (size_t)T * E->cfg.dim;
+  if (E->arp && n <= arp_capacity(E->arp)) return arp_allreduce_sum(E->arp, E->x, n, E->stream);
+  return comm_allreduce_sum_f32(E->comm, E->x, n, E->stream, &E->err);
 }
 
 // The forward pass over T activation rows already embedded in E->x, with tokens' positions in E->pos and
@@ -358,6 +365,14 @@ int logits_to_host(Engine* E, int rows, float* host) {
 }
 
 int wait(Engine* E) { return comm_wait(E->comm, E->stream, E->timeout_ms, &E->err); }
+
+// Brings every rank's host thread to the same point (after per-rank host work such as graph capture, before
+// kernels that wait on their peers): a one-float NCCL all-reduce, waited for.
+int rank_barrier(Engine* E) {
+  if (E->tp_size == 1) return kOk;
+  E_RC(comm_allreduce_sum_f32(E->comm, E->barrier_buf, 1, E->stream, &E->err));
+  return wait(E);
+}
 
 // Pages covering positions [0, upto) of a sequence; allocates from the free stack and updates the device row.
 int ensure_pages(Engine* E, Seq& s, int upto) {
@@ -597,7 +612,7 @@ int32_t zcu_engine_create_tp(const zcu_engine_config* cfg, int32_t tp_size, int3
   step(dalloc(E, &E->attn, (size_t)R * E->q_dim));
   step(dalloc(E, &E->gu, (size_t)R * 2 * E->ffn));
   step(dalloc(E, &E->sw, (size_t)R * E->ffn));
-  step(dalloc(E, &E->xh, (size_t)R * std::max(std::max(c.dim, E->q_dim), E->ffn)));
+  step(dalloc(E, &E->xh, (size_t)R * 2 * std::max(std::max(c.dim, E->q_dim), E->ffn)));
   step(dalloc(E, &E->logits, (size_t)c.max_batch * E->vocab_chunk));
   if (tp_size > 1) {
     step(dalloc(E, &E->logits_all, (size_t)tp_size * c.max_batch * E->vocab_chunk));
@@ -631,6 +646,7 @@ int32_t zcu_engine_create_tp(const zcu_engine_config* cfg, int32_t tp_size, int3
   step(dalloc(E, &E->gen_done, 1));
   step(dalloc(E, &E->batch_out, (size_t)c.max_batch * E->gen_cap));
   step(dalloc(E, &E->batch_step, 1));
+  step(dalloc(E, &E->barrier_buf, 1));
   if (rc == kOk) {
     cudaMemset(E->attn_ctr, 0, (size_t)R * E->hq * sizeof(int));
     cudaMemset(E->status, 0, sizeof(int));
@@ -642,6 +658,28 @@ int32_t zcu_engine_create_tp(const zcu_engine_config* cfg, int32_t tp_size, int3
     cudaMemcpy(E->ffn_norm, ones.data(), ones.size() * 4, cudaMemcpyHostToDevice);
     cudaMemcpy(E->final_norm, ones.data(), (size_t)c.dim * 4, cudaMemcpyHostToDevice);
     if (cudaDeviceSynchronize() != cudaSuccess) rc = kCudaError;
+  }
+  if (rc == kOk && tp_size > 1) {
+    // the residual all-reduce of decode steps (up to max_batch rows) goes over peer memory when the GPUs have
+    // peer access; larger ones (prefill) and systems without it use NCCL
+    std::string err;
+    if (arp_create(E->comm, (size_t)c.max_batch * c.dim, E->status, &E->arp, &err) != kOk) E->arp = nullptr;
+    // every rank must take the same path: keep the peer all-reduce only if all ranks could map their peers
+    float* ok = nullptr;
+    if (cudaMalloc(&ok, sizeof(float)) == cudaSuccess) {
+      const float mine = E->arp ? 1.0f : 0.0f;
+      float sum = 0.f;
+      cudaMemcpy(ok, &mine, sizeof(float), cudaMemcpyHostToDevice);
+      if (comm_allreduce_sum_f32(E->comm, ok, 1, E->stream, &err) == kOk && cudaStreamSynchronize(E->stream) == cudaSuccess)
+        cudaMemcpy(&sum, ok, sizeof(float), cudaMemcpyDeviceToHost);
+      cudaFree(ok);
+      if (sum != (float)tp_size && E->arp) {
+        arp_destroy(E->arp);
+        E->arp = nullptr;
+      }
+    } else {
+      rc = kOutOfMemory;
+    }
   }
   if (rc != kOk) {
     for (void* p : E->allocs) cudaFree(p);
@@ -664,6 +702,7 @@ int32_t zcu_engine_destroy(void* engine) {
   // graphs that hold collectives go before the communicator
   for (auto& kv : E->step_graphs) cudaGraphExecDestroy(kv.second);
   for (auto& kv : E->batch_graphs) cudaGraphExecDestroy(kv.second);
+  zc::arp_destroy(E->arp);
   zc::comm_destroy(E->comm);
   for (void* p : E->allocs) cudaFree(p);
   if (E->stage) cudaFree(E->stage);
@@ -828,6 +867,7 @@ int32_t zcu_engine_generate(void* engine, int32_t seq_id, const int32_t* prompt,
       E_RC(capture_gen_step(E, repetition_penalty, eos_token, &ge));
       it = E->step_graphs.emplace(key, ge).first;
     }
+    E_RC(rank_barrier(E));
     for (int i = 0; i < n_new; ++i) E_CUDA(cudaGraphLaunch(it->second, E->stream));
   }
   E_CUDA(cudaEventRecord(ev[2], E->stream));
@@ -844,7 +884,8 @@ int32_t zcu_engine_generate(void* engine, int32_t seq_id, const int32_t* prompt,
   int st = 0;
   cudaMemcpy(&st, E->status, 4, cudaMemcpyDeviceToHost);
   if (st) {
-    E->err = "a kernel's bounded wait expired";
+    E->err = "a kernel's bounded wait expired (status " + std::to_string(st) + ")";
+    if (E->arp) E->err += "; " + arp_describe(E->arp);
     return kCudaError;
   }
   return produced;
@@ -983,6 +1024,7 @@ int32_t zcu_engine_generate_batch(void* engine, int32_t batch, const int32_t* se
     E_RC(capture_batch_step(E, batch, &ge));
     it = E->batch_graphs.emplace(batch, ge).first;
   }
+  if (n_new > 0) E_RC(rank_barrier(E));
   cudaEvent_t ev[2];
   for (auto& e : ev) E_CUDA(cudaEventCreate(&e));
   E_CUDA(cudaEventRecord(ev[0], E->stream));
@@ -1004,7 +1046,8 @@ int32_t zcu_engine_generate_batch(void* engine, int32_t batch, const int32_t* se
   int st = 0;
   cudaMemcpy(&st, E->status, 4, cudaMemcpyDeviceToHost);
   if (st) {
-    E->err = "a kernel's bounded wait expired";
+    E->err = "a kernel's bounded wait expired (status " + std::to_string(st) + ")";
+    if (E->arp) E->err += "; " + arp_describe(E->arp);
     return kCudaError;
   }
   return n_new;

@@ -73,7 +73,8 @@ __global__ void swiglu_rows_kernel(const float* __restrict__ gu, OutT* __restric
     const float g = gu[(size_t)t * 2 * ffn + j];
     const float u = gu[(size_t)t * 2 * ffn + ffn + j];
     const float sg = 1.0f / (1.0f + expf(-g));
-    out[i] = (OutT)__fmul_rn(__fmul_rn(g, sg), u);
+    constexpr int kPlanes = sizeof(OutT) == 2 ? 2 : 1;  // __half: rows [hi ffn | lo ffn]
+    store_act(out + (size_t)t * ffn * kPlanes + j, (size_t)ffn, __fmul_rn(__fmul_rn(g, sg), u));
   }
 }
 

@@ -5,8 +5,10 @@
 // QuantizedKernels.MatVecMulQ8_0 / MatVecAddQ8_0 (ZeroLlm/src/ZeroLlm.Core/Engine/LlmEngine.cs:208-304,
 // Quantization/QuantizedKernels.cs:190-308) executed as one contraction.
 //
-// Numerics: the weights enter the tensor core as fp16(q * d) -- the exact product rounded once -- and
-// the activations as fp16(x); products accumulate in fp32 in TMEM.  (An int8 MMA cannot apply the
+// Numerics: the weights enter the tensor core as fp16(q * d) -- the exact product rounded once -- and the
+// activations as a pair of fp16 values, hi = fp16(x) and lo = fp16(x - hi) (x to about 2^-22); each k-step
+// issues one MMA against hi and one against lo into the same fp32 TMEM accumulator, so only the weights'
+// fp16 rounding remains (the tensor core has cycles to spare at the batch sizes where that matters most).  (An int8 MMA cannot apply the
 // per-32-value fp16 block scales inside the tensor core, and a CUDA-core epilogue per block would
 // run several times slower than the MMA itself.)
 //
@@ -172,8 +174,9 @@ __device__ __forceinline__ void dequant32_q4(int4 w, __half2 d2, uint4 (&c)[4]) 
 // QT = 8: Q8_0 weights (int8 tiles); QT = 4: Q4_0 weights (nibble tiles, one 32-value block per dequant item).
 template <int QT>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
-    gemm_q8_0_tc_kernel(const __grid_constant__ CUtensorMap x_map, const __grid_constant__ CUtensorMap w_map,
-                        const __grid_constant__ CUtensorMap s_map, GemmParams p) {
+    gemm_q8_0_tc_kernel(const __grid_constant__ CUtensorMap x_map, const __grid_constant__ CUtensorMap xl_map,
+                        const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap s_map,
+                        GemmParams p) {
   constexpr int W_STAGE_BYTES = w_stage_bytes(QT);
   constexpr int W_TILE_BYTES = w_tile_bytes(QT);
   extern __shared__ uint8_t smem_raw[];
@@ -181,9 +184,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const int bn = p.bn;
   const int AST = p.ab_stages;
   const int WSTAGES = p.w_stages;
-  const int b_stage_bytes = bn * BK * 2;
+  const int b_tile_bytes = bn * BK * 2;         // one fp16 activation tile (hi or lo)
+  const int b_stage_bytes = 2 * b_tile_bytes;   // hi tile, then lo tile
   uint8_t* a_st = smem;                                  // AST x 16 KB (fp16 A, SW128)
-  uint8_t* b_st = a_st + AST * A_STAGE_BYTES;            // AST x bn*128 B (fp16 X, SW128 by TMA)
+  uint8_t* b_st = a_st + AST * A_STAGE_BYTES;            // AST x 2 x bn*128 B (fp16 X hi, lo; SW128 by TMA)
   uint8_t* w_st = b_st + AST * b_stage_bytes;            // WSTAGES x 8 KB (int8 W, TMA, unswizzled)
   uint64_t* bars = reinterpret_cast<uint64_t*>(w_st + WSTAGES * W_STAGE_BYTES);
   uint64_t* ab_full = bars;                            // [AST]: DQ_THREADS dequant arrivals + 1 X TMA (tx)
@@ -273,6 +277,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           if (!mbar_wait(smem_u32(&ab_empty[s]), ph ^ 1, abort_flag, p.status, 6)) break;
           mbar_arrive_tx(smem_u32(&ab_full[s]), (uint32_t)b_stage_bytes);
           tma_load_2d(smem_u32(b_st + s * b_stage_bytes), &x_map, kb * BK, tok0, smem_u32(&ab_full[s]));
+          tma_load_2d(smem_u32(b_st + s * b_stage_bytes + b_tile_bytes), &xl_map, kb * BK, tok0,
+                      smem_u32(&ab_full[s]));
           if (++s == AST) {
             s = 0;
             ph ^= 1;
@@ -306,8 +312,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           const uint32_t b_addr = smem_u32(b_st + s * b_stage_bytes);
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
-            umma_f16(d_tmem, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32), idesc,
-                     (kb != kb0 || kk != 0) ? 1u : 0u);
+            const uint64_t adesc = umma_desc_sw128(a_addr + kk * 32);
+            umma_f16(d_tmem, adesc, umma_desc_sw128(b_addr + kk * 32), idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
+            umma_f16(d_tmem, adesc, umma_desc_sw128(b_addr + b_tile_bytes + kk * 32), idesc, 1u);  // x's lo part
           }
           umma_commit(smem_u32(&ab_empty[s]));  // frees the A/B stage once these MMAs have read it
           if (++s == AST) {
@@ -458,17 +465,23 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ part, float* __re
   }
 }
 
-__global__ void f32_to_f16_kernel(const float* __restrict__ x, __half* __restrict__ y, size_t n) {
+// x [m][k] fp32 -> y [m][hi k | lo k] fp16 with hi = fp16(x), lo = fp16(x - hi).
+__global__ void f32_to_f16_kernel(const float* __restrict__ x, __half* __restrict__ y, int m, int k) {
   pdl_trigger();
   pdl_wait();
-  const size_t n4 = n / 4;
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
-    const float4 v = reinterpret_cast<const float4*>(x)[i];
+  const int k4 = k / 4;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < (size_t)m * k4; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / k4, c = i % k4;
+    const float4 v = reinterpret_cast<const float4*>(x + r * k)[c];
     __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
-    uint2 o;
-    o.x = *reinterpret_cast<uint32_t*>(&a);
-    o.y = *reinterpret_cast<uint32_t*>(&b);
-    reinterpret_cast<uint2*>(y)[i] = o;
+    const float2 fa = __half22float2(a), fb = __half22float2(b);
+    __half2 la = __floats2half2_rn(v.x - fa.x, v.y - fa.y), lb = __floats2half2_rn(v.z - fb.x, v.w - fb.y);
+    __half2* hi = reinterpret_cast<__half2*>(y + r * 2 * k + 4 * c);
+    __half2* lo = reinterpret_cast<__half2*>(y + r * 2 * k + k + 4 * c);
+    hi[0] = a;
+    hi[1] = b;
+    lo[0] = la;
+    lo[1] = lb;
   }
 }
 
@@ -512,7 +525,7 @@ constexpr int SMEM_FIXED = 1024 + 512;  // alignment slack + barriers, TMEM slot
 static void ring_depths(int qt, int bn, int& ab, int& w) {
   w = bn <= 64 ? 3 : 2;
   if (qt == 4) ++w;  // nibble tiles are half the size
-  ab = (SMEM_LIMIT - SMEM_FIXED - w * w_stage_bytes(qt)) / (A_STAGE_BYTES + bn * BK * 2);
+  ab = (SMEM_LIMIT - SMEM_FIXED - w * w_stage_bytes(qt)) / (A_STAGE_BYTES + 2 * bn * BK * 2);
   if (ab > MAX_STAGES) ab = MAX_STAGES;
 }
 
@@ -557,7 +570,7 @@ static size_t align256(size_t b) { return (b + 255) & ~size_t(255); }
 
 size_t gemm_q8_0_workspace_bytes(int m, int n, int k) {
   const GemmConfig c = choose_config(m, n, k);
-  size_t b = align256((size_t)m * k * 2);
+  size_t b = align256((size_t)m * k * 4);  // fp16 [m][hi k | lo k]
   if (c.splits > 1) b += (size_t)c.splits * m * n * sizeof(float);
   return b;
 }
@@ -571,21 +584,21 @@ size_t gemm_workspace_max(int m_max, int n, int k) {
 
 // Core launcher on fp16 activations x16 [m][k] (16-byte aligned rows); QT = 8 (Q8_0) or 4 (Q4_0) weights.
 template <int QT>
-static int launch_gemm(const void* qs, const uint16_t* d, const __half* x16, float* y, int m, int n, int k,
-                       int accumulate, char* ws, int* status, cudaStream_t s) {
+static int launch_gemm(const void* qs, const uint16_t* d, const __half* x_hi, const __half* x_lo, int ldx, float* y,
+                       int m, int n, int k, int accumulate, char* ws, int* status, cudaStream_t s) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return kCudaError;
   const GemmConfig c = choose_config(m, n, k, QT);
-  float* part = reinterpret_cast<float*>(ws + align256((size_t)m * k * 2));
-  CUtensorMap xmap, wmap;
-  {
+  float* part = reinterpret_cast<float*>(ws + align256((size_t)m * k * 4));
+  CUtensorMap xmap, xlmap, wmap;
+  for (int half = 0; half < 2; ++half) {  // the hi and the lo values of x: [m][k] each, row pitch ldx elements
     cuuint64_t gdim[2] = {(cuuint64_t)k, (cuuint64_t)m};
-    cuuint64_t gstride[1] = {(cuuint64_t)k * 2};
+    cuuint64_t gstride[1] = {(cuuint64_t)ldx * 2};
     cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)c.bn};
     cuuint32_t estride[2] = {1, 1};
-    if (enc(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(x16), gdim, gstride, box, estride,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    if (enc(half ? &xlmap : &xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(half ? x_lo : x_hi), gdim,
+            gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return kCudaError;
   }
   {
@@ -631,12 +644,12 @@ static int launch_gemm(const void* qs, const uint16_t* d, const __half* x16, flo
   p.n_tiles = c.n_tiles;
   p.splits = c.splits;
   p.kb_per_split = c.kb_per;
-  const int smem = SMEM_FIXED + c.ab_stages * (A_STAGE_BYTES + c.bn * BK * 2) + c.w_stages * w_stage_bytes(QT);
+  const int smem = SMEM_FIXED + c.ab_stages * (A_STAGE_BYTES + 2 * c.bn * BK * 2) + c.w_stages * w_stage_bytes(QT);
   if (cudaFuncSetAttribute(gemm_q8_0_tc_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return kCudaError;
   const int grid = std::min(c.n_tiles * c.splits, num_sms());
-  if (launch_pdl(gemm_q8_0_tc_kernel<QT>, dim3(grid), dim3(GEMM_THREADS), (size_t)smem, s, xmap, wmap, smap, p) !=
-      cudaSuccess)
+  if (launch_pdl(gemm_q8_0_tc_kernel<QT>, dim3(grid), dim3(GEMM_THREADS), (size_t)smem, s, xmap, xlmap, wmap, smap,
+                 p) != cudaSuccess)
     return kCudaError;
   if (c.splits > 1) {
     const size_t mn = (size_t)m * n;
@@ -658,24 +671,31 @@ static int check_gemm_args(const void* qs, const void* d, const void* x, const v
   return kOk;
 }
 
+static int convert_x(const float* x, char* ws, int m, int k, cudaStream_t s) {
+  const size_t n4 = (size_t)m * k / 4;
+  return launch_pdl(f32_to_f16_kernel, dim3((unsigned)std::min<size_t>((n4 + 255) / 256, 148 * 8)), dim3(256), 0, s, x,
+                    reinterpret_cast<__half*>(ws), m, k) == cudaSuccess
+             ? kOk
+             : kCudaError;
+}
+
 int gemm_q8_0_tc(const int8_t* qs, const uint16_t* d, const float* x, float* y, int m, int n, int k, int accumulate,
                  void* workspace, size_t workspace_bytes, int* status, cudaStream_t s) {
   const int rc = check_gemm_args(qs, d, x, y, m, n, k, workspace, workspace_bytes, status);
   if (rc != kOk) return rc;
   char* ws = static_cast<char*>(workspace);
-  __half* x16 = reinterpret_cast<__half*>(ws);
-  const size_t nx = (size_t)m * k;
-  if (launch_pdl(f32_to_f16_kernel, dim3((unsigned)std::min<size_t>((nx / 4 + 255) / 256, 148 * 8)), dim3(256), 0, s,
-                 x, x16, nx) != cudaSuccess)
-    return kCudaError;
-  return launch_gemm<8>(qs, d, x16, y, m, n, k, accumulate, ws, status, s);
+  if (convert_x(x, ws, m, k, s) != kOk) return kCudaError;
+  const __half* x16 = reinterpret_cast<const __half*>(ws);
+  return launch_gemm<8>(qs, d, x16, x16 + k, 2 * k, y, m, n, k, accumulate, ws, status, s);
 }
 
-int gemm_q8_0_tc_h(const int8_t* qs, const uint16_t* d, const __half* x16, float* y, int m, int n, int k,
-                   int accumulate, void* workspace, size_t workspace_bytes, int* status, cudaStream_t s) {
-  const int rc = check_gemm_args(qs, d, x16, y, m, n, k, workspace, workspace_bytes, status);
+int gemm_q8_0_tc_h(const int8_t* qs, const uint16_t* d, const __half* x_hi, const __half* x_lo, int ldx, float* y,
+                   int m, int n, int k, int accumulate, void* workspace, size_t workspace_bytes, int* status,
+                   cudaStream_t s) {
+  const int rc = check_gemm_args(qs, d, x_hi, y, m, n, k, workspace, workspace_bytes, status);
   if (rc != kOk) return rc;
-  return launch_gemm<8>(qs, d, x16, y, m, n, k, accumulate, static_cast<char*>(workspace), status, s);
+  if ((reinterpret_cast<uintptr_t>(x_lo) & 15) || (ldx * 2) % 16) return kUnsupported;
+  return launch_gemm<8>(qs, d, x_hi, x_lo, ldx, y, m, n, k, accumulate, static_cast<char*>(workspace), status, s);
 }
 
 int gemm_q4_0_tc(const uint8_t* qs, const uint16_t* d, const float* x, float* y, int m, int n, int k, int accumulate,
@@ -684,19 +704,18 @@ int gemm_q4_0_tc(const uint8_t* qs, const uint16_t* d, const float* x, float* y,
   if (rc != kOk) return rc;
   if (k % 32) return kUnsupported;  // nibble rows (K / 2 bytes) must be 16-byte multiples
   char* ws = static_cast<char*>(workspace);
-  __half* x16 = reinterpret_cast<__half*>(ws);
-  const size_t nx = (size_t)m * k;
-  if (launch_pdl(f32_to_f16_kernel, dim3((unsigned)std::min<size_t>((nx / 4 + 255) / 256, 148 * 8)), dim3(256), 0, s,
-                 x, x16, nx) != cudaSuccess)
-    return kCudaError;
-  return launch_gemm<4>(qs, d, x16, y, m, n, k, accumulate, ws, status, s);
+  if (convert_x(x, ws, m, k, s) != kOk) return kCudaError;
+  const __half* x16 = reinterpret_cast<const __half*>(ws);
+  return launch_gemm<4>(qs, d, x16, x16 + k, 2 * k, y, m, n, k, accumulate, ws, status, s);
 }
 
-int gemm_q4_0_tc_h(const uint8_t* qs, const uint16_t* d, const __half* x16, float* y, int m, int n, int k,
-                   int accumulate, void* workspace, size_t workspace_bytes, int* status, cudaStream_t s) {
-  const int rc = check_gemm_args(qs, d, x16, y, m, n, k, workspace, workspace_bytes, status);
+int gemm_q4_0_tc_h(const uint8_t* qs, const uint16_t* d, const __half* x_hi, const __half* x_lo, int ldx, float* y,
+                   int m, int n, int k, int accumulate, void* workspace, size_t workspace_bytes, int* status,
+                   cudaStream_t s) {
+  const int rc = check_gemm_args(qs, d, x_hi, y, m, n, k, workspace, workspace_bytes, status);
   if (rc != kOk) return rc;
-  return launch_gemm<4>(qs, d, x16, y, m, n, k, accumulate, static_cast<char*>(workspace), status, s);
+  if ((reinterpret_cast<uintptr_t>(x_lo) & 15) || (ldx * 2) % 16) return kUnsupported;
+  return launch_gemm<4>(qs, d, x_hi, x_lo, ldx, y, m, n, k, accumulate, static_cast<char*>(workspace), status, s);
 }
 
 }  // namespace zc

@@ -32,14 +32,17 @@ size_t gemm_q8_0_workspace_bytes(int m, int n, int k);  // fp16 activations + sp
 size_t gemm_workspace_max(int m_max, int n, int k);       // the largest of the above over 1 <= m <= m_max
 int gemm_q8_0_tc(const int8_t* qs, const uint16_t* d, const float* x, float* y, int m, int n, int k, int accumulate,
                  void* workspace, size_t workspace_bytes, int* status, cudaStream_t s);
-// The same on fp16 activations [m][k] (a producer that writes fp16 saves the conversion kernel).
-int gemm_q8_0_tc_h(const int8_t* qs, const uint16_t* d, const __half* x16, float* y, int m, int n, int k,
-                   int accumulate, void* workspace, size_t workspace_bytes, int* status, cudaStream_t s);
+// The same on fp16 activations given as hi / lo pairs (x = hi + lo, see gemm_tc.cu): x_hi and x_lo rows of k
+// values with a row pitch of ldx elements (producers write [rows][hi k | lo k]: x_lo = x_hi + k, ldx = 2k).
+int gemm_q8_0_tc_h(const int8_t* qs, const uint16_t* d, const __half* x_hi, const __half* x_lo, int ldx, float* y,
+                   int m, int n, int k, int accumulate, void* workspace, size_t workspace_bytes, int* status,
+                   cudaStream_t s);
 // Q4_0 weights (SoA nibbles [N][K/32][16] + fp16 scales), same workspace size rule.
 int gemm_q4_0_tc(const uint8_t* qs, const uint16_t* d, const float* x, float* y, int m, int n, int k, int accumulate,
                  void* workspace, size_t workspace_bytes, int* status, cudaStream_t s);
-int gemm_q4_0_tc_h(const uint8_t* qs, const uint16_t* d, const __half* x16, float* y, int m, int n, int k,
-                   int accumulate, void* workspace, size_t workspace_bytes, int* status, cudaStream_t s);
+int gemm_q4_0_tc_h(const uint8_t* qs, const uint16_t* d, const __half* x_hi, const __half* x_lo, int ldx, float* y,
+                   int m, int n, int k, int accumulate, void* workspace, size_t workspace_bytes, int* status,
+                   cudaStream_t s);
 
 // ---- paged decode attention (attention.cu) ----
 // One query token per sequence. K/V element (page p, slot t, kv head h, dim e) lives at
@@ -62,7 +65,9 @@ struct PagedAttnArgs {
   float* workspace;   // split-K partials; may be null when splits == 1
   int* counters;      // [batch*hq] zero-initialised arrival counters (left zeroed); null when splits == 1
   int splits;         // 0 = choose automatically
-  int out_half = 0;   // 1: out is __half (the input of a tensor-core GEMM), else float
+  int out_half = 0;   // 1: out is __half hi / lo pairs (the input of a tensor-core GEMM): hi at the float
+                      //    layout's index, lo out_lo_offset elements after it; else float
+  long long out_lo_offset = 0;
   long long q_stride = 0;     // elements between consecutive queries (0: hq*hd)
   long long out_stride = 0;   // elements between consecutive outputs (0: hq*hd)
   long long pt_stride = -1;   // elements between page-table rows (-1: max_pages; 0: all queries share row 0)
@@ -74,6 +79,7 @@ int paged_attention(const PagedAttnArgs& a, cudaStream_t s);
 
 // ---- small decode-step operators (ops.cu) ----
 int rmsnorm(const float* x, const float* w, float* out, int rows, int n, float eps, cudaStream_t s);
+// out [rows][hi n | lo n]: the GEMM's activation pairs (hi = fp16(v), lo = fp16(v - hi)).
 int rmsnorm_h(const float* x, const float* w, __half* out, int rows, int n, float eps, cudaStream_t s);
 int swiglu(const float* gate, const float* up, float* out, size_t n, cudaStream_t s);
 int silu(const float* x, float* out, size_t n, cudaStream_t s);
@@ -92,7 +98,7 @@ int rope_append_kv(float* qkv, int T, int hq, int hkv, int hd, const int32_t* po
                    int max_pos, __half* k_pool, __half* v_pool, cudaStream_t s);
 // out[t][i] = SwiGLU(gu[t][i], gu[t][ffn + i])
 int swiglu_rows(const float* gu, float* out, int T, int ffn, cudaStream_t s);
-int swiglu_rows_h(const float* gu, __half* out, int T, int ffn, cudaStream_t s);
+int swiglu_rows_h(const float* gu, __half* out, int T, int ffn, cudaStream_t s);  // out [T][hi ffn | lo ffn]
 // LlmSampler greedy branch per row: repetition penalty over past[row][0:past_len[row]] then argmax
 // (first index wins ties).  penalty <= 1 disables the penalty.  out[row] = token.
 int greedy_sample(float* logits, int rows, int vocab, const int32_t* past, const int32_t* past_len, int past_cap,

@@ -137,7 +137,7 @@ __global__ void moe_plan_kernel(const int32_t* __restrict__ sel_idx, int pairs, 
   for (int e = threadIdx.x; e < E; e += blockDim.x) fill[e] = cur[e];
 }
 
-// xs[row_of[p]] = fp16(x[p / k]) for every pair p.
+// xs[row_of[p]] = x[p / k] as fp16 hi / lo pairs ([hi dim | lo dim] per row) for every pair p.
 __global__ void moe_gather_kernel(const float* __restrict__ x, const int32_t* __restrict__ row_of, int pairs, int k,
                                   int dim, __half* __restrict__ xs) {
   pdl_trigger();
@@ -147,9 +147,11 @@ __global__ void moe_gather_kernel(const float* __restrict__ x, const int32_t* __
        i += (size_t)gridDim.x * blockDim.x) {
     const int p = (int)(i / n4), c = (int)(i % n4);
     const float4 v = reinterpret_cast<const float4*>(x + (size_t)(p / k) * dim)[c];
-    __half2* o = reinterpret_cast<__half2*>(xs + (size_t)row_of[p] * dim + 4 * c);
-    o[0] = __floats2half2_rn(v.x, v.y);
-    o[1] = __floats2half2_rn(v.z, v.w);
+    __half* o = xs + (size_t)row_of[p] * 2 * dim + 4 * c;
+    store_hl(o + 0, dim, v.x);
+    store_hl(o + 1, dim, v.y);
+    store_hl(o + 2, dim, v.z);
+    store_hl(o + 3, dim, v.w);
   }
 }
 
@@ -213,9 +215,9 @@ struct Moe {
   // routing state for up to max_tokens tokens
   int32_t *sel_idx = nullptr, *counts = nullptr, *offsets = nullptr, *fill = nullptr, *row_of = nullptr;
   float* sel_w = nullptr;
-  __half* xs = nullptr;     // gathered rows, expert order [pairs][dim] (fp16)
-  __half* xr = nullptr;     // rows received for local experts [recv][dim] (fp16)
-  __half* hbuf = nullptr;   // SwiGLU output [rows][ffn] fp16
+  __half* xs = nullptr;     // gathered rows, expert order [pairs][hi dim | lo dim] (fp16 pairs)
+  __half* xr = nullptr;     // rows received for local experts [recv][hi dim | lo dim]
+  __half* hbuf = nullptr;   // SwiGLU output [rows][hi ffn | lo ffn]
   float* gu = nullptr;      // gate|up [rows][2*ffn]
   float* yl = nullptr;      // local expert outputs [recv rows][dim]
   float* ys = nullptr;      // outputs back in this rank's pair order [pairs][dim]
@@ -275,8 +277,8 @@ int ensure_rows(Moe* M, size_t rows) {
   for (void* p : {(void*)M->xr, (void*)M->hbuf, (void*)M->gu, (void*)M->yl, (void*)M->perm, M->gemm_ws})
     if (p) free_one(M, p);
   const zcu_moe_config& c = M->cfg;
-  M_RC(malloc_into(M, &M->xr, rows * c.dim));
-  M_RC(malloc_into(M, &M->hbuf, rows * c.ffn));
+  M_RC(malloc_into(M, &M->xr, rows * 2 * c.dim));
+  M_RC(malloc_into(M, &M->hbuf, rows * 2 * c.ffn));
   M_RC(malloc_into(M, &M->gu, rows * 2 * c.ffn));
   M_RC(malloc_into(M, &M->yl, rows * c.dim));
   M_RC(malloc_into(M, &M->perm, rows));
@@ -288,21 +290,23 @@ int ensure_rows(Moe* M, size_t rows) {
   return kOk;
 }
 
+// x16 rows are [hi k | lo k].
 int expert_gemm(Moe* M, const ExpertW& w, const __half* x16, float* y, int rows, int n, int k) {
   if (M->cfg.qtype == 4)
-    return gemm_q4_0_tc_h(w.qs, w.d, x16, y, rows, n, k, 0, M->gemm_ws, M->gemm_ws_bytes, M->status, M->stream);
-  return gemm_q8_0_tc_h(reinterpret_cast<const int8_t*>(w.qs), w.d, x16, y, rows, n, k, 0, M->gemm_ws,
-                        M->gemm_ws_bytes, M->status, M->stream);
+    return gemm_q4_0_tc_h(w.qs, w.d, x16, x16 + k, 2 * k, y, rows, n, k, 0, M->gemm_ws, M->gemm_ws_bytes, M->status,
+                          M->stream);
+  return gemm_q8_0_tc_h(reinterpret_cast<const int8_t*>(w.qs), w.d, x16, x16 + k, 2 * k, y, rows, n, k, 0,
+                        M->gemm_ws, M->gemm_ws_bytes, M->status, M->stream);
 }
 
-// Runs the local experts over `rows` fp16 rows sorted by local expert (counts per local expert on the host).
+// Runs the local experts over fp16 hi / lo rows sorted by local expert (counts per local expert on the host).
 int run_local_experts(Moe* M, const __half* x16, const std::vector<int>& cnt, float* out) {
   const zcu_moe_config& c = M->cfg;
   int row = 0;
   for (int le = 0; le < M->e_count; ++le) {
     const int n = cnt[le];
     if (n == 0) continue;
-    const __half* xe = x16 + (size_t)row * c.dim;
+    const __half* xe = x16 + (size_t)row * 2 * c.dim;
     M_RC(expert_gemm(M, M->w1[le], xe, M->gu, n, 2 * c.ffn, c.dim));  // [gate | up]
     M_RC(swiglu_rows_h(M->gu, M->hbuf, n, c.ffn, M->stream));
     M_RC(expert_gemm(M, M->w2[le], M->hbuf, out + (size_t)row * c.dim, n, c.dim, c.ffn));
@@ -330,6 +334,7 @@ int32_t zcu_moe_create(const zcu_moe_config* cfg, int32_t ep_size, int32_t ep_ra
       (c.qtype != 4 && c.qtype != 8) || ep_size < 1 || ep_rank < 0 || ep_rank >= ep_size ||
       c.n_experts % ep_size)
     return kBadArgument;
+  if (2 * c.ffn < c.dim) return kUnsupported;  // gu rows (2 * ffn floats) double as row scratch of dim floats
   Moe* M = new Moe();
   M->cfg = c;
   M->ep_size = ep_size;
@@ -370,7 +375,7 @@ int32_t zcu_moe_create(const zcu_moe_config* cfg, int32_t ep_size, int32_t ep_ra
   step(malloc_into(M, &M->counts, MOE_MAX_EXPERTS));
   step(malloc_into(M, &M->offsets, MOE_MAX_EXPERTS + 1));
   step(malloc_into(M, &M->fill, MOE_MAX_EXPERTS));
-  step(malloc_into(M, &M->xs, pairs * c.dim));
+  step(malloc_into(M, &M->xs, pairs * 2 * c.dim));
   step(malloc_into(M, &M->ys, pairs * c.dim));
   step(malloc_into(M, &M->status, 1));
   if (rc == kOk) rc = ensure_rows(M, std::max<size_t>(pairs, 64));
@@ -476,7 +481,7 @@ int32_t zcu_moe_forward(void* moe, const float* xnorm, const float* router_logit
   const int epr = M->e_count;
   std::vector<int> send_rows(W, 0), recv_rows(W, 0);
   for (int e = 0; e < E; ++e) send_rows[e / epr] += cnt[e];
-  const size_t row_bytes = (size_t)c.dim * sizeof(__half);
+  const size_t row_bytes = (size_t)2 * c.dim * sizeof(__half);  // one hi / lo row
   std::vector<int> local_cnt(epr, 0);  // rows per local expert over all sources
   std::vector<int> recv_cnt((size_t)W * epr, 0);  // [source][local expert]
   if (W == 1) {
@@ -530,9 +535,10 @@ int32_t zcu_moe_forward(void* moe, const float* xnorm, const float* router_logit
     if (total_recv > 0) {
       M_CUDA(cudaMemcpyAsync(M->perm, perm.data(), perm.size() * sizeof(int32_t), cudaMemcpyHostToDevice, s));
       // xr -> expert-contiguous copy in hbuf's place is not possible (different widths): use gu as scratch
+      // (a hi / lo row is dim floats' worth of bytes; gu holds 2 * ffn floats per row)
       __half* xsorted = reinterpret_cast<__half*>(M->gu);
-      M_CUDA(launch_pdl(moe_scatter_rows_kernel<__half>, dim3(grid_for((size_t)total_recv * c.dim)), dim3(256), 0, s,
-                        (const __half*)M->xr, (const int32_t*)M->perm, total_recv, c.dim, xsorted));
+      M_CUDA(launch_pdl(moe_scatter_rows_kernel<__half>, dim3(grid_for((size_t)total_recv * 2 * c.dim)), dim3(256), 0,
+                        s, (const __half*)M->xr, (const int32_t*)M->perm, total_recv, 2 * c.dim, xsorted));
       // the expert pass needs gu for gate|up: move the sorted rows back into xr first
       M_CUDA(cudaMemcpyAsync(M->xr, xsorted, (size_t)total_recv * row_bytes, cudaMemcpyDeviceToDevice, s));
       M_RC(run_local_experts(M, M->xr, local_cnt, M->yl));

@@ -17,8 +17,9 @@ namespace zc {
 
 namespace {
 
-// One CTA per row.  OutT = float, or __half when the row feeds the tensor-core GEMM directly.  Launched with
-// programmatic dependent launch: it waits for the previous kernel before reading x.
+// One CTA per row.  OutT = float, or __half when the row feeds the tensor-core GEMM directly: then out rows are
+// [hi n | lo n] (store_hl).  Launched with programmatic dependent launch: it waits for the previous kernel
+// before reading x.
 template <typename OutT>
 __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w, OutT* __restrict__ out,
                                int n, float eps) {
@@ -26,7 +27,8 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
   pdl_wait();
   __shared__ float red[32];
   const float* xr = x + (size_t)blockIdx.x * n;
-  OutT* orow = out + (size_t)blockIdx.x * n;
+  constexpr int kPlanes = sizeof(OutT) == 2 ? 2 : 1;
+  OutT* orow = out + (size_t)blockIdx.x * n * kPlanes;
   float ss = 0.f;
   for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
   ss = warp_sum(ss);
@@ -40,7 +42,7 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
   __syncthreads();
   const float mean_sq = red[0] / (float)n;
   const float inv = 1.0f / (float)sqrt((double)(mean_sq + eps));
-  for (int i = threadIdx.x; i < n; i += blockDim.x) orow[i] = (OutT)(xr[i] * inv * w[i]);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) store_act(orow + i, (size_t)n, xr[i] * inv * w[i]);
 }
 
 __global__ void swiglu_kernel(const float* __restrict__ g, const float* __restrict__ u, float* __restrict__ out,
