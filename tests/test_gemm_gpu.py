@@ -1,7 +1,8 @@
 """Prefill / batched Q8_0 GEMM on tcgen05 vs the oracle's token-parallel MatVecMulQ8_0 (LlmEngine.PrefillPrompt).
 
 Tolerance: max|Y - Y_oracle| / max|Y_oracle| <= 1e-3 -- the north-star bound for fp32 outputs.  The tensor
-core consumes fp16(q*d) and fp16(x) with fp32 accumulation; the measured error is printed.
+core consumes fp16(q*d) and x as an fp16 pair (hi = fp16(x), lo = fp16(x - hi): x to about 2^-22) with fp32
+accumulation, so the weights' single fp16 rounding is the only approximation; the measured error is printed.
 """
 import numpy as np
 import pytest
@@ -66,7 +67,8 @@ def test_gemm_is_deterministic_and_repeatable():
 
 
 def test_gemm_matches_fp16_rounded_reference_tightly():
-    """With X and q*d rounded to fp16 exactly as the kernel does, only the fp32 summation order differs."""
+    """With q*d rounded to fp16 exactly as the kernel does (and x exact: the hi / lo pair carries it to ~2^-22),
+    only the fp32 summation order differs."""
     from zeroplatform_b200.ops import QuantizedWeight
     rng = np.random.default_rng(2)
     n, k, m = 256, 512, 96
@@ -76,8 +78,7 @@ def test_gemm_matches_fp16_rounded_reference_tightly():
     d = b[:, :, :2].copy().view(np.float16).astype(np.float32)          # [n, k/32, 1]
     q = b[:, :, 2:].view(np.int8).astype(np.float32)                   # [n, k/32, 32]
     w16 = (q * d).astype(np.float16).astype(np.float64).reshape(n, k)  # fp16(q*d): single rounding of the exact product
-    x16 = x.astype(np.float16).astype(np.float64)
-    ref = x16 @ w16.T
+    ref = x.astype(np.float64) @ w16.T
     qw = QuantizedWeight.upload(8, blocks, n, k)
     y = torch.empty((m, n), device="cuda")
     _run(qw, torch.from_numpy(x).cuda(), y)

@@ -151,3 +151,20 @@ def test_registered_weights_are_used_and_released():
     assert L.zc_register_weights(2, _np_ptr(b4), 300, 2048) == 0
     assert rel_err(TensorBlas.gemv_q4_0(x4, b4, 300, 2048), O.matvec(4, b4, x4, 300, 2048)) <= TOL
     assert L.zc_unregister_weights(_np_ptr(b4)) == 0
+
+
+def test_registered_weights_replayed_calls_track_new_activations():
+    """Calls on registered weights after the first replay one recorded graph (zero-copy x / y through pinned
+    buffers): every call must see its own x, including a row count whose y is not a whole number of 16 bytes."""
+    from zeroplatform_b200 import _lib
+    from zeroplatform_b200.ops import TensorBlas, _np_ptr
+    L = _lib.lib()
+    for qtype, ggml, n, k in ((8, 8, 301, 512), (4, 2, 77, 1024)):
+        blocks, _, _ = _case(qtype, n, k, 11)
+        assert L.zc_register_weights(ggml, _np_ptr(blocks), n, k) == 0
+        rng = np.random.default_rng(12)
+        gemv = TensorBlas.gemv_q8_0 if qtype == 8 else TensorBlas.gemv_q4_0
+        for _ in range(4):
+            x = rng.standard_normal(k, dtype=np.float32)
+            assert rel_err(gemv(x, blocks, n, k), O.matvec(qtype, blocks, x, n, k)) <= TOL
+        assert L.zc_unregister_weights(_np_ptr(blocks)) == 0

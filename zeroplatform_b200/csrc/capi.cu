@@ -64,7 +64,18 @@ struct HostCtx {
   cudaStream_t stream = nullptr;
   void* buf[8] = {};
   size_t cap[8] = {};
+  // Registered-weight calls: x and y pass through pinned host buffers mapped into the device's address space
+  // (copied by kernels, no DMA set-up), and the fetch -> GEMV -> store sequence of each registered tensor is
+  // replayed as one CUDA graph.  Graphs name the staging buffers, so any reallocation drops them all.
+  void* pin[2] = {};  // [0] x, [1] y (host pointers; the device uses the same addresses)
+  size_t pin_cap[2] = {};
+  std::map<uint64_t, cudaGraphExec_t> graphs;  // registration id -> fetch x, GEMV, store y
 };
+
+void drop_graphs(HostCtx* c) {
+  for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second);
+  c->graphs.clear();
+}
 thread_local std::vector<HostCtx*> t_ctx;
 
 int host_ctx(HostCtx** out) {
@@ -86,6 +97,7 @@ int host_ctx(HostCtx** out) {
 int staging(HostCtx* c, int slot, size_t bytes, void** p) {
   if (bytes == 0) bytes = 16;
   if (c->cap[slot] < bytes) {
+    drop_graphs(c);
     if (c->buf[slot]) {
       ZC_CUDA(cudaStreamSynchronize(c->stream));
       ZC_CUDA(cudaFree(c->buf[slot]));
@@ -100,6 +112,29 @@ int staging(HostCtx* c, int slot, size_t bytes, void** p) {
     c->cap[slot] = cap;
   }
   *p = c->buf[slot];
+  return kOk;
+}
+
+// Pinned, device-mapped host buffer `slot` of at least `bytes` (grow-only).
+int pinned(HostCtx* c, int slot, size_t bytes, void** p) {
+  if (bytes == 0) bytes = 16;
+  if (c->pin_cap[slot] < bytes) {
+    drop_graphs(c);
+    if (c->pin[slot]) {
+      ZC_CUDA(cudaStreamSynchronize(c->stream));
+      ZC_CUDA(cudaFreeHost(c->pin[slot]));
+      c->pin[slot] = nullptr;
+      c->pin_cap[slot] = 0;
+    }
+    const size_t cap = std::max(bytes, c->pin_cap[slot] * 2);
+    if (cudaHostAlloc(&c->pin[slot], cap, cudaHostAllocMapped) != cudaSuccess) {
+      cudaGetLastError();
+      c->pin[slot] = nullptr;
+      return fail(kOutOfMemory, "pinned staging allocation failed");
+    }
+    c->pin_cap[slot] = cap;
+  }
+  *p = c->pin[slot];
   return kOk;
 }
 
@@ -192,6 +227,7 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 
 // Weights registered with zc_register_weights: host pointer -> device-resident SoA copy.
 struct Registered {
+  uint64_t id = 0;  // unique per registration (keys the per-thread replay graphs)
   int qtype = 0;
   size_t n = 0, k = 0;
   int device = -1;
@@ -200,6 +236,7 @@ struct Registered {
 };
 std::mutex g_reg_mu;
 std::map<std::pair<const uint8_t*, int>, Registered> g_reg;  // (host pointer, device)
+uint64_t g_reg_next_id = 1;
 
 bool find_registered(const uint8_t* w, int qtype, size_t n, size_t k, Registered* out) {
   int dev = 0;
@@ -220,18 +257,48 @@ int gemv_host(int qtype, const uint8_t* w, const float* x, float* y, size_t n, s
   ZC_RC(host_ctx(&c));
   Registered reg;
   if (find_registered(w, qtype, n, k, &reg)) {  // resident weights: only x and y cross PCIe
-    void *d_x, *d_y;
+    void *d_x, *d_y, *h_x, *h_y;
     ZC_RC(staging(c, 3, k * sizeof(float), &d_x));
     ZC_RC(staging(c, 4, n * sizeof(float), &d_y));
-    ZC_CUDA(cudaMemcpyAsync(d_x, x, k * sizeof(float), cudaMemcpyHostToDevice, c->stream));
-    if (qtype == 8)
-      ZC_RC(gemv_q8_0((const int8_t*)reg.qs, (const uint16_t*)reg.d, (const float*)d_x, (float*)d_y, (int)n, (int)k,
-                      0, c->stream));
-    else
-      ZC_RC(gemv_q4_0((const uint8_t*)reg.qs, (const uint16_t*)reg.d, (const float*)d_x, (float*)d_y, (int)n, (int)k,
-                      0, c->stream));
-    ZC_CUDA(cudaMemcpyAsync(y, d_y, n * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
-    return finish(c);
+    ZC_RC(pinned(c, 0, k * sizeof(float), &h_x));
+    ZC_RC(pinned(c, 1, n * sizeof(float), &h_y));
+    std::memcpy(h_x, x, k * sizeof(float));
+    // fetch x over the bus, the GEMV (its weight loads start while x is in flight), store y over the bus
+    auto enqueue = [&]() -> int {
+      ZC_RC(copy_words(h_x, d_x, k * sizeof(float), c->stream));
+      if (qtype == 8)
+        ZC_RC(gemv_q8_0((const int8_t*)reg.qs, (const uint16_t*)reg.d, (const float*)d_x, (float*)d_y, (int)n,
+                        (int)k, 0, c->stream));
+      else
+        ZC_RC(gemv_q4_0((const uint8_t*)reg.qs, (const uint16_t*)reg.d, (const float*)d_x, (float*)d_y, (int)n,
+                        (int)k, 0, c->stream));
+      return copy_words(d_y, h_y, n * sizeof(float), c->stream);
+    };
+    auto it = c->graphs.find(reg.id);
+    if (it != c->graphs.end()) {
+      ZC_CUDA(cudaGraphLaunch(it->second, c->stream));
+    } else {
+      ZC_RC(enqueue());  // first call of this tensor on this thread: run directly, then record the graph
+      ZC_RC(finish(c));
+      if (c->graphs.size() >= 256) drop_graphs(c);
+      cudaGraph_t g = nullptr;
+      cudaGraphExec_t ge = nullptr;
+      ZC_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+      const int rc = enqueue();
+      const cudaError_t ec = cudaStreamEndCapture(c->stream, &g);
+      if (rc != kOk) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+      }
+      ZC_CUDA(ec);
+      const cudaError_t ei = cudaGraphInstantiate(&ge, g, 0);
+      cudaGraphDestroy(g);
+      ZC_CUDA(ei);
+      c->graphs[reg.id] = ge;
+    }
+    ZC_RC(finish(c));
+    std::memcpy(y, h_y, n * sizeof(float));
+    return kOk;
   }
   const size_t nb = n * (k / QK);
   const size_t aos_bytes = nb * (qtype == 8 ? Q8_BLOCK_BYTES : Q4_BLOCK_BYTES);
@@ -335,6 +402,7 @@ int32_t zc_register_weights(int32_t ggml_type, const uint8_t* w, size_t n_rows, 
     return rc;
   }
   std::lock_guard<std::mutex> g(g_reg_mu);
+  r.id = g_reg_next_id++;
   g_reg[{w, dev}] = r;
   return kOk;
 }

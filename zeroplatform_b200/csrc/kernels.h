@@ -78,6 +78,8 @@ int paged_attention_choose_splits(int batch, int hkv, int max_ctx, int page_size
 int paged_attention(const PagedAttnArgs& a, cudaStream_t s);
 
 // ---- small decode-step operators (ops.cu) ----
+// dst = src, `bytes` a multiple of 4, both 16-byte aligned; either side may be mapped pinned host memory.
+int copy_words(const void* src, void* dst, size_t bytes, cudaStream_t s);
 int rmsnorm(const float* x, const float* w, float* out, int rows, int n, float eps, cudaStream_t s);
 // out [rows][hi n | lo n]: the GEMM's activation pairs (hi = fp16(v), lo = fp16(v - hi)).
 int rmsnorm_h(const float* x, const float* w, __half* out, int rows, int n, float eps, cudaStream_t s);

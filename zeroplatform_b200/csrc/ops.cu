@@ -6,9 +6,12 @@
 //   swiglu     SwiGLU.Forward            (Layers/SwiGLU.cs:13-51): (g * sigmoid(g)) * up
 //   silu       TensorOps SiLU            (ZeroTensor bridge zc_silu_f32)
 //   embed      LlmEngine.LookupTokenEmbedding for Q8_0 tables (Engine/LlmEngine.cs:317-345)
+//   copy_words the host-pointer entries' zero-copy transfers (pinned, mapped host buffers)
 // All are HBM/latency bound element-wise kernels.
 
 #include <math.h>
+
+#include <algorithm>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -176,6 +179,35 @@ inline int grid_for(size_t n, int threads) {
 inline int launched() { return cudaPeekAtLastError() == cudaSuccess ? kOk : kCudaError; }
 
 }  // namespace
+
+namespace {
+
+// dst[0, bytes) = src[0, bytes): 16-byte words, then the 4-byte tail.  Either side may be pinned host memory
+// mapped into the device's address space (the host-pointer entries' zero-copy activations and results).
+__global__ void copy_words_kernel(const int4* __restrict__ src, int4* __restrict__ dst, size_t n16,
+                                  const uint32_t* __restrict__ tsrc, uint32_t* __restrict__ tdst, int ntail) {
+  pdl_trigger();
+  pdl_wait();
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n16; i += (size_t)gridDim.x * blockDim.x)
+    dst[i] = src[i];
+  if (blockIdx.x == 0 && (int)threadIdx.x < ntail) tdst[threadIdx.x] = tsrc[threadIdx.x];
+}
+
+}  // namespace
+
+int copy_words(const void* src, void* dst, size_t bytes, cudaStream_t s) {
+  if (!src || !dst || bytes % 4 || (reinterpret_cast<uintptr_t>(src) & 15) || (reinterpret_cast<uintptr_t>(dst) & 15))
+    return kBadArgument;
+  if (bytes == 0) return kOk;
+  const size_t n16 = bytes / 16;
+  const int ntail = (int)(bytes % 16) / 4;
+  const unsigned grid = (unsigned)std::max<size_t>(1, std::min<size_t>((n16 + 127) / 128, 148));
+  return launch_pdl(copy_words_kernel, dim3(grid), dim3(128), 0, s, static_cast<const int4*>(src),
+                    static_cast<int4*>(dst), n16, static_cast<const uint32_t*>(src) + n16 * 4,
+                    static_cast<uint32_t*>(dst) + n16 * 4, ntail) == cudaSuccess
+             ? kOk
+             : kCudaError;
+}
 
 int rmsnorm(const float* x, const float* w, float* out, int rows, int n, float eps, cudaStream_t s) {
   if (!x || !w || !out || rows < 0 || n <= 0) return kBadArgument;
