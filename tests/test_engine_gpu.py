@@ -54,7 +54,7 @@ def test_kv_cache_accounting_matches_reference_allocator():
     assert e.seq_len(101) == 0 and e.free_pages() == 16
 
 
-@pytest.mark.parametrize("heads,kv_heads,dim,ffn", [(12, 12, 768, 2048), (8, 2, 512, 1024)])
+@pytest.mark.parametrize("heads,kv_heads,dim,ffn", [(12, 12, 768, 2048), (8, 2, 512, 1024), (32, 32, 4096, 512)])
 def test_prefill_and_decode_logits_match_oracle(heads, kv_heads, dim, ffn):
     m = O.make_model(vocab=4096, dim=dim, layers=3, heads=heads, kv_heads=kv_heads, ffn=ffn, seed=11)
     e = _engine(m)

@@ -18,10 +18,11 @@ pytestmark = pytest.mark.gpu
 TOL = 3e-4
 
 # (32768, 4096) is large enough (>= 64 MB of weights) for the streaming form (int16 activations, DP2A, L2
-# prefetch); the others run the fp32-activation form, K > 8192 in segments.
+# prefetch); the others run the fp32-activation forms: Q8_0 rows of K = 4096 the slab form (7 rows a CTA, 4 in
+# registers and 3 bulk-copied: 10 and 13 rows leave partial CTAs), K > 8192 in segments.
 SHAPES = [(1, 32), (3, 64), (17, 96), (1023, 768), (2304, 768), (4096, 4096), (768, 2048), (4096, 11008),
           (11008, 4096), (257, 14336), (33, 20480), (64, 1056), (40, 2080), (150, 256), (149, 512), (2, 4096),
-          (32768, 4096)]
+          (10, 4096), (13, 4096), (32768, 4096)]
 
 
 def _case(qtype, rows, cols, seed):

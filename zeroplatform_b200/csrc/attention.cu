@@ -19,6 +19,8 @@
 
 #include <math.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -302,7 +304,11 @@ int paged_attention_choose_splits(int batch, int hkv, int max_ctx, int page_size
   if (max_ctx <= 0 || page_size <= 0) return 1;
   const int n_pages = (max_ctx + page_size - 1) / page_size;
   const int ctas = batch * hkv;
-  const int want = (2 * 148 + ctas - 1) / ctas;  // about two CTAs per SM
+  // Enough CTAs to keep HBM busy: the fp16 kernel needs about 7 resident CTAs per SM (1000 on 148 SMs) once
+  // the batch itself supplies many (a tensor-parallel rank's share of the heads); small batches get at least
+  // two CTAs per SM
+  const int target = std::max(2 * 148, std::min(1000, 8 * ctas));
+  const int want = (target + ctas - 1) / ctas;
   int splits = want < 1 ? 1 : want;
   if (splits > n_pages) splits = n_pages;
   if (splits > 64) splits = 64;

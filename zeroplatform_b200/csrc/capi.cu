@@ -686,7 +686,9 @@ int32_t zcu_device_status(int32_t reset) {
   if (cudaDeviceSynchronize() != cudaSuccess || cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
     return cuda_fail(cudaGetLastError(), "reading the device status word");
   if (reset && v) cudaMemset(p, 0, sizeof(int));
-  return v;
+  const int g = gemv_wait_status(reset);
+  if (g < 0) return g;
+  return v ? v : g;
 }
 
 int32_t zcu_paged_attention(const float* q, const void* k_pool, const void* v_pool, int32_t kv_dtype,

@@ -661,9 +661,13 @@ int32_t zcu_engine_create_tp(const zcu_engine_config* cfg, int32_t tp_size, int3
   }
   if (rc == kOk && tp_size > 1) {
     // the residual all-reduce of decode steps (up to max_batch rows) goes over peer memory when the GPUs have
-    // peer access; larger ones (prefill) and systems without it use NCCL
+    // peer access; larger ones (prefill) and systems without it use NCCL.  ZCU_TP_ALLREDUCE=nccl keeps every
+    // all-reduce on NCCL (set it on every rank).
     std::string err;
-    if (arp_create(E->comm, (size_t)c.max_batch * c.dim, E->status, &E->arp, &err) != kOk) E->arp = nullptr;
+    const char* ar = std::getenv("ZCU_TP_ALLREDUCE");
+    const bool want_p2p = !(ar && std::string(ar) == "nccl");
+    if (!want_p2p || arp_create(E->comm, (size_t)c.max_batch * c.dim, E->status, &E->arp, &err) != kOk)
+      E->arp = nullptr;
     // every rank must take the same path: keep the peer all-reduce only if all ranks could map their peers
     float* ok = nullptr;
     if (cudaMalloc(&ok, sizeof(float)) == cudaSuccess) {

@@ -23,6 +23,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "sync.cuh"
 
 namespace zc {
 
@@ -395,6 +396,126 @@ __global__ void __launch_bounds__(GEMV_THREADS, R == 1 ? GEMV_MIN_CTAS : GEMV_MI
   }
 }
 
+// Error word of the slab form's bounded waits (0 = healthy); read and cleared through gemv_wait_status().
+__device__ int g_gemv_status;
+
+// Sum over the 32 lanes of each of 8 values with 9 shuffles (a transposed butterfly: each level halves the
+// values a lane carries).  Lane l ends with the sum of value (l >> 4 & 1) * 4 + (l >> 3 & 1) * 2 + (l >> 2 & 1).
+__device__ __forceinline__ float transposed_sum8(const float (&p)[8], int lane) {
+  const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+  float q4[4], q2[2];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float send = b4 ? p[i] : p[i + 4], keep = b4 ? p[i + 4] : p[i];
+    q4[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float send = b3 ? q4[i] : q4[i + 2], keep = b3 ? q4[i + 2] : q4[i];
+    q2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  float q1 = (b2 ? q2[1] : q2[0]) + __shfl_xor_sync(0xffffffffu, b2 ? q2[0] : q2[1], 4);
+  q1 += __shfl_xor_sync(0xffffffffu, q1, 2);
+  return q1 + __shfl_xor_sync(0xffffffffu, q1, 1);
+}
+
+// 16 int8 weights (one 16-byte chunk) . 16 fp32 activations, exact conversion, packed FMAs
+__device__ __forceinline__ float dot16_regs(const int4& w, const float2 (&x)[8]) {
+  const float2 bias = f2(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
+  const uint32_t* wv = reinterpret_cast<const uint32_t*>(&w);
+  float2 s = f2(0.f, 0.f);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float2 p01, p23;
+    bytes_to_f2(wv[j] ^ 0x80808080u, bias, p01, p23);
+    s = __ffma2_rn(p01, x[2 * j], s);
+    s = __ffma2_rn(p23, x[2 * j + 1], s);
+  }
+  return s.x + s.y;
+}
+
+// Slab form of the decode-chain Q8_0 GEMV for K == 4096 (d_model of the 7B-class shapes).  Warp w owns the
+// columns [512 w, 512 w + 512) of every row of its CTA, so each lane keeps its 16 activations in registers (x is
+// never staged in shared memory).  A CTA owns SLAB_ROWS = 7 rows: SLAB_REG = 4 stream into registers (one 16-byte
+// load per lane and row) and SLAB_SMEM = 3 are bulk-copied into shared memory by one thread, all issued before
+// griddepcontrol.wait.  Row sums leave each warp through the transposed butterfly and the 8 warps' slab sums
+// are added in warp order in shared memory.  At most 64 registers: four CTAs per SM.
+constexpr int SLAB_K = 4096, SLAB_REG = 4, SLAB_SMEM = 3, SLAB_ROWS = SLAB_REG + SLAB_SMEM;
+
+template <class XP>
+__global__ void __launch_bounds__(GEMV_THREADS, 4)
+    gemv_slab_kernel(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, XP xp, float* __restrict__ y,
+                     int N, int accumulate) {
+  constexpr int K = SLAB_K, KB = K / QK;
+  static_assert(GEMV_WARPS * 32 * 16 == K, "one 16-value chunk per lane covers a row");
+  __shared__ __align__(128) uint8_t srow[SLAB_SMEM][K];
+  __shared__ __align__(16) uint16_t ssc[SLAB_SMEM][KB];
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ float red[GEMV_WARPS][8];
+  __shared__ float xred[GEMV_WARPS + 1];
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = warp * 32 + lane;  // this lane's chunk: columns [16 c, 16 c + 16)
+  const int r0 = blockIdx.x * SLAB_ROWS;
+  const int nrows = min(SLAB_ROWS, N - r0);
+  const int nreg = min(SLAB_REG, nrows), nsm = nrows - nreg;
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    mbar_init(smem_u32(&bar), 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_trigger();
+  if (threadIdx.x == 0) {
+    mbar_arrive_tx(smem_u32(&bar), (uint32_t)nsm * (K + KB * 2));
+    for (int j = 0; j < nsm; ++j) {
+      const size_t row = (size_t)(r0 + nreg + j);
+      bulk_g2s(smem_u32(srow[j]), qs + row * K, K, smem_u32(&bar));
+      bulk_g2s(smem_u32(ssc[j]), dsc + row * KB, KB * 2, smem_u32(&bar));
+    }
+  }
+  int4 w[SLAB_REG];
+  float sc[SLAB_REG];
+#pragma unroll
+  for (int r = 0; r < SLAB_REG; ++r) {
+    const bool ok = r < nreg;
+    w[r] = ok ? ld_stream_v4(qs + (size_t)(r0 + r) * K + (size_t)c * 16) : make_int4(0, 0, 0, 0);
+    sc[r] = ok ? h2f(__ldg(dsc + (size_t)(r0 + r) * KB + (c >> 1))) : 0.f;
+  }
+  pdl_wait();  // x (and y when accumulating) may come from the previous kernel
+  xp.prepare(xred);
+  float2 xr[8];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float4 v = xp.get4(c * 16 + 4 * j, xred);
+    xr[2 * j] = f2(v.x, v.y);
+    xr[2 * j + 1] = f2(v.z, v.w);
+  }
+  float p[8];
+#pragma unroll
+  for (int r = 0; r < SLAB_REG; ++r) p[r] = sc[r] * dot16_regs(w[r], xr);
+  const bool ok = nsm == 0 || mbar_wait(smem_u32(&bar), 0, &abort_flag, &g_gemv_status, 31);
+#pragma unroll
+  for (int j = 0; j < SLAB_SMEM; ++j) {
+    p[SLAB_REG + j] = 0.f;
+    if (ok && j < nsm)
+      p[SLAB_REG + j] = h2f(ssc[j][c >> 1]) * dot16_regs(*reinterpret_cast<const int4*>(&srow[j][c * 16]), xr);
+  }
+#pragma unroll
+  for (int r = SLAB_ROWS; r < 8; ++r) p[r] = 0.f;
+  const float v = transposed_sum8(p, lane);
+  const int row = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+  if ((lane & 3) == 0 && row < SLAB_ROWS) red[warp][row] = v;
+  __syncthreads();
+  if ((int)threadIdx.x < nrows && ok) {
+    float t = 0.f;
+#pragma unroll
+    for (int q = 0; q < GEMV_WARPS; ++q) t += red[q][threadIdx.x];
+    float* yo = y + r0 + threadIdx.x;
+    *yo = accumulate ? *yo + t : t;
+  }
+}
+
 // QT = 8: Q8_0 rows (K bytes, 16-value chunks); QT = 4: Q4_0 rows (K / 2 bytes, one 32-value block per chunk).
 // CTA c owns the contiguous rows [c * N / G, (c + 1) * N / G) (G = grid size).  When K fits one staged
 // segment each warp walks the CTA's rows in batches of R rows, x is staged once, and the first batch is
@@ -571,6 +692,12 @@ static int launch_gemv(const uint8_t* qs, const uint16_t* d, const XP& xp, float
   };
   const int fsmem = len * 4;
   if constexpr (QT == 8) {
+    const bool aligned = !(reinterpret_cast<uintptr_t>(qs) & 15) && !(reinterpret_cast<uintptr_t>(d) & 15);
+    if (!stream && k == SLAB_K && aligned)
+      return launch_pdl(gemv_slab_kernel<XP>, dim3((n + SLAB_ROWS - 1) / SLAB_ROWS), dim3(GEMV_THREADS), 0, s, qs, d,
+                        xp, y, n, accumulate) == cudaSuccess
+                 ? kOk
+                 : kCudaError;
     if (stream) {
       if (nch > 128) return go(gemv_kernel<QT, 1, 8, XP>, 1, smem);
       if (nch > 64) return go(gemv_kernel<QT, 2, 4, XP>, 2, smem);
@@ -615,6 +742,16 @@ int gemv_q8_0_swiglu(const int8_t* qs, const uint16_t* d, const float* gate_up, 
                      int accumulate, cudaStream_t s) {
   if (!gate_up) return kBadArgument;
   return launch_q8(qs, d, XSwiGLU{gate_up, k}, y, n, k, accumulate, s);
+}
+
+int gemv_wait_status(int reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_gemv_status, sizeof(int)) != cudaSuccess) return kCudaError;
+  if (reset && v) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_gemv_status, &zero, sizeof(int));
+  }
+  return v;
 }
 
 int gemv_q4_0(const uint8_t* qs, const uint16_t* d, const float* x, float* y, int n, int k, int accumulate,

@@ -19,6 +19,8 @@ int quantize_q4_0(const float* src, uint8_t* dst, size_t n, cudaStream_t s);
 // ---- decode GEMV (gemv.cu): y = W x (accumulate = 0) or y += W x ----
 int gemv_q8_0(const int8_t* qs, const uint16_t* d, const float* x, float* y, int n, int k, int accumulate,
               cudaStream_t s);
+// Error word of the GEMV's bounded waits on its own bulk copies (0 = healthy); reset clears it.
+int gemv_wait_status(int reset);
 int gemv_q4_0(const uint8_t* qs, const uint16_t* d, const float* x, float* y, int n, int k, int accumulate,
               cudaStream_t s);
 // Fused prologues for the decode step: x = RmsNorm(x_raw) * norm_w, or x = SwiGLU(gate_up[0:k], gate_up[k:2k]).
