@@ -1,8 +1,9 @@
 """Prefill / batched Q8_0 GEMM on tcgen05 vs the oracle's token-parallel MatVecMulQ8_0 (LlmEngine.PrefillPrompt).
 
 Tolerance: max|Y - Y_oracle| / max|Y_oracle| <= 1e-3 -- the north-star bound for fp32 outputs.  The tensor
-core consumes fp16(q*d) and x as an fp16 pair (hi = fp16(x), lo = fp16(x - hi): x to about 2^-22) with fp32
-accumulation, so the weights' single fp16 rounding is the only approximation; the measured error is printed.
+core consumes both operands as fp16 pairs (weights hi = fp16(q*d), lo = fp16(q*d - hi); activations hi = fp16(x),
+lo = fp16(x - hi)) with fp32 accumulation, so the products carry ~2^-22 and the result differs from the fp32
+restatement by summation order; the measured error is printed.
 """
 import numpy as np
 import pytest
@@ -66,9 +67,9 @@ def test_gemm_is_deterministic_and_repeatable():
     assert torch.equal(y1, y2)
 
 
-def test_gemm_matches_fp16_rounded_reference_tightly():
-    """With q*d rounded to fp16 exactly as the kernel does (and x exact: the hi / lo pair carries it to ~2^-22),
-    only the fp32 summation order differs."""
+def test_gemm_matches_exact_products_tightly():
+    """The weight and activation hi / lo pairs carry q*d and x to ~2^-22: against float64 sums of the exact
+    products only fp32 summation order differs."""
     from zeroplatform_b200.ops import QuantizedWeight
     rng = np.random.default_rng(2)
     n, k, m = 256, 512, 96
@@ -77,8 +78,8 @@ def test_gemm_matches_fp16_rounded_reference_tightly():
     b = blocks.reshape(n, k // 32, 34)
     d = b[:, :, :2].copy().view(np.float16).astype(np.float32)          # [n, k/32, 1]
     q = b[:, :, 2:].view(np.int8).astype(np.float32)                   # [n, k/32, 32]
-    w16 = (q * d).astype(np.float16).astype(np.float64).reshape(n, k)  # fp16(q*d): single rounding of the exact product
-    ref = x.astype(np.float64) @ w16.T
+    w = (q.astype(np.float64) * d).reshape(n, k)                       # exact q*d
+    ref = x.astype(np.float64) @ w.T
     qw = QuantizedWeight.upload(8, blocks, n, k)
     y = torch.empty((m, n), device="cuda")
     _run(qw, torch.from_numpy(x).cuda(), y)

@@ -5,19 +5,21 @@
 // QuantizedKernels.MatVecMulQ8_0 / MatVecAddQ8_0 (ZeroLlm/src/ZeroLlm.Core/Engine/LlmEngine.cs:208-304,
 // Quantization/QuantizedKernels.cs:190-308) executed as one contraction.
 //
-// Numerics: the weights enter the tensor core as fp16(q * d) -- the exact product rounded once -- and the
-// activations as a pair of fp16 values, hi = fp16(x) and lo = fp16(x - hi) (x to about 2^-22); each k-step
-// issues one MMA against hi and one against lo into the same fp32 TMEM accumulator, so only the weights'
-// fp16 rounding remains (the tensor core has cycles to spare at the batch sizes where that matters most).  (An int8 MMA cannot apply the
-// per-32-value fp16 block scales inside the tensor core, and a CUDA-core epilogue per block would
-// run several times slower than the MMA itself.)
+// Numerics: both operands enter the tensor core as pairs of fp16 values.  Weights: a_hi = fp16(q * d) (the
+// exact product rounded once) and a_lo = fp16(q * d - a_hi) (one fused multiply-add: the residual rounded
+// once); activations: x_hi = fp16(x) and x_lo = fp16(x - x_hi).  Each 16-wide k-step issues three MMAs into the
+// same fp32 TMEM accumulator -- a_hi x_hi + a_hi x_lo + a_lo x_hi -- whose products are exact, so the result
+// carries both operands to about 2^-22 (the dropped a_lo x_lo term is below 2^-22) and differs from the fp32
+// reference only by summation order.  A single fp16(q * d) x fp16(x) product misses the 1e-3 bound on
+// 4096-wide layers.  (An int8 MMA cannot apply the per-32-value fp16 block scales inside the tensor core, and a
+// CUDA-core epilogue per block would run several times slower than the MMA itself.)
 //
 // Structure (one persistent CTA per SM, 16 warps):
 //   warp 0      TMA producer: raw int8 W tiles [128 rows x 256 k] into a shared-memory ring (2-3 deep)
-//   warp 1      MMA issuer: one thread issues 4 x tcgen05.mma.kind::f16 (M=128, N=BN, K=16) per stage
+//   warp 1      MMA issuer: one thread issues 4 x 3 tcgen05.mma.kind::f16 (M=128, N=BN, K=16) per stage
 //   warp 2      TMA producer: activation tiles (fp16, pre-converted) [BN tokens x 64 k], 128B swizzle
-//   warps 4-11  dequantizers: int8 W tile (shared memory) x fp16 block scales -> fp16 q*d in the UMMA
-//               K-major 128B-swizzled layout (fence.proxy.async before signalling the MMA warp)
+//   warps 4-11  dequantizers: int8 W tile (shared memory) x fp16 block scales -> fp16 hi / lo planes of q*d in
+//               the UMMA K-major 128B-swizzled layout (fence.proxy.async before signalling the MMA warp)
 //   warps 12-15 epilogue: tcgen05.ld 32 TMEM columns at a time, coalesced fp32 stores of Y (or of the
 //               split-K partials, summed afterwards in split order by splitk_reduce_kernel)
 // The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue of one tile overlaps the
@@ -44,7 +46,8 @@ constexpr int DQ_THREADS = DQ_WARPS * 32;
 constexpr int DQ_ITEMS = BM * BK / 16 / DQ_THREADS;  // 16-value chunks per dequantizer thread per stage
 constexpr int EPI_WARP0 = 4 + DQ_WARPS;       // first of the four epilogue warps
 constexpr int GEMM_THREADS = (EPI_WARP0 + 4) * 32;
-constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KB of fp16 A per stage
+constexpr int A_PLANE_BYTES = BM * BK * 2;      // 16 KB: one fp16 plane (hi or lo) of A
+constexpr int A_STAGE_BYTES = 2 * A_PLANE_BYTES;  // a stage holds both planes
 constexpr int W_SUB = 4;                    // k-stages per int8 weight tile (one TMA box of 256 bytes x 128 rows)
 constexpr int S_TILE_BYTES = BM * BK * W_SUB / QK * 2;  // fp16 block scales of a weight tile (8 per row)
 // Quantized bytes of a weight tile [128 rows x 256 k]: 32 KB of int8 (Q8_0) or 16 KB of nibbles (Q4_0).
@@ -123,10 +126,20 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// 16 int8 weights (one int4) times the fp16 block scale -> 16 fp16 values (exactly-rounded products).
-__device__ __forceinline__ void dequant16(int4 w, __half2 d2, uint4& lo, uint4& hi) {
+// q (exact fp16 pair) times the block scale -> (hi, lo) = (fp16(q d), fp16(q d - hi)): the fused multiply-add
+// forms q d - hi exactly before its single rounding.
+__device__ __forceinline__ void scale_hl(__half2 q, __half2 d2, uint32_t& hi, uint32_t& lo) {
+  const __half2 h = __hmul2_rn(q, d2);
+  const __half2 l = __hfma2(q, d2, __hneg2(h));
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+// 16 int8 weights (one int4) times the fp16 block scale -> 16 hi and 16 lo fp16 values, as 16-byte chunks of
+// values 0-7 (h0, l0) and 8-15 (h1, l1).
+__device__ __forceinline__ void dequant16(int4 w, __half2 d2, uint4& h0, uint4& h1, uint4& l0, uint4& l1) {
   const uint32_t* wv = reinterpret_cast<const uint32_t*>(&w);
-  uint32_t out[8];
+  uint32_t oh[8], ol[8];
   const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1024 + 128
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
@@ -134,41 +147,40 @@ __device__ __forceinline__ void dequant16(int4 w, __half2 d2, uint4& lo, uint4& 
     // halves 0x64XX = 1024 + XX (exact), pairs (byte0, byte1) and (byte2, byte3)
     const uint32_t p01 = __byte_perm(b, 0x64646464u, 0x5140);
     const uint32_t p23 = __byte_perm(b, 0x64646464u, 0x7362);
-    __half2 h01 = __hsub2(*reinterpret_cast<const __half2*>(&p01), bias);  // exact q
-    __half2 h23 = __hsub2(*reinterpret_cast<const __half2*>(&p23), bias);
-    h01 = __hmul2_rn(h01, d2);
-    h23 = __hmul2_rn(h23, d2);
-    out[2 * j] = *reinterpret_cast<uint32_t*>(&h01);
-    out[2 * j + 1] = *reinterpret_cast<uint32_t*>(&h23);
+    scale_hl(__hsub2(*reinterpret_cast<const __half2*>(&p01), bias), d2, oh[2 * j], ol[2 * j]);  // exact q first
+    scale_hl(__hsub2(*reinterpret_cast<const __half2*>(&p23), bias), d2, oh[2 * j + 1], ol[2 * j + 1]);
   }
-  lo = make_uint4(out[0], out[1], out[2], out[3]);
-  hi = make_uint4(out[4], out[5], out[6], out[7]);
+  h0 = make_uint4(oh[0], oh[1], oh[2], oh[3]);
+  h1 = make_uint4(oh[4], oh[5], oh[6], oh[7]);
+  l0 = make_uint4(ol[0], ol[1], ol[2], ol[3]);
+  l1 = make_uint4(ol[4], ol[5], ol[6], ol[7]);
 }
 
-// Four nibbles (one per byte, 0..15) -> two half2 of (u - 8) * d.
-__device__ __forceinline__ void nib4(uint32_t u, __half2 d2, uint32_t& p0, uint32_t& p1) {
+// Four nibbles (one per byte, 0..15) -> two half2 of (u - 8) * d, hi and lo.
+__device__ __forceinline__ void nib4(uint32_t u, __half2 d2, uint32_t& h0, uint32_t& h1, uint32_t& l0, uint32_t& l1) {
   const __half2 bias = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));  // 1024 + 8
   const uint32_t a = __byte_perm(u, 0x64646464u, 0x5140);
   const uint32_t b = __byte_perm(u, 0x64646464u, 0x7362);
-  __half2 h0 = __hmul2_rn(__hsub2(*reinterpret_cast<const __half2*>(&a), bias), d2);  // exact u - 8, then * d
-  __half2 h1 = __hmul2_rn(__hsub2(*reinterpret_cast<const __half2*>(&b), bias), d2);
-  p0 = *reinterpret_cast<uint32_t*>(&h0);
-  p1 = *reinterpret_cast<uint32_t*>(&h1);
+  scale_hl(__hsub2(*reinterpret_cast<const __half2*>(&a), bias), d2, h0, l0);  // exact u - 8, then * d
+  scale_hl(__hsub2(*reinterpret_cast<const __half2*>(&b), bias), d2, h1, l1);
 }
 
-// One Q4_0 block (16 bytes: byte j = value j | value j+16 << 4) times its scale -> 32 fp16 values as four
-// 16-byte chunks (values 0-7, 8-15, 16-23, 24-31).
-__device__ __forceinline__ void dequant32_q4(int4 w, __half2 d2, uint4 (&c)[4]) {
+// One Q4_0 block (16 bytes: byte j = value j | value j+16 << 4) times its scale -> 32 hi and 32 lo fp16 values
+// as four 16-byte chunks each (values 0-7, 8-15, 16-23, 24-31).
+__device__ __forceinline__ void dequant32_q4(int4 w, __half2 d2, uint4 (&ch)[4], uint4 (&cl)[4]) {
   const uint32_t m = 0x0F0F0F0Fu;
   const uint32_t wv[4] = {(uint32_t)w.x, (uint32_t)w.y, (uint32_t)w.z, (uint32_t)w.w};
-  uint32_t o[16];
+  uint32_t oh[16], ol[16];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    nib4(wv[j] & m, d2, o[2 * j], o[2 * j + 1]);             // values 4j .. 4j+3
-    nib4((wv[j] >> 4) & m, d2, o[8 + 2 * j], o[8 + 2 * j + 1]);  // values 16+4j .. 16+4j+3
+    nib4(wv[j] & m, d2, oh[2 * j], oh[2 * j + 1], ol[2 * j], ol[2 * j + 1]);  // values 4j .. 4j+3
+    nib4((wv[j] >> 4) & m, d2, oh[8 + 2 * j], oh[8 + 2 * j + 1], ol[8 + 2 * j], ol[8 + 2 * j + 1]);  // 16+4j ..
   }
 #pragma unroll
-  for (int q = 0; q < 4; ++q) c[q] = make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+  for (int q = 0; q < 4; ++q) {
+    ch[q] = make_uint4(oh[4 * q], oh[4 * q + 1], oh[4 * q + 2], oh[4 * q + 3]);
+    cl[q] = make_uint4(ol[4 * q], ol[4 * q + 1], ol[4 * q + 2], ol[4 * q + 3]);
+  }
 }
 
 // QT = 8: Q8_0 weights (int8 tiles); QT = 4: Q4_0 weights (nibble tiles, one 32-value block per dequant item).
@@ -186,7 +198,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const int WSTAGES = p.w_stages;
   const int b_tile_bytes = bn * BK * 2;         // one fp16 activation tile (hi or lo)
   const int b_stage_bytes = 2 * b_tile_bytes;   // hi tile, then lo tile
-  uint8_t* a_st = smem;                                  // AST x 16 KB (fp16 A, SW128)
+  uint8_t* a_st = smem;                                  // AST x 2 x 16 KB (fp16 A hi, lo planes; SW128)
   uint8_t* b_st = a_st + AST * A_STAGE_BYTES;            // AST x 2 x bn*128 B (fp16 X hi, lo; SW128 by TMA)
   uint8_t* w_st = b_st + AST * b_stage_bytes;            // WSTAGES x 8 KB (int8 W, TMA, unswizzled)
   uint64_t* bars = reinterpret_cast<uint64_t*>(w_st + WSTAGES * W_STAGE_BYTES);
@@ -312,9 +324,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           const uint32_t b_addr = smem_u32(b_st + s * b_stage_bytes);
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint64_t adesc = umma_desc_sw128(a_addr + kk * 32);
-            umma_f16(d_tmem, adesc, umma_desc_sw128(b_addr + kk * 32), idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
-            umma_f16(d_tmem, adesc, umma_desc_sw128(b_addr + b_tile_bytes + kk * 32), idesc, 1u);  // x's lo part
+            const uint64_t ahi = umma_desc_sw128(a_addr + kk * 32);
+            const uint64_t bhi = umma_desc_sw128(b_addr + kk * 32);
+            umma_f16(d_tmem, ahi, bhi, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
+            umma_f16(d_tmem, ahi, umma_desc_sw128(b_addr + b_tile_bytes + kk * 32), idesc, 1u);  // a_hi x_lo
+            umma_f16(d_tmem, umma_desc_sw128(a_addr + A_PLANE_BYTES + kk * 32), bhi, idesc, 1u);  // a_lo x_hi
           }
           umma_commit(smem_u32(&ab_empty[s]));  // frees the A/B stage once these MMAs have read it
           if (++s == AST) {
@@ -387,16 +401,23 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           uint8_t* line = a + (r >> 3) * 1024 + (r & 7) * 128;
           if (QT == 8) {
             const int c = item & 3;
-            uint4 lo, hi;
-            dequant16(cw[j], cd[j], lo, hi);
-            *reinterpret_cast<uint4*>(line + (((2 * c) ^ (r & 7)) << 4)) = lo;
-            *reinterpret_cast<uint4*>(line + (((2 * c + 1) ^ (r & 7)) << 4)) = hi;
+            uint4 h0, h1, l0, l1;
+            dequant16(cw[j], cd[j], h0, h1, l0, l1);
+            const int o0 = ((2 * c) ^ (r & 7)) << 4, o1 = ((2 * c + 1) ^ (r & 7)) << 4;
+            *reinterpret_cast<uint4*>(line + o0) = h0;
+            *reinterpret_cast<uint4*>(line + o1) = h1;
+            *reinterpret_cast<uint4*>(line + A_PLANE_BYTES + o0) = l0;
+            *reinterpret_cast<uint4*>(line + A_PLANE_BYTES + o1) = l1;
           } else {
             const int b = item & 1;
-            uint4 q4[4];
-            dequant32_q4(cw[j], cd[j], q4);
+            uint4 qh[4], ql[4];
+            dequant32_q4(cw[j], cd[j], qh, ql);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) *reinterpret_cast<uint4*>(line + (((4 * b + q) ^ (r & 7)) << 4)) = q4[q];
+            for (int q = 0; q < 4; ++q) {
+              const int o = ((4 * b + q) ^ (r & 7)) << 4;
+              *reinterpret_cast<uint4*>(line + o) = qh[q];
+              *reinterpret_cast<uint4*>(line + A_PLANE_BYTES + o) = ql[q];
+            }
           }
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -529,6 +550,14 @@ static void ring_depths(int qt, int bn, int& ab, int& w) {
   if (ab > MAX_STAGES) ab = MAX_STAGES;
 }
 
+// A tile width is usable when its A/B ring is at least double-buffered (dequantizing one stage while the
+// tensor core reads the other).
+static bool ring_ok(int qt, int bn) {
+  int ab, w;
+  ring_depths(qt, bn, ab, w);
+  return ab >= 2;
+}
+
 // Tile width and split-K for an M x N x K problem.  Cost model: waves of work units on the SMs, each unit
 // costing (its k-stages) x (bn + 64) (the 64 stands for the A-operand traffic every stage pays whatever bn
 // is), plus a small charge per extra split for the partial-sum traffic.  Split-K only when M <= 128 (small
@@ -541,6 +570,7 @@ static GemmConfig choose_config(int m, int n, int k, int qt = 8) {
   const int bns[4] = {32, 64, 128, 256};
   for (int bn : bns) {
     if (bn > 32 && m <= bn / 2) continue;  // a narrower tile already covers every token
+    if (!ring_ok(qt, bn)) continue;
     const int tok_tiles = (m + bn - 1) / bn;
     const int tiles = ((n + BM - 1) / BM) * tok_tiles;
     const int max_s = m <= 128 ? MAX_SPLITS : 1;
