@@ -37,9 +37,9 @@ ALGO_BYTES = QBYTES + COLS * 4 + ROWS * 4        # + x read + y written
 AOS_BYTES = ROWS * (COLS // 32) * 34             # the reference's packed weight bytes
 # Published CPU figure for this exact GEMV (ZeroTensor/README.md:198-203): 3.79 ms for the 17.8 MB weight.
 PUBLISHED_GBS = AOS_BYTES / 3.79e-3 / 1e9
-# dram__bytes_read.sum + dram__bytes_write.sum of one gemv_q8_0_kernel launch of this workload, from the ncu
-# capture summarised in profiles/gemv_q8_0_4096x4096.md (17,873,920 read + 0 written).
-NCU_TRAFFIC_BYTES = 17873920
+# dram__bytes_read.sum + dram__bytes_write.sum of one gemv_slab_kernel launch of this workload, from the ncu
+# capture summarised in profiles/gemv_slab_q8_0_4096x4096.md (17,856,000 read + 0 written).
+NCU_TRAFFIC_BYTES = 17856000
 
 
 def _peaks():
@@ -221,8 +221,8 @@ def prefill_gemm_leg(dev, L, iters=20):
     return {"ms": round(ms, 4), "tflops": round(tf, 1), "weight_GBs": round(w.nbytes / (ms * 1e-3) / 1e9, 1),
             "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak, "unit": "TFLOP/s",
                          "frac": round(tf / peak, 3), "peak_source": src},
-            "note": "fp16(q*d) x fp16(x) on tcgen05 kind::f16, fp32 accumulate; includes the fp32->fp16 "
-                    "activation conversion kernel", "device_status": status}
+            "note": "tcgen05 kind::f16 on fp16 hi/lo pairs of q*d and x (three MMAs per k-step), fp32 "
+                    "accumulate; includes the fp32 -> fp16 hi/lo activation conversion kernel", "device_status": status}
 
 
 def decode_12l_leg(dev, with_cpu, n_prompt=512, n_new=128):
@@ -592,7 +592,7 @@ def run_ours(args):
                 "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                              "frac": round(achieved / peak, 3), "peak_source": peak_kind,
                              "traffic": NCU_TRAFFIC_BYTES, "algorithmic_bytes_per_launch": ALGO_BYTES,
-                             "kernel": "gemv_direct_kernel<8,1,8,XPlain>", "launch_us": round(launch_s * 1e6, 3)},
+                             "kernel": "gemv_slab_kernel<XPlain>", "launch_us": round(launch_s * 1e6, 3)},
                 "e2e": e2e, "e2e_weights_copied_per_call": e2e_copy, "gpu_launches": launches,
                 "clocks": sampler.summary(), "cpu_baseline": cpu, "extra_configs": extra}
         print(json.dumps(line), flush=True)
