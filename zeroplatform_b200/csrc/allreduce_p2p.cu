@@ -58,21 +58,52 @@ struct PeerPtrs {
   unsigned int* flag[ARP_MAX_RANKS];   // each rank's flags [W]
 };
 
-// Both kernels are launched without programmatic dependent launch and never trigger their dependents early:
+// The all-reduce pair is launched without programmatic dependent launch and never triggers its dependents early:
 // a push starts only after everything before it in the stream has completed, and nothing after a reduce starts
 // before it has completed, so the epoch and the arrival counters are never read and written by overlapping grids.
-__global__ void arp_push_kernel(const float* __restrict__ x, size_t n, size_t cap, PeerPtrs peers, int W, int me,
+// The fused pair (arp_push_partials + arp_reduce_rmsnorm_h) uses programmatic dependent launch with the trigger
+// first and griddepcontrol.wait before any read: a dependent grid is launched only once every CTA of its
+// predecessor is resident, so the reduce's spinning CTAs never keep the push's CTAs off the SMs, and each grid
+// still reads the epoch only after its predecessor has completed.
+//
+// Push: slot[me] of every rank's current buffer = sum over s < splits of src[s * stride + i] (+ resid[i]); the
+// last CTA to finish publishes the new epoch into every rank's flag[me].
+template <bool PDL>
+__global__ void arp_push_kernel(const float* __restrict__ src, int splits, size_t stride,
+                                const float* __restrict__ resid, size_t n, size_t cap, PeerPtrs peers, int W, int me,
                                 const unsigned int* __restrict__ epoch, unsigned int* __restrict__ arrivals) {
+  if (PDL) {
+    pdl_trigger();
+    pdl_wait();
+  }
   __shared__ int last;
   const unsigned int e = *epoch + 1;
   const size_t buf = (size_t)(e & 1) * W * cap;
   const size_t n4 = n / 4;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
-    const float4 v = reinterpret_cast<const float4*>(x)[i];
+    float4 v = reinterpret_cast<const float4*>(src)[i];
+    for (int sp = 1; sp < splits; ++sp) {
+      const float4 u = reinterpret_cast<const float4*>(src + (size_t)sp * stride)[i];
+      v.x += u.x;
+      v.y += u.y;
+      v.z += u.z;
+      v.w += u.w;
+    }
+    if (resid) {  // y += W x on the rank that carries the residual: the sum of the splits, then the add
+      const float4 u = reinterpret_cast<const float4*>(resid)[i];
+      v.x = u.x + v.x;
+      v.y = u.y + v.y;
+      v.z = u.z + v.z;
+      v.w = u.w + v.w;
+    }
     for (int r = 0; r < W; ++r) reinterpret_cast<float4*>(peers.data[r] + buf + (size_t)me * cap)[i] = v;
   }
-  for (size_t i = n4 * 4 + blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-    for (int r = 0; r < W; ++r) peers.data[r][buf + (size_t)me * cap + i] = x[i];
+  for (size_t i = n4 * 4 + blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    float v = src[i];
+    for (int sp = 1; sp < splits; ++sp) v += src[(size_t)sp * stride + i];
+    if (resid) v = resid[i] + v;
+    for (int r = 0; r < W; ++r) peers.data[r][buf + (size_t)me * cap + i] = v;
+  }
   // the last CTA publishes the epoch once every CTA's stores are visible system-wide
   __threadfence_system();
   __syncthreads();
@@ -85,30 +116,86 @@ __global__ void arp_push_kernel(const float* __restrict__ x, size_t n, size_t ca
   }
 }
 
-__global__ void arp_reduce_kernel(float* __restrict__ x, size_t n, size_t cap, const float* __restrict__ area,
-                                  const unsigned int* __restrict__ flags, int W, unsigned int* __restrict__ epoch,
-                                  unsigned int* __restrict__ departures, int* __restrict__ status) {
-  __shared__ int ok, last;
-  const unsigned int e = *epoch + 1;
-  if (threadIdx.x == 0) {
-    ok = 1;
-    const uint64_t t0 = now_ns();
-    for (int r = 0; r < W && ok; ++r) {
-      uint32_t polls = 0;
-      // a peer may already have published e + 1 (it finished this all-reduce and pushed the next one into the
-      // other buffer), so wait for "at least e", wrap-around safe
-      while ((int)(ld_acquire_sys(flags + r) - e) < 0) {
-        if (++polls > AR_WAIT_POLLS || now_ns() - t0 > AR_WAIT_NS) {
-          ok = 0;
-          atomicExch(status, 21);
-          // what the wait saw, for the host's error message: the epoch it needed and every rank's flag
-          epoch[4] = e;
-          for (int q = 0; q < W; ++q) epoch[5 + q] = flags[q];
-          break;
-        }
+// Thread 0 of the calling CTA waits (bounded) until every rank's flag in this rank's area carries at least the
+// epoch e; returns 0 (and records the failure) when the wait ran out.
+__device__ __forceinline__ int wait_flags(const unsigned int* flags, int W, unsigned int e, unsigned int* state,
+                                          int* status) {
+  const uint64_t t0 = now_ns();
+  for (int r = 0; r < W; ++r) {
+    uint32_t polls = 0;
+    // a peer may already have published e + 1 (it finished this all-reduce and pushed the next one into the
+    // other buffer), so wait for "at least e", wrap-around safe
+    while ((int)(ld_acquire_sys(flags + r) - e) < 0) {
+      if (++polls > AR_WAIT_POLLS || now_ns() - t0 > AR_WAIT_NS) {
+        atomicExch(status, 21);
+        // what the wait saw, for the host's error message: the epoch it needed and every rank's flag
+        state[4] = e;
+        for (int q = 0; q < W; ++q) state[5 + q] = flags[q];
+        return 0;
       }
     }
   }
+  return 1;
+}
+
+// The last CTA to leave advances the epoch (every CTA has read it by then).
+__device__ __forceinline__ void depart(unsigned int* epoch, unsigned int* departures, unsigned int e) {
+  __shared__ int last;
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicAdd(departures, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (last && threadIdx.x == 0) {
+    *departures = 0;
+    *epoch = e;
+  }
+}
+
+// One CTA per row: x[row] = sum over ranks r = 0 .. W-1 of slot[r][row] (the same order on every rank), then
+// out[row] = RmsNorm(x[row]) * w as fp16 hi / lo pairs [hi dim | lo dim] (the operand of the tensor-core GEMM
+// that follows) -- the computation of rmsnorm_kernel<__half> on the reduced row.
+__global__ void arp_reduce_rmsnorm_kernel(float* __restrict__ x, int dim, size_t cap, const float* __restrict__ area,
+                                          const unsigned int* __restrict__ flags, int W, unsigned int* __restrict__ epoch,
+                                          unsigned int* __restrict__ departures, int* __restrict__ status,
+                                          const float* __restrict__ w, float eps, __half* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ int ok;
+  __shared__ float red[32];
+  const unsigned int e = *epoch + 1;
+  if (threadIdx.x == 0) ok = wait_flags(flags, W, e, epoch, status);
+  __syncthreads();
+  if (ok) {
+    const float* buf = area + (size_t)(e & 1) * W * cap + (size_t)blockIdx.x * dim;
+    float* xr = x + (size_t)blockIdx.x * dim;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+      float v = __ldcv(buf + i);
+      for (int r = 1; r < W; ++r) v += __ldcv(buf + (size_t)r * cap + i);
+      xr[i] = v;
+      ss = fmaf(v, v, ss);
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+      v = warp_sum(v);
+      if (threadIdx.x == 0) red[0] = v;
+    }
+    __syncthreads();
+    const float inv = 1.0f / (float)sqrt((double)(red[0] / (float)dim + eps));
+    __half* orow = out + (size_t)blockIdx.x * 2 * dim;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) store_hl(orow + i, (size_t)dim, xr[i] * inv * w[i]);
+  }
+  depart(epoch, departures, e);
+}
+
+__global__ void arp_reduce_kernel(float* __restrict__ x, size_t n, size_t cap, const float* __restrict__ area,
+                                  const unsigned int* __restrict__ flags, int W, unsigned int* __restrict__ epoch,
+                                  unsigned int* __restrict__ departures, int* __restrict__ status) {
+  __shared__ int ok;
+  const unsigned int e = *epoch + 1;
+  if (threadIdx.x == 0) ok = wait_flags(flags, W, e, epoch, status);
   __syncthreads();
   if (ok) {
     const float* buf = area + (size_t)(e & 1) * W * cap;
@@ -130,14 +217,7 @@ __global__ void arp_reduce_kernel(float* __restrict__ x, size_t n, size_t cap, c
       x[i] = s;
     }
   }
-  // the last CTA to leave advances the epoch (every CTA has read it by then)
-  __syncthreads();
-  if (threadIdx.x == 0) last = atomicAdd(departures, 1u) == gridDim.x - 1;
-  __syncthreads();
-  if (last && threadIdx.x == 0) {
-    *departures = 0;
-    *epoch = e;
-  }
+  depart(epoch, departures, e);
 }
 
 }  // namespace
@@ -243,15 +323,39 @@ std::string arp_describe(const P2pAllReduce* A) {
   return m;
 }
 
+static int push_grid(size_t n) { return (int)std::min<size_t>((n / 4 + 255) / 256 + 1, 148 * 2); }
+
 int arp_allreduce_sum(P2pAllReduce* A, float* x, size_t n, cudaStream_t s) {
   if (!A || n > A->cap) return kTooLarge;
   if (n == 0) return kOk;
-  const int threads = 256;
-  const int grid = (int)std::min<size_t>((n / 4 + threads - 1) / threads + 1, 148 * 2);
-  arp_push_kernel<<<grid, threads, 0, s>>>(x, n, A->cap, A->peers, A->W, A->me, A->state, A->state + 1);
+  const int grid = push_grid(n);
+  arp_push_kernel<false><<<grid, 256, 0, s>>>(x, 1, 0, (const float*)nullptr, n, A->cap, A->peers, A->W, A->me,
+                                              A->state, A->state + 1);
   if (cudaPeekAtLastError() != cudaSuccess) return kCudaError;
-  arp_reduce_kernel<<<grid, threads, 0, s>>>(x, n, A->cap, A->area, A->flags, A->W, A->state, A->state + 2, A->status);
+  arp_reduce_kernel<<<grid, 256, 0, s>>>(x, n, A->cap, A->area, A->flags, A->W, A->state, A->state + 2, A->status);
   return cudaPeekAtLastError() == cudaSuccess ? kOk : kCudaError;
+}
+
+int arp_push_partials(P2pAllReduce* A, const float* part, int splits, size_t n, const float* resid, cudaStream_t s) {
+  if (!A || n > A->cap) return kTooLarge;
+  if (!part || splits < 1) return kBadArgument;
+  if (n == 0) return kOk;
+  return launch_pdl(arp_push_kernel<true>, dim3(push_grid(n)), dim3(256), 0, s, part, splits, n, resid, n, A->cap,
+                    A->peers, A->W, A->me, (const unsigned int*)A->state, A->state + 1) == cudaSuccess
+             ? kOk
+             : kCudaError;
+}
+
+int arp_reduce_rmsnorm_h(P2pAllReduce* A, float* x, const float* w, float eps, __half* out, int rows, int dim,
+                         cudaStream_t s) {
+  if (!A || (size_t)rows * dim > A->cap) return kTooLarge;
+  if (!x || !w || !out || rows <= 0 || dim <= 0) return kBadArgument;
+  const int threads = dim >= 1024 ? 512 : (dim >= 256 ? 256 : 128);
+  return launch_pdl(arp_reduce_rmsnorm_kernel, dim3(rows), dim3(threads), 0, s, x, dim, A->cap,
+                    (const float*)A->area, (const unsigned int*)A->flags, A->W, A->state, A->state + 2, A->status, w,
+                    eps, out) == cudaSuccess
+             ? kOk
+             : kCudaError;
 }
 
 }  // namespace zc

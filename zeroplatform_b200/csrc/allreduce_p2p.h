@@ -1,6 +1,7 @@
 // allreduce_p2p.h -- one-shot all-reduce over NVLink peer memory (allreduce_p2p.cu).
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 
@@ -23,5 +24,16 @@ size_t arp_capacity(const P2pAllReduce* a);
 std::string arp_describe(const P2pAllReduce* a);
 // In-place sum of x[0, n) over all ranks (n <= capacity); two kernels on stream s, graph-capturable.
 int arp_allreduce_sum(P2pAllReduce* a, float* x, size_t n, cudaStream_t s);
+
+// The same all-reduce split around the kernels that produce and consume it (tensor-parallel decode steps):
+//   arp_push_partials     this rank's term = sum over s < splits of part[s * n + i] (+ resid[i]), the split-K
+//                         partials of the GEMM before it, stored straight into every rank's slot (no x round trip)
+//   arp_reduce_rmsnorm_h  x[rows][dim] = sum of the ranks' terms, and out = RmsNorm(x) * w as fp16 hi / lo pairs
+//                         [rows][hi dim | lo dim] for the tensor-core GEMM after it
+// Every arp_push_partials must be followed by one arp_reduce_rmsnorm_h (or an arp_allreduce_sum never starts
+// between them); rows * dim = n <= capacity.
+int arp_push_partials(P2pAllReduce* a, const float* part, int splits, size_t n, const float* resid, cudaStream_t s);
+int arp_reduce_rmsnorm_h(P2pAllReduce* a, float* x, const float* w, float eps, __half* out, int rows, int dim,
+                         cudaStream_t s);
 
 }  // namespace zc

@@ -267,6 +267,17 @@ int allreduce_x(Engine* E, int T) {
   return comm_allreduce_sum_f32(E->comm, E->x, n, E->stream, &E->err);
 }
 
+// Tensor-parallel row-split projection whose all-reduce is fused around it: the GEMM leaves its split-K
+// partials, and the push kernel sums them (rank 0 adding the residual x) straight into every rank's all-reduce
+// slot; the caller follows with arp_reduce_rmsnorm_h.
+int linear_push(Engine* E, const DevW& w, int rows) {
+  float* part = nullptr;
+  int splits = 0;
+  E_RC(gemm_q8_0_tc_h_partials(w.qs, w.d, E->xh, E->xh + w.k, 2 * w.k, rows, w.n, w.k, E->gemm_ws, E->gemm_ws_bytes,
+                               E->status, E->stream, &part, &splits));
+  return arp_push_partials(E->arp, part, splits, (size_t)rows * w.n, residual_mode(E) ? E->x : nullptr, E->stream);
+}
+
 // The forward pass over T activation rows already embedded in E->x, with tokens' positions in E->pos and
 // page-table rows in E->rows.  Leaves the last row's logits (or every row's when all_logits) of this rank's
 // vocabulary slice in E->logits.
@@ -279,13 +290,18 @@ int forward(Engine* E, int T, bool all_logits) {
   // kernel before it (RmsNorm, attention, SwiGLU); 1 < T < kGemmMinRows: fp32 GEMVs per row; T == 1: the
   // fused GEMVs.
   const bool tc = T >= kGemmMinRows;
+  // tensor parallel on the tensor cores with rows that fit the peer all-reduce: the Wo / Wdown all-reduces are
+  // fused into the kernels around them (linear_push, then arp_reduce_rmsnorm_h, which also writes the next
+  // RmsNorm's fp16 operand)
+  const bool fused = tc && E->arp && (size_t)T * c.dim <= arp_capacity(E->arp);
+  bool normed = false;  // E->xh already holds the next RmsNorm's output (written by arp_reduce_rmsnorm_h)
   for (int l = 0; l < L; ++l) {
     const float* an = E->attn_norm + (size_t)l * c.dim;
     const float* fn = E->ffn_norm + (size_t)l * c.dim;
     if (T == 1) {
       E_RC(gemv_q8_0_rmsnorm(E->wqkv[l].qs, E->wqkv[l].d, E->x, an, c.eps, E->qkv, E->qkv_dim, c.dim, 0, E->stream));
     } else if (tc) {
-      E_RC(rmsnorm_h(E->x, an, E->xh, T, c.dim, c.eps, E->stream));
+      if (!normed) E_RC(rmsnorm_h(E->x, an, E->xh, T, c.dim, c.eps, E->stream));
       E_RC(linear_h(E, E->wqkv[l], E->xh, E->qkv, T, 0));
     } else {
       E_RC(rmsnorm(E->x, an, E->xn, T, c.dim, c.eps, E->stream));
@@ -296,6 +312,17 @@ int forward(Engine* E, int T, bool all_logits) {
                         E->vpool + (size_t)l * E->layer_pool_elems, E->stream));
     const int32_t* ctx = (c.reference_causal_quirk && l != L - 1) ? E->ctx_ex : E->ctx_in;
     E_RC(attention(E, l, T, ctx, tc));
+    if (fused) {
+      E_RC(linear_push(E, E->wo[l], T));  // x += Wo . attn, summed over ranks
+      E_RC(arp_reduce_rmsnorm_h(E->arp, E->x, fn, c.eps, E->xh, T, c.dim, E->stream));
+      E_RC(linear_h(E, E->wgu[l], E->xh, E->gu, T, 0));
+      E_RC(swiglu_rows_h(E->gu, E->xh, T, E->ffn, E->stream));
+      E_RC(linear_push(E, E->wdown[l], T));  // x += Wdown . s, summed over ranks
+      const float* next_norm = l + 1 < L ? E->attn_norm + (size_t)(l + 1) * c.dim : E->final_norm;
+      E_RC(arp_reduce_rmsnorm_h(E->arp, E->x, next_norm, c.eps, E->xh, T, c.dim, E->stream));
+      normed = true;
+      continue;
+    }
     if (tc)
       E_RC(linear_h(E, E->wo[l], E->xh, E->x, T, acc));  // x += Wo . attn (MatVecAddQ8_0)
     else
@@ -319,7 +346,7 @@ int forward(Engine* E, int T, bool all_logits) {
   }
   if (all_logits && T > 1) {
     if (tc) {
-      E_RC(rmsnorm_h(E->x, E->final_norm, E->xh, T, c.dim, c.eps, E->stream));
+      if (!normed) E_RC(rmsnorm_h(E->x, E->final_norm, E->xh, T, c.dim, c.eps, E->stream));
       E_RC(linear_h(E, E->lm_head, E->xh, E->logits, T, 0));
     } else {
       E_RC(rmsnorm(E->x, E->final_norm, E->xn, T, c.dim, c.eps, E->stream));

@@ -601,7 +601,9 @@ static size_t align256(size_t b) { return (b + 255) & ~size_t(255); }
 size_t gemm_q8_0_workspace_bytes(int m, int n, int k) {
   const GemmConfig c = choose_config(m, n, k);
   size_t b = align256((size_t)m * k * 4);  // fp16 [m][hi k | lo k]
-  if (c.splits > 1) b += (size_t)c.splits * m * n * sizeof(float);
+  // split partials; up to M = 128 (decode batches) room for one even without split-K: gemm_*_tc_h_partials
+  // leaves a single-split result there
+  if (c.splits > 1 || m <= 128) b += (size_t)std::max(c.splits, 1) * m * n * sizeof(float);
   return b;
 }
 
@@ -613,13 +615,25 @@ size_t gemm_workspace_max(int m_max, int n, int k) {
 }
 
 // Core launcher on fp16 activations x16 [m][k] (16-byte aligned rows); QT = 8 (Q8_0) or 4 (Q4_0) weights.
+// partials != nullptr: no reduction -- the products stay in the workspace as *nsplit partials [m][n]
+// (*partials, one or more, summed in split order by the caller); y and accumulate are then unused.
 template <int QT>
 static int launch_gemm(const void* qs, const uint16_t* d, const __half* x_hi, const __half* x_lo, int ldx, float* y,
-                       int m, int n, int k, int accumulate, char* ws, int* status, cudaStream_t s) {
+                       int m, int n, int k, int accumulate, char* ws, int* status, cudaStream_t s,
+                       float** partials = nullptr, int* nsplit = nullptr) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return kCudaError;
   const GemmConfig c = choose_config(m, n, k, QT);
   float* part = reinterpret_cast<float*>(ws + align256((size_t)m * k * 4));
+  if (partials) {
+    if (m > 128 && c.splits == 1) return kUnsupported;  // no partial space reserved (see the workspace rule)
+    *partials = part;
+    *nsplit = c.splits;
+    if (c.splits == 1) {  // the single split writes its result straight into the partial slot
+      y = part;
+      accumulate = 0;
+    }
+  }
   CUtensorMap xmap, xlmap, wmap;
   for (int half = 0; half < 2; ++half) {  // the hi and the lo values of x: [m][k] each, row pitch ldx elements
     cuuint64_t gdim[2] = {(cuuint64_t)k, (cuuint64_t)m};
@@ -681,7 +695,7 @@ static int launch_gemm(const void* qs, const uint16_t* d, const __half* x_hi, co
   if (launch_pdl(gemm_q8_0_tc_kernel<QT>, dim3(grid), dim3(GEMM_THREADS), (size_t)smem, s, xmap, xlmap, wmap, smap,
                  p) != cudaSuccess)
     return kCudaError;
-  if (c.splits > 1) {
+  if (c.splits > 1 && !partials) {
     const size_t mn = (size_t)m * n;
     if (launch_pdl(splitk_reduce_kernel, dim3((unsigned)std::min<size_t>((mn + 255) / 256, 148 * 8)), dim3(256), 0,
                    s, (const float*)part, y, mn, c.splits, accumulate) != cudaSuccess)
@@ -737,6 +751,17 @@ int gemm_q4_0_tc(const uint8_t* qs, const uint16_t* d, const float* x, float* y,
   if (convert_x(x, ws, m, k, s) != kOk) return kCudaError;
   const __half* x16 = reinterpret_cast<const __half*>(ws);
   return launch_gemm<4>(qs, d, x16, x16 + k, 2 * k, y, m, n, k, accumulate, ws, status, s);
+}
+
+int gemm_q8_0_tc_h_partials(const int8_t* qs, const uint16_t* d, const __half* x_hi, const __half* x_lo, int ldx,
+                            int m, int n, int k, void* workspace, size_t workspace_bytes, int* status, cudaStream_t s,
+                            float** partials, int* nsplit) {
+  if (!partials || !nsplit) return kBadArgument;
+  const int rc = check_gemm_args(qs, d, x_hi, x_hi, m, n, k, workspace, workspace_bytes, status);
+  if (rc != kOk) return rc;
+  if ((reinterpret_cast<uintptr_t>(x_lo) & 15) || (ldx * 2) % 16) return kUnsupported;
+  return launch_gemm<8>(qs, d, x_hi, x_lo, ldx, nullptr, m, n, k, 0, static_cast<char*>(workspace), status, s,
+                        partials, nsplit);
 }
 
 int gemm_q4_0_tc_h(const uint8_t* qs, const uint16_t* d, const __half* x_hi, const __half* x_lo, int ldx, float* y,

@@ -39,6 +39,13 @@ int gemm_q8_0_tc(const int8_t* qs, const uint16_t* d, const float* x, float* y, 
 int gemm_q8_0_tc_h(const int8_t* qs, const uint16_t* d, const __half* x_hi, const __half* x_lo, int ldx, float* y,
                    int m, int n, int k, int accumulate, void* workspace, size_t workspace_bytes, int* status,
                    cudaStream_t s);
+// The same GEMM without its split-K reduction (m <= 128): the products are left in the workspace as *nsplit >= 1
+// partials [m][n] starting at *partials, for a consumer that sums them in split order (the tensor-parallel
+// all-reduce push).  Stream-ordered like the other entries; the partials live until the next call on the
+// workspace.
+int gemm_q8_0_tc_h_partials(const int8_t* qs, const uint16_t* d, const __half* x_hi, const __half* x_lo, int ldx,
+                            int m, int n, int k, void* workspace, size_t workspace_bytes, int* status, cudaStream_t s,
+                            float** partials, int* nsplit);
 // Q4_0 weights (SoA nibbles [N][K/32][16] + fp16 scales), same workspace size rule.
 int gemm_q4_0_tc(const uint8_t* qs, const uint16_t* d, const float* x, float* y, int m, int n, int k, int accumulate,
                  void* workspace, size_t workspace_bytes, int* status, cudaStream_t s);
