@@ -61,10 +61,11 @@ struct PeerPtrs {
 // The all-reduce pair is launched without programmatic dependent launch and never triggers its dependents early:
 // a push starts only after everything before it in the stream has completed, and nothing after a reduce starts
 // before it has completed, so the epoch and the arrival counters are never read and written by overlapping grids.
-// The fused pair (arp_push_partials + arp_reduce_rmsnorm_h) uses programmatic dependent launch with the trigger
-// first and griddepcontrol.wait before any read: a dependent grid is launched only once every CTA of its
-// predecessor is resident, so the reduce's spinning CTAs never keep the push's CTAs off the SMs, and each grid
-// still reads the epoch only after its predecessor has completed.
+// The fused pair (arp_push_partials + arp_reduce_rmsnorm_h) is launched with programmatic dependent launch and
+// waits (griddepcontrol.wait) before any read.  The push triggers its dependent first: the reduce's grid is
+// launched only once every CTA of the push is resident, so its spinning CTAs never keep the push's CTAs off the
+// SMs.  The reduce never triggers: like the plain pair, nothing after it starts before it has completed and
+// advanced the epoch.
 //
 // Push: slot[me] of every rank's current buffer = sum over s < splits of src[s * stride + i] (+ resid[i]); the
 // last CTA to finish publishes the new epoch into every rank's flag[me].
@@ -77,7 +78,7 @@ __global__ void arp_push_kernel(const float* __restrict__ src, int splits, size_
     pdl_wait();
   }
   __shared__ int last;
-  const unsigned int e = *epoch + 1;
+  const unsigned int e = *reinterpret_cast<const volatile unsigned int*>(epoch) + 1;
   const size_t buf = (size_t)(e & 1) * W * cap;
   const size_t n4 = n / 4;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
@@ -157,11 +158,10 @@ __global__ void arp_reduce_rmsnorm_kernel(float* __restrict__ x, int dim, size_t
                                           const unsigned int* __restrict__ flags, int W, unsigned int* __restrict__ epoch,
                                           unsigned int* __restrict__ departures, int* __restrict__ status,
                                           const float* __restrict__ w, float eps, __half* __restrict__ out) {
-  pdl_trigger();
   pdl_wait();
   __shared__ int ok;
   __shared__ float red[32];
-  const unsigned int e = *epoch + 1;
+  const unsigned int e = *reinterpret_cast<volatile unsigned int*>(epoch) + 1;
   if (threadIdx.x == 0) ok = wait_flags(flags, W, e, epoch, status);
   __syncthreads();
   if (ok) {
@@ -194,7 +194,7 @@ __global__ void arp_reduce_kernel(float* __restrict__ x, size_t n, size_t cap, c
                                   const unsigned int* __restrict__ flags, int W, unsigned int* __restrict__ epoch,
                                   unsigned int* __restrict__ departures, int* __restrict__ status) {
   __shared__ int ok;
-  const unsigned int e = *epoch + 1;
+  const unsigned int e = *reinterpret_cast<volatile unsigned int*>(epoch) + 1;
   if (threadIdx.x == 0) ok = wait_flags(flags, W, e, epoch, status);
   __syncthreads();
   if (ok) {
