@@ -601,9 +601,39 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def gemm_leg(dev, m, n, k, iters=5):
+    """One Q8_0 tensor-core GEMM shape alone (seeded N(0,0.02) weights, N(0,1) activations), `iters` calls of
+    zcu_gemm_q8_0 timed together -- the small command the GEMM profiles capture."""
+    import torch
+    from zeroplatform_b200 import _lib
+    from zeroplatform_b200.ops import QuantizedWeight, quantize
+    L = _lib.lib()
+    g = torch.Generator(device=dev)
+    g.manual_seed(1)
+    w = QuantizedWeight.upload(8, quantize(8, torch.randn((n, k), generator=g, device=dev) * 0.02), n, k, device=dev)
+    x = torch.randn((m, k), generator=g, device=dev)
+    y = torch.empty((m, n), device=dev)
+    s = torch.cuda.current_stream()
+
+    def call():
+        if L.zcu_gemm_q8_0(w.qs.data_ptr(), w.d.data_ptr(), x.data_ptr(), y.data_ptr(), m, n, k, 0, s.cuda_stream):
+            raise RuntimeError("zcu_gemm_q8_0 failed")
+    call()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(iters):
+        call()
+    e1.record(s)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / iters
+    return {"us": round(us, 2), "tflops": round(2.0 * m * n * k / us / 1e6, 1),
+            "weight_GBs": round(w.nbytes / us / 1e3, 1), "device_status": L.zcu_device_status(1)}
+
+
 def run_leg(args):
-    """`--leg decode_7b` / `--leg moe`: one extra leg alone, printed as its own JSON line (rank 0).
-    --layers / --new-tokens shrink the decode leg for profiler captures."""
+    """`--leg decode_7b` / `--leg moe` / `--leg gemm --shape M,N,K`: one extra leg alone, printed as its own JSON
+    line (rank 0).  --layers / --new-tokens shrink the decode leg for profiler captures."""
     import torch
     import torch.distributed as dist
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -617,6 +647,10 @@ def run_leg(args):
     if args.leg == "moe":
         res = moe_leg(dev, rank, world)
         name = f"moe_8x14336_top2_ep{world}"
+    elif args.leg == "gemm":
+        m, n, k = (int(v) for v in args.shape.split(","))
+        res = gemm_leg(dev, m, n, k)
+        name = f"gemm_q8_0_{m}x{n}x{k}"
     else:
         res = decode_7b_leg(dev, rank, world, n_new=args.new_tokens, layers=args.layers)
         name = f"decode_7b_b32_tp{world}"
@@ -629,9 +663,10 @@ def run_leg(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--leg", choices=["all", "decode_7b", "moe"], default="all",
+    ap.add_argument("--leg", choices=["all", "decode_7b", "moe", "gemm"], default="all",
                     help="all: the headline and every extra leg; decode_7b: only the 7B tensor-parallel decode; "
-                         "moe: only the expert-parallel MoE layer")
+                         "moe: only the expert-parallel MoE layer; gemm: one GEMM shape (--shape)")
+    ap.add_argument("--shape", default="512,11008,4096", help="gemm: M,N,K")
     ap.add_argument("--layers", type=int, default=32, help="decode_7b: decoder layers (32 = the 7B shape)")
     ap.add_argument("--new-tokens", type=int, default=128, help="decode_7b: generated tokens per sequence")
     ap.add_argument("--gpus", type=int, default=1)
@@ -647,7 +682,7 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
-    elif args.leg in ("decode_7b", "moe"):
+    elif args.leg in ("decode_7b", "moe", "gemm"):
         run_leg(args)
     else:
         run_ours(args)

@@ -163,7 +163,10 @@ ZC_API int32_t zcu_engine_create(const zcu_engine_config* cfg, void* stream, voi
  * rows, Wo columns and K/V pages; K/V heads [kv_head_begin, +kv_heads) with their Wk/Wv rows; FFN units
  * [ffn_begin, +ffn) (whole 32-blocks) with their Wgate/Wup rows and Wdown columns; LM-head rows [vocab_begin,
  * +vocab).  Embedding and norms are replicated.  After Wo and after Wdown the residual stream is summed over
- * ranks (NCCL all-reduce); greedy sampling takes the arg-max of every rank's slice and merges them.
+ * ranks: up to max_batch rows over NVLink peer memory (CUDA IPC mappings, a one-shot push into every rank's
+ * slot and a rank-ordered sum; on the tensor-core path fused into the GEMM's split-K partials and the next
+ * RmsNorm), larger ones (prefill) by NCCL all-reduce; ZCU_TP_ALLREDUCE=nccl in the environment of every rank
+ * keeps all of them on NCCL.  Greedy sampling takes the arg-max of every rank's slice and merges them.
  * zcu_tp_plan is host-only (no GPU needed) and fails when heads or kv_heads do not divide by tp_size, when a
  * rank's Wo column slice is not a whole number of 32-blocks, or when there are fewer FFN blocks than ranks. */
 typedef struct {
