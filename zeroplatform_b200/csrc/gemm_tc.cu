@@ -7,16 +7,16 @@
 //
 // Numerics: both operands enter the tensor core as pairs of fp16 values.  Weights: a_hi = fp16(q * d) (the
 // exact product rounded once) and a_lo = fp16(q * d - a_hi) (one fused multiply-add: the residual rounded
-// once); activations: x_hi = fp16(x) and x_lo = fp16(x - x_hi).  Each 16-wide k-step issues three MMAs into the
-// same fp32 TMEM accumulator -- a_hi x_hi + a_hi x_lo + a_lo x_hi -- whose products are exact, so the result
-// carries both operands to about 2^-22 (the dropped a_lo x_lo term is below 2^-22) and differs from the fp32
+// once); activations: x_hi = fp16(x) and x_lo = fp16(x - x_hi).  Each 16-wide k-step accumulates three products
+// in fp32 TMEM -- a_hi x_hi + a_hi x_lo + a_lo x_hi, two instructions since the x_hi and x_lo tiles form one
+// operand of twice the width -- and the products are exact, so the result carries both operands to about 2^-22 (the dropped a_lo x_lo term is below 2^-22) and differs from the fp32
 // reference only by summation order.  A single fp16(q * d) x fp16(x) product misses the 1e-3 bound on
 // 4096-wide layers.  (An int8 MMA cannot apply the per-32-value fp16 block scales inside the tensor core, and a
 // CUDA-core epilogue per block would run several times slower than the MMA itself.)
 //
 // Structure (one persistent CTA per SM, 16 warps):
 //   warp 0      TMA producer: raw int8 W tiles [128 rows x 256 k] into a shared-memory ring (2-3 deep)
-//   warp 1      MMA issuer: one thread issues 4 x 3 tcgen05.mma.kind::f16 (M=128, N=BN, K=16) per stage
+//   warp 1      MMA issuer: one thread issues 4 x 2 tcgen05.mma.kind::f16 (M=128, N=2 BN and BN, K=16) per stage
 //   warp 2      TMA producer: activation tiles (fp16, pre-converted) [BN tokens x 64 k], 128B swizzle
 //   warps 4-11  dequantizers: int8 W tile (shared memory) x fp16 block scales -> fp16 hi / lo planes of q*d in
 //               the UMMA K-major 128B-swizzled layout (fence.proxy.async before signalling the MMA warp)
@@ -98,12 +98,11 @@ __host__ __device__ constexpr uint32_t idesc_f16(int m, int n) {
 }
 
 __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-  uint32_t z = 0;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(tmem_d),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(z), "r"(z), "r"(z), "r"(z));
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
 }
 
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
@@ -234,8 +233,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
-  if (warp == 1) {  // 2 accumulators of bn fp32 columns (power of two >= 32)
-    const uint32_t ncols = 2u * (uint32_t)bn;
+  if (warp == 1) {  // 2 accumulators of 2 bn fp32 columns: [x_hi sums | x_lo sums] (power of two >= 128)
+    const uint32_t ncols = 4u * (uint32_t)bn;
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(ncols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -302,7 +301,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      const uint32_t idesc = idesc_f16(BM, bn);
+      // Per 16-wide k-step two MMAs: a_hi x [x_hi | x_lo] (N = 2 bn: the hi and lo activation tiles are adjacent
+      // rows of the B stage) into accumulator columns [0, 2 bn), then a_lo x x_hi (N = bn) added into [0, bn); the
+      // epilogue adds column c + bn to column c.  Shared-memory descriptors advance by address / 16, so they are
+      // formed once and offset per stage and k-step.
+      const uint32_t idesc2 = idesc_f16(BM, 2 * bn), idesc1 = idesc_f16(BM, bn);
+      const uint64_t adesc0 = umma_desc_sw128(smem_u32(a_st)), bdesc0 = umma_desc_sw128(smem_u32(b_st));
       int s = 0;
       uint32_t ph = 0;
       int it = 0;
@@ -311,7 +315,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         const uint32_t acc_ph = (uint32_t)(it >> 1) & 1;
         if (!mbar_wait(smem_u32(&tempty[acc]), acc_ph ^ 1, abort_flag, p.status, 2)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * bn);
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * 2 * bn);
         bool ok = true;
         const int kb0 = unit_kb0(u);
         for (int kb = kb0; kb < unit_kb1(u); ++kb) {
@@ -320,15 +324,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(a_st + s * A_STAGE_BYTES);
-          const uint32_t b_addr = smem_u32(b_st + s * b_stage_bytes);
+          const uint64_t ad = adesc0 + (uint64_t)(s * (A_STAGE_BYTES >> 4));
+          const uint64_t bd = bdesc0 + (uint64_t)(s * (b_stage_bytes >> 4));
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint64_t ahi = umma_desc_sw128(a_addr + kk * 32);
-            const uint64_t bhi = umma_desc_sw128(b_addr + kk * 32);
-            umma_f16(d_tmem, ahi, bhi, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
-            umma_f16(d_tmem, ahi, umma_desc_sw128(b_addr + b_tile_bytes + kk * 32), idesc, 1u);  // a_hi x_lo
-            umma_f16(d_tmem, umma_desc_sw128(a_addr + A_PLANE_BYTES + kk * 32), bhi, idesc, 1u);  // a_lo x_hi
+          for (int kk = 0; kk < BK / 16; ++kk) {  // +32 bytes of K per step = +2 in the descriptor
+            umma_f16(d_tmem, ad + 2 * kk, bd + 2 * kk, idesc2, (kb != kb0 || kk != 0) ? 1u : 0u);  // a_hi x [hi|lo]
+            umma_f16(d_tmem, ad + (A_PLANE_BYTES >> 4) + 2 * kk, bd + 2 * kk, idesc1, 1u);          // a_lo x x_hi
           }
           umma_commit(smem_u32(&ab_empty[s]));  // frees the A/B stage once these MMAs have read it
           if (++s == AST) {
@@ -447,14 +448,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const bool acc_mode = p.splits == 1 && p.accumulate;
       for (int c0 = 0; c0 < bn; c0 += 32) {
         uint32_t r[32];
-        tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * bn + c0), r);
+        uint32_t rl[32];
+        const uint32_t tcol = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * 2 * bn + c0);
+        tmem_ld32(tcol, r);                  // a_hi x_hi + a_lo x_hi
+        tmem_ld32(tcol + (uint32_t)bn, rl);  // a_hi x_lo
         if (row < p.N) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int m = tok0 + c0 + j;
             if (m < p.M) {
               float* yp = out + (size_t)m * p.N + row;
-              const float v = __uint_as_float(r[j]);
+              const float v = __uint_as_float(r[j]) + __uint_as_float(rl[j]);
               *yp = acc_mode ? *yp + v : v;
             }
           }
@@ -470,7 +474,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(2u * (uint32_t)bn));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(4u * (uint32_t)bn));
   }
 }
 
