@@ -189,7 +189,7 @@ def _peak_tflops():
 
 
 def prefill_gemm_leg(dev, L, iters=20):
-    """Batched prefill GEMM: X fp32 [512, 4096] ~ N(0,1), W Q8_0 [11008, 4096] ~ N(0,0.02)."""
+    """Batched prefill GEMM (the 512-token prefill workload): X fp32 [512, 4096] ~ N(0,1), W Q8_0 [11008, 4096] ~ N(0,0.02)."""
     import torch
     from zeroplatform_b200.ops import QuantizedWeight, quantize
     M, N, K = 512, 11008, 4096
@@ -226,7 +226,7 @@ def prefill_gemm_leg(dev, L, iters=20):
 
 
 def decode_12l_leg(dev, with_cpu, n_prompt=512, n_new=128):
-    """BASELINE config 2: 12 layers, d 768, 12 heads x 64, SwiGLU 2048, vocab 32000, Q8_0 from N(0,0.02);
+    """Small Llama decode workload: 12 layers, d 768, 12 heads x 64, SwiGLU 2048, vocab 32000, Q8_0 from N(0,0.02);
     512 random prompt ids then 128 greedy tokens (repetition penalty 1.0), 16-token fp16 KV pages."""
     import numpy as np
     import torch
@@ -277,7 +277,7 @@ def decode_12l_leg(dev, with_cpu, n_prompt=512, n_new=128):
     return out
 
 def decode_7b_leg(dev, rank, world, batch=32, n_ctx=2048, n_new=128, n_warm=3, layers=32):
-    """Llama-2-7B-shaped decoder (32 layers, d 4096, 32 heads, FFN 11008, vocab 32000, Q8_0
+    """Tensor-parallel 7B decode workload: Llama-2-7B-shaped decoder (32 layers, d 4096, 32 heads, FFN 11008, vocab 32000, Q8_0
     from N(0,0.02)), decode batch 32, each sequence with a 2048-token context in 16-token fp16 pages, then 128
     greedy tokens per sequence; tensor parallel over the `world` GPUs of this job (one engine per rank).
 
@@ -359,7 +359,7 @@ def decode_7b_leg(dev, rank, world, batch=32, n_ctx=2048, n_new=128, n_warm=3, l
 
 
 def moe_leg(dev, rank, world, iters=10, tokens=256, n_experts=8, top_k=2, dim=4096, ffn=14336):
-    """MoE FFN layer, 8 experts x SwiGLU FFN 14336 at d_model 4096, Q4_0 (group 32, fp16 scales)
+    """Expert-parallel MoE workload: MoE FFN layer, 8 experts x SwiGLU FFN 14336 at d_model 4096, Q4_0 (group 32, fp16 scales)
     from N(0,0.02); 256 tokens of N(0,1) activations, router logits N(0,1), softmax over the top 2.  Expert
     parallel over the `world` GPUs of this job: each rank holds n_experts / world experts and 256 / world of the
     tokens; rows travel to the experts' ranks and back by NCCL all-to-all.  Timing: device events around the

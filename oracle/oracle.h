@@ -96,7 +96,7 @@ void orc_paged_attention(const float* q, const float* kcache, const float* vcach
 
 /* SparseMoeLayer.Forward (Layers/SparseMoeLayer.cs:32-125) for one token, Q4_0 or Q8_0 experts.
  * qtype: 8 or 4. router_logits: if non-null, used as the router output instead of the router GEMV
- * (BASELINE's MoE config draws router logits directly); else router_w (fp32 [E][dim]) is applied.
+ * (the MoE benchmark draws router logits directly); else router_w (fp32 [E][dim]) is applied.
  * experts_gate/up: [E][ffn][dim] blocks, experts_down: [E][dim][ffn] blocks. residual += sum_k w_k * expert_k(x).
  * sel_idx/sel_w (optional, length top_k) receive the selected experts and their softmax weights. */
 void orc_moe_forward(const float* xnorm, const float* router_w, const float* router_logits, int n_experts, int top_k,

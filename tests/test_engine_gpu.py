@@ -1,7 +1,7 @@
 """Device decode engine (LlmEngine over a paged fp16 KV cache) vs the oracle engine.
 
 The oracle runs with kv_fp16=True (it rounds every appended K/V to binary16, the device cache's storage
-precision) so that the comparison isolates the kernels.  Tolerances: logits max-rel <= 1e-3 (the north-star
+precision) so that the comparison isolates the kernels.  Tolerances: logits max-rel <= 1e-3 (the parity
 bound; batched prefill runs on fp16 tensor cores), greedy tokens identical.
 """
 import numpy as np

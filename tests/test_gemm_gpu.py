@@ -1,6 +1,6 @@
 """Prefill / batched Q8_0 GEMM on tcgen05 vs the oracle's token-parallel MatVecMulQ8_0 (LlmEngine.PrefillPrompt).
 
-Tolerance: max|Y - Y_oracle| / max|Y_oracle| <= 1e-3 -- the north-star bound for fp32 outputs.  The tensor
+Tolerance: max|Y - Y_oracle| / max|Y_oracle| <= 1e-3 -- the parity bound for fp32 outputs.  The tensor
 core consumes both operands as fp16 pairs (weights hi = fp16(q*d), lo = fp16(q*d - hi); activations hi = fp16(x),
 lo = fp16(x - hi)) with fp32 accumulation, so the products carry ~2^-22 and the result differs from the fp32
 restatement by summation order; the measured error is printed.

@@ -1,6 +1,6 @@
 """Decode GEMV parity: CUDA (libzero_tensor.so) vs the CPU oracle on identical seeded inputs.
 
-Tolerance: max|y - y_oracle| / max|y_oracle| <= 3e-4 (the north-star bound is 1e-3).  GEMVs below 64 MB of
+Tolerance: max|y - y_oracle| / max|y_oracle| <= 3e-4 (the parity bound for fp32 outputs is 1e-3).  GEMVs below 64 MB of
 weights keep x in fp32 (only the summation order differs: ~1e-6).  The streaming form for large weights
 re-expresses x per 32-value block as int16 (scale max|x| / 32767, so each value is within 2^-16 of the block
 maximum) and sums int16 x int8 products exactly in int32 (DP2A): for N(0,1) activations and N(0,0.02) weights

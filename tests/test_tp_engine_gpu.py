@@ -4,7 +4,7 @@
   hold binary16(k), binary16(v) and the sequence length moves when the last layer is written.
 * zcu_engine_generate_batch = GenerateStreamAsync greedy for several live sequences at once: the tokens must
   equal the oracle's per-sequence ForwardToken + arg-max loop.
-* tp_size 2 (two processes, one GPU each; skipped with fewer GPUs): prefill logits within the north-star bound
+* tp_size 2 (two processes, one GPU each; skipped with fewer GPUs): prefill logits within the 1e-3 parity bound
   (max-rel <= 1e-3) of the oracle, batched-decode logits equal to the same engine at tp_size 1 up to fp32
   summation order (which TP1 holds to the bound), greedy tokens identical, with an uneven vocabulary split
   (1001 rows) and an uneven FFN split (17 blocks).
