@@ -55,6 +55,13 @@ __host__ __device__ constexpr int w_tile_bytes(int qt) { return qt == 8 ? BM * B
 __host__ __device__ constexpr int w_stage_bytes(int qt) { return w_tile_bytes(qt) + S_TILE_BYTES; }
 __host__ __device__ constexpr int w_row_bytes(int qt) { return w_tile_bytes(qt) / BM; }  // 256 or 128
 constexpr int MAX_SPLITS = 8;               // split-K ranges per output tile at most
+// Tensor-memory A (tile widths BN <= 64 with TMA'd scales): the dequantizers store the fp16 hi / lo planes of
+// each k-stage into TMEM columns after the accumulators (64 columns a stage: 32 hi, 32 lo), so A never
+// occupies shared memory or its bandwidth.  The weight tile then arrives 128B-swizzled (128-byte boxes) so that
+// one-row-per-lane reads are conflict free.
+constexpr int TMEM_COLS = 512;
+constexpr int A_TMEM_STAGE_COLS = 64;
+constexpr int AT_MAX_BN = 64;
 
 struct GemmParams {
   const uint16_t* d;
@@ -104,6 +111,27 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t a, uint64_t b
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
       "l"(a), "l"(b), "r"(idesc), "r"(acc));
 }
+
+// The same with A read from tensor memory at column address a_tmem (rows on lanes, two fp16 per column).
+__device__ __forceinline__ void umma_f16_ta(uint32_t tmem_d, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                            uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
+}
+
+// 16 consecutive 32-bit columns of this thread's TMEM lane (the warp's lane quadrant) from registers.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
@@ -183,7 +211,8 @@ __device__ __forceinline__ void dequant32_q4(int4 w, __half2 d2, uint4 (&ch)[4],
 }
 
 // QT = 8: Q8_0 weights (int8 tiles); QT = 4: Q4_0 weights (nibble tiles, one 32-value block per dequant item).
-template <int QT>
+// AT: A in tensor memory (see TMEM_COLS); otherwise A in shared memory.
+template <int QT, bool AT>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_q8_0_tc_kernel(const __grid_constant__ CUtensorMap x_map, const __grid_constant__ CUtensorMap xl_map,
                         const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap s_map,
@@ -197,8 +226,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const int WSTAGES = p.w_stages;
   const int b_tile_bytes = bn * BK * 2;         // one fp16 activation tile (hi or lo)
   const int b_stage_bytes = 2 * b_tile_bytes;   // hi tile, then lo tile
-  uint8_t* a_st = smem;                                  // AST x 2 x 16 KB (fp16 A hi, lo planes; SW128)
-  uint8_t* b_st = a_st + AST * A_STAGE_BYTES;            // AST x 2 x bn*128 B (fp16 X hi, lo; SW128 by TMA)
+  uint8_t* a_st = smem;                                  // AST x 2 x 16 KB (fp16 A hi, lo planes; SW128); none if AT
+  uint8_t* b_st = AT ? smem : a_st + AST * A_STAGE_BYTES;  // AST x 2 x bn*128 B (fp16 X hi, lo; SW128 by TMA)
   uint8_t* w_st = b_st + AST * b_stage_bytes;            // WSTAGES x 8 KB (int8 W, TMA, unswizzled)
   uint64_t* bars = reinterpret_cast<uint64_t*>(w_st + WSTAGES * W_STAGE_BYTES);
   uint64_t* ab_full = bars;                            // [AST]: DQ_THREADS dequant arrivals + 1 X TMA (tx)
@@ -233,8 +262,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
-  if (warp == 1) {  // 2 accumulators of 2 bn fp32 columns: [x_hi sums | x_lo sums] (power of two >= 128)
-    const uint32_t ncols = 4u * (uint32_t)bn;
+  if (warp == 1) {  // 2 accumulators of 2 bn fp32 columns: [x_hi sums | x_lo sums] (power of two >= 128),
+                    // with A's stages after them when AT
+    const uint32_t ncols = AT ? (uint32_t)TMEM_COLS : 4u * (uint32_t)bn;
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(ncols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -265,6 +295,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           mbar_arrive_tx(smem_u32(&w_full[s]), (uint32_t)(p.scale_tma ? W_STAGE_BYTES : W_TILE_BYTES));
           tma_load_2d(smem_u32(w_st + s * W_STAGE_BYTES), &w_map, QT == 8 ? kb * BK : kb * BK / 2, row0,
                       smem_u32(&w_full[s]));
+          if (AT && QT == 8)  // the second 128-byte half of the 256-byte rows
+            tma_load_2d(smem_u32(w_st + s * W_STAGE_BYTES + BM * 128), &w_map, kb * BK + 128, row0,
+                        smem_u32(&w_full[s]));
           if (p.scale_tma)  // the 8 scales per row of these 256 k (x = kb * 2, a multiple of 8 scales = 16 bytes)
             tma_load_2d(smem_u32(w_st + s * W_STAGE_BYTES + W_TILE_BYTES), &s_map, kb * (BK / QK), row0,
                         smem_u32(&w_full[s]));
@@ -324,12 +357,21 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint64_t ad = adesc0 + (uint64_t)(s * (A_STAGE_BYTES >> 4));
           const uint64_t bd = bdesc0 + (uint64_t)(s * (b_stage_bytes >> 4));
+          if constexpr (AT) {  // A stage s: TMEM columns [4 bn + 64 s, +32) hi, [+32, +64) lo; 8 columns per k16
+            const uint32_t at = tmem_base + (uint32_t)(4 * bn + s * A_TMEM_STAGE_COLS);
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {  // +32 bytes of K per step = +2 in the descriptor
-            umma_f16(d_tmem, ad + 2 * kk, bd + 2 * kk, idesc2, (kb != kb0 || kk != 0) ? 1u : 0u);  // a_hi x [hi|lo]
-            umma_f16(d_tmem, ad + (A_PLANE_BYTES >> 4) + 2 * kk, bd + 2 * kk, idesc1, 1u);          // a_lo x x_hi
+            for (int kk = 0; kk < BK / 16; ++kk) {
+              umma_f16_ta(d_tmem, at + 8 * kk, bd + 2 * kk, idesc2, (kb != kb0 || kk != 0) ? 1u : 0u);
+              umma_f16_ta(d_tmem, at + 32 + 8 * kk, bd + 2 * kk, idesc1, 1u);
+            }
+          } else {
+            const uint64_t ad = adesc0 + (uint64_t)(s * (A_STAGE_BYTES >> 4));
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk) {  // +32 bytes of K per step = +2 in the descriptor
+              umma_f16(d_tmem, ad + 2 * kk, bd + 2 * kk, idesc2, (kb != kb0 || kk != 0) ? 1u : 0u);  // a_hi x [hi|lo]
+              umma_f16(d_tmem, ad + (A_PLANE_BYTES >> 4) + 2 * kk, bd + 2 * kk, idesc1, 1u);          // a_lo x x_hi
+            }
           }
           umma_commit(smem_u32(&ab_empty[s]));  // frees the A/B stage once these MMAs have read it
           if (++s == AST) {
@@ -358,6 +400,70 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       for (int kb = kb0; kb < kb1 && !stop; ++kb) {
         const int sub = (kb - kb0) % W_SUB;  // which 64-byte column block of the current weight tile
         if (sub == 0 && !mbar_wait(smem_u32(&w_full[ws]), wph, abort_flag, p.status, 4)) break;
+        if constexpr (AT) {
+          // One weight row per lane (row 32 * (warp % 4) + lane: the warp's TMEM lane quadrant), 32 values per
+          // lane per stage: warps 4-7 take values [0, 32) of the stage, warps 8-11 values [32, 64).
+          const int g = (warp - 4) >> 2, r = 32 * (warp & 3) + lane;
+          const uint8_t* tile = w_st + ws * W_STAGE_BYTES;
+          const uint16_t* ssrc = reinterpret_cast<const uint16_t*>(tile + W_TILE_BYTES);
+          int4 w0, w1 = make_int4(0, 0, 0, 0);
+          if (QT == 8) {  // bytes [64 sub + 32 g, +32) of the row: 128-byte box o >> 7, chunks XOR-swizzled by r % 8
+            const int o = sub * 64 + g * 32;
+            const uint8_t* rowp = tile + (o >> 7) * (BM * 128) + r * 128;
+            const int c0 = (o & 127) >> 4;
+            w0 = *reinterpret_cast<const int4*>(rowp + ((c0 ^ (r & 7)) << 4));
+            w1 = *reinterpret_cast<const int4*>(rowp + (((c0 + 1) ^ (r & 7)) << 4));
+          } else {  // one 16-byte Q4_0 block at byte 32 sub + 16 g of the 128-byte row
+            const int c0 = sub * 2 + g;
+            w0 = *reinterpret_cast<const int4*>(tile + r * 128 + ((c0 ^ (r & 7)) << 4));
+          }
+          const __half h = __ushort_as_half(ssrc[r * (W_SUB * BK / QK) + sub * (BK / QK) + g]);
+          const __half2 d2 = __halves2half2(h, h);
+          if (sub == W_SUB - 1 || kb == kb1 - 1) {  // last use of this tile: release it to the TMA producer
+            mbar_arrive(smem_u32(&w_empty[ws]));
+            if (++ws == WSTAGES) {
+              ws = 0;
+              wph ^= 1;
+            }
+          }
+          if (!mbar_wait(smem_u32(&ab_empty[as]), aph ^ 1, abort_flag, p.status, 5)) {
+            stop = true;
+            break;
+          }
+          tc_fence_after();  // the MMAs that read this A stage have completed (their commit released it)
+          uint32_t hv[16], lv[16];  // column c of the lane's 16 holds values (2c, 2c + 1), low half first
+          if (QT == 8) {
+            uint4 h0, h1, l0, l1;
+            dequant16(w0, d2, h0, h1, l0, l1);
+            hv[0] = h0.x, hv[1] = h0.y, hv[2] = h0.z, hv[3] = h0.w, hv[4] = h1.x, hv[5] = h1.y, hv[6] = h1.z, hv[7] = h1.w;
+            lv[0] = l0.x, lv[1] = l0.y, lv[2] = l0.z, lv[3] = l0.w, lv[4] = l1.x, lv[5] = l1.y, lv[6] = l1.z, lv[7] = l1.w;
+            dequant16(w1, d2, h0, h1, l0, l1);
+            hv[8] = h0.x, hv[9] = h0.y, hv[10] = h0.z, hv[11] = h0.w, hv[12] = h1.x, hv[13] = h1.y, hv[14] = h1.z,
+            hv[15] = h1.w;
+            lv[8] = l0.x, lv[9] = l0.y, lv[10] = l0.z, lv[11] = l0.w, lv[12] = l1.x, lv[13] = l1.y, lv[14] = l1.z,
+            lv[15] = l1.w;
+          } else {
+            uint4 qh[4], ql[4];
+            dequant32_q4(w0, d2, qh, ql);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              hv[4 * q] = qh[q].x, hv[4 * q + 1] = qh[q].y, hv[4 * q + 2] = qh[q].z, hv[4 * q + 3] = qh[q].w;
+              lv[4 * q] = ql[q].x, lv[4 * q + 1] = ql[q].y, lv[4 * q + 2] = ql[q].z, lv[4 * q + 3] = ql[q].w;
+            }
+          }
+          const uint32_t ta = tmem_base + ((uint32_t)(32 * (warp & 3)) << 16) +
+                              (uint32_t)(4 * bn + as * A_TMEM_STAGE_COLS + 16 * g);
+          tmem_st16(ta, hv);
+          tmem_st16(ta + 32, lv);
+          tmem_st_wait();
+          tc_fence_before();
+          mbar_arrive(smem_u32(&ab_full[as]));
+          if (++as == AST) {
+            as = 0;
+            aph ^= 1;
+          }
+          continue;
+        }
         // Q8_0: DQ_ITEMS items of 16 values (row r, 16-value chunk c); Q4_0: one item of one 32-value block
         // (row r, block b of the stage) per thread.
         constexpr int ITEMS = QT == 8 ? DQ_ITEMS : BM * BK / 32 / DQ_THREADS;
@@ -474,7 +580,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(4u * (uint32_t)bn));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(AT ? (uint32_t)TMEM_COLS : 4u * (uint32_t)bn));
   }
 }
 
@@ -554,6 +660,14 @@ static void ring_depths(int qt, int bn, int& ab, int& w) {
   if (ab > MAX_STAGES) ab = MAX_STAGES;
 }
 
+// Ring depths with A in tensor memory: as many A stages as TMEM holds after the accumulators (at most
+// MAX_STAGES), the weight ring as deep as shared memory allows (2 .. 4 tiles, 6 for the half-size Q4_0 tiles).
+static void ring_depths_at(int qt, int bn, int& ab, int& w) {
+  ab = std::min(MAX_STAGES, (TMEM_COLS - 4 * bn) / A_TMEM_STAGE_COLS);
+  w = qt == 8 ? 4 : 6;
+  while (w > 2 && SMEM_FIXED + ab * 2 * bn * BK * 2 + w * w_stage_bytes(qt) > SMEM_LIMIT) --w;
+}
+
 // A tile width is usable when its A/B ring is at least double-buffered (dequantizing one stage while the
 // tensor core reads the other).
 static bool ring_ok(int qt, int bn) {
@@ -627,7 +741,11 @@ static int launch_gemm(const void* qs, const uint16_t* d, const __half* x_hi, co
                        float** partials = nullptr, int* nsplit = nullptr) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return kCudaError;
-  const GemmConfig c = choose_config(m, n, k, QT);
+  GemmConfig c = choose_config(m, n, k, QT);
+  // Block scales [N][K/32] fp16 by TMA, 8 per row per weight tile (needs a 16-byte row pitch: K % 256 == 0).
+  const int scale_tma = (k % 256 == 0) ? 1 : 0;
+  const bool at = c.bn <= AT_MAX_BN && scale_tma;  // A in tensor memory
+  if (at) ring_depths_at(QT, c.bn, c.ab_stages, c.w_stages);
   float* part = reinterpret_cast<float*>(ws + align256((size_t)m * k * 4));
   if (partials) {
     if (m > 128 && c.splits == 1) return kUnsupported;  // no partial space reserved (see the workspace rule)
@@ -650,19 +768,19 @@ static int launch_gemm(const void* qs, const uint16_t* d, const __half* x_hi, co
       return kCudaError;
   }
   {
+    // weight tiles: whole 256- (Q8_0) or 128-byte (Q4_0) rows unswizzled, or with A in TMEM 128-byte boxes
+    // with the 128B swizzle (a Q8_0 tile is then two boxes)
     const cuuint64_t row_bytes = QT == 8 ? (cuuint64_t)k : (cuuint64_t)k / 2;
     cuuint64_t gdim[2] = {row_bytes, (cuuint64_t)n};
     cuuint64_t gstride[1] = {row_bytes};
-    cuuint32_t box[2] = {(cuuint32_t)w_row_bytes(QT), (cuuint32_t)BM};
+    cuuint32_t box[2] = {(cuuint32_t)(at ? 128 : w_row_bytes(QT)), (cuuint32_t)BM};
     cuuint32_t estride[2] = {1, 1};
     if (enc(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(qs), gdim, gstride, box, estride,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            CU_TENSOR_MAP_INTERLEAVE_NONE, at ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return kCudaError;
   }
 
-  // Block scales [N][K/32] fp16 by TMA, 8 per row per weight tile (needs a 16-byte row pitch: K % 256 == 0).
-  const int scale_tma = (k % 256 == 0) ? 1 : 0;
   CUtensorMap smap = wmap;
   if (scale_tma) {
     cuuint64_t gdim[2] = {(cuuint64_t)(k / QK), (cuuint64_t)n};
@@ -692,12 +810,12 @@ static int launch_gemm(const void* qs, const uint16_t* d, const __half* x_hi, co
   p.n_tiles = c.n_tiles;
   p.splits = c.splits;
   p.kb_per_split = c.kb_per;
-  const int smem = SMEM_FIXED + c.ab_stages * (A_STAGE_BYTES + 2 * c.bn * BK * 2) + c.w_stages * w_stage_bytes(QT);
-  if (cudaFuncSetAttribute(gemm_q8_0_tc_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-    return kCudaError;
+  const int smem = SMEM_FIXED + c.ab_stages * ((at ? 0 : A_STAGE_BYTES) + 2 * c.bn * BK * 2) +
+                   c.w_stages * w_stage_bytes(QT);
+  auto kern = at ? gemm_q8_0_tc_kernel<QT, true> : gemm_q8_0_tc_kernel<QT, false>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return kCudaError;
   const int grid = std::min(c.n_tiles * c.splits, num_sms());
-  if (launch_pdl(gemm_q8_0_tc_kernel<QT>, dim3(grid), dim3(GEMM_THREADS), (size_t)smem, s, xmap, xlmap, wmap, smap,
-                 p) != cudaSuccess)
+  if (launch_pdl(kern, dim3(grid), dim3(GEMM_THREADS), (size_t)smem, s, xmap, xlmap, wmap, smap, p) != cudaSuccess)
     return kCudaError;
   if (c.splits > 1 && !partials) {
     const size_t mn = (size_t)m * n;
