@@ -50,3 +50,18 @@ def test_no_silent_cpu_fallback_without_gpu():
     rc = L.zc_gemv_q8_0(ctypes.addressof(w), ctypes.addressof(x), ctypes.addressof(y), 1, 32)
     assert rc != 0  # not handled: the C# caller runs its managed path; the library itself never computes on CPU
     assert L.zc_cuda_last_error()
+
+
+def test_bad_arguments_are_refused_before_any_device_work():
+    """The bridge entries validate their arguments on the host first (non-zero = the C# caller runs its managed
+    path): a k that is not a whole number of 32-blocks, null buffers, tensor types other than Q8_0 / Q4_0."""
+    from zeroplatform_b200 import _lib
+    L = _lib.lib()
+    x = (ctypes.c_float * 48)()
+    y = (ctypes.c_float * 1)()
+    w = (ctypes.c_uint8 * 64)()
+    assert L.zc_gemv_q8_0(ctypes.addressof(w), ctypes.addressof(x), ctypes.addressof(y), 1, 48) == -2
+    assert b"k_cols" in L.zc_cuda_last_error()
+    assert L.zc_gemv_q4_0(None, ctypes.addressof(x), ctypes.addressof(y), 1, 32) == -2
+    assert L.zc_register_weights(0, ctypes.addressof(w), 1, 32) == -4   # F32 tensors are not registered
+    assert L.zc_register_weights(8, ctypes.addressof(w), 1, 48) == -2   # not a whole number of blocks
