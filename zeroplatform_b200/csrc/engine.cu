@@ -10,8 +10,9 @@
 // Step (one token per sequence, B sequences -- ForwardToken, LlmEngine.cs:347-461):
 //   embed -> per layer: [RmsNorm + Wqkv] -> RoPE + KV append -> paged attention (per-layer causal length)
 //   -> x += Wo.attn -> [RmsNorm + Wgate|Wup] -> [SwiGLU + x += Wdown.s] -> final [RmsNorm + LM head] -> greedy
-// B = 1 uses the GEMV kernels with the RmsNorm / SwiGLU prologues fused; B > 1 and batched prefill use the
-// tcgen05 GEMM.  Prefill of T > 1 tokens follows PrefillPrompt (:157-315): all T tokens per layer at once,
+// B = 1 uses the GEMV kernels with the RmsNorm / SwiGLU prologues fused; 1 < B < 9 one fp32 GEMV per row;
+// B >= 9 and batched prefill the tcgen05 GEMM, whose fp16 hi / lo activation operands the kernels before it
+// (RmsNorm, attention, SwiGLU) write directly.  Prefill of T > 1 tokens follows PrefillPrompt (:157-315): all T tokens per layer at once,
 // K/V appended for all of them, then attention with causal length (l == L-1 ? pos + 1 : pos) per token.
 // The reference's causal rule (non-final layers exclude the current token) is on by default; off gives the
 // standard rule (pos + 1 everywhere).
@@ -21,8 +22,10 @@
 // Tensor parallelism (tp_size > 1, one engine per GPU): every rank holds the query heads, K/V heads, FFN units
 // and vocabulary rows that zcu_tp_plan assigns it.  Wq|Wk|Wv and Wgate|Wup are split by output rows, Wo and
 // Wdown by input columns on 32-block boundaries, so each rank's Wo / Wdown product is a partial sum of the
-// residual update: rank 0 adds its partial to x, the other ranks write theirs over x, and one in-place NCCL
-// all-reduce of x [T][dim] leaves x + sum(partials) on every rank (two all-reduces per layer).  Attention
+// residual update: rank 0 adds its partial to x, the other ranks write theirs over x, and an all-reduce of
+// x [T][dim] leaves x + sum(partials) on every rank (two per layer).  Up to max_batch rows it runs over NVLink
+// peer memory (allreduce_p2p.cu; on the tensor-core path fused into the GEMM's split-K partials and the next
+// RmsNorm), beyond that (prefill) as an in-place NCCL all-reduce.  Attention
 // needs no exchange (whole heads and their pages stay on one rank; page tables are replicated because every
 // rank runs the same allocator on the same calls).  Greedy sampling: each rank's arg-max over its vocabulary
 // slice, an all-gather of (value, index) pairs, and a merge that keeps the lowest index on ties.

@@ -15,15 +15,17 @@
 // CUDA-core epilogue per block would run several times slower than the MMA itself.)
 //
 // Structure (one persistent CTA per SM, 16 warps):
-//   warp 0      TMA producer: raw int8 W tiles [128 rows x 256 k] into a shared-memory ring (2-3 deep)
+//   warp 0      TMA producer: raw int8 W tiles [128 rows x 256 k] into a shared-memory ring (2-6 deep)
 //   warp 1      MMA issuer: one thread issues 4 x 2 tcgen05.mma.kind::f16 (M=128, N=2 BN and BN, K=16) per stage
 //   warp 2      TMA producer: activation tiles (fp16, pre-converted) [BN tokens x 64 k], 128B swizzle
-//   warps 4-11  dequantizers: int8 W tile (shared memory) x fp16 block scales -> fp16 hi / lo planes of q*d in
-//               the UMMA K-major 128B-swizzled layout (fence.proxy.async before signalling the MMA warp)
+//   warps 4-11  dequantizers: int8 W tile (shared memory) x fp16 block scales -> fp16 hi / lo planes of q*d,
+//               either in shared memory in the UMMA K-major 128B-swizzled layout (fence.proxy.async before
+//               signalling the MMA warp) or, for tiles of at most 64 tokens, in TMEM (tcgen05.st, one weight row
+//               per lane; the MMA then reads A from TMEM)
 //   warps 12-15 epilogue: tcgen05.ld 32 TMEM columns at a time, coalesced fp32 stores of Y (or of the
 //               split-K partials, summed afterwards in split order by splitk_reduce_kernel)
-// The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue of one tile overlaps the
-// MMAs of the next.  Every mbarrier wait is bounded: on time-out the CTA records an error code in
+// The accumulator is double-buffered in TMEM (2 x 2 BN columns: the x_hi and x_lo halves) so the epilogue of
+// one tile overlaps the MMAs of the next.  Every mbarrier wait is bounded: on time-out the CTA records an error code in
 // `status`, stops issuing work, drains what it issued and frees its TMEM before returning.
 //
 // Roofline: tensor (fp16 dense), flops = 2 * M * N * K.

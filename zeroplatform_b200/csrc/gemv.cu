@@ -11,8 +11,11 @@
 // so every row of quantized values is 16-byte aligned and streams with 128-bit loads; the reference's
 // 34/18-byte array-of-structs blocks are not 16-byte aligned.
 //
-// Kernel shape: one warp owns R rows; each lane keeps 8 L1-bypassing 128-bit weight loads in flight (U
-// chunks of each of the R rows), the activation vector is staged once per CTA in shared memory
+// Forms: the slab form (Q8_0, K = 4096: activations in registers, 7 rows a CTA split between registers and
+// bulk copies), the direct form below for the other decode shapes, and the streaming form (int16 activations,
+// DP2A, L2 prefetch) for >= 64 MB of weights.  Direct form: one warp owns R rows; each lane keeps 8
+// L1-bypassing 128-bit weight loads in flight (U chunks of each of the R rows), the activation vector is
+// staged once per CTA in shared memory
 // (XOR-swizzled so that the 128-bit shared loads of a warp are bank-conflict free), int8/nibble -> fp32
 // conversion is exact (PRMT + packed FADD), products accumulate in packed fp32x2 FMAs, per-chunk sums are
 // scaled by the block scale, and a warp-shuffle reduction finishes each row.  At most 64 registers a
