@@ -52,7 +52,7 @@ def _tiles(plans, begin, count, total, multiple=1):
     assert pos == total
 
 
-@pytest.mark.parametrize("world,model", [(2, SEVEN_B), (4, SEVEN_B),
+@pytest.mark.parametrize("world,model", [(2, SEVEN_B), (4, SEVEN_B), (8, SEVEN_B),
                                          (2, dict(vocab=1001, dim=256, layers=2, heads=8, kv_heads=4, ffn=544))])
 def test_plan_tiles_the_model_and_every_rank_gets_rank0s_nccl_id(world, model):
     port = _free_port()
