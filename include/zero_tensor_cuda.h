@@ -91,9 +91,9 @@ ZC_API int32_t zcu_paged_attention(const float* q, const void* k_pool, const voi
                             int64_t page_stride, int64_t slot_stride, int64_t head_stride, float scale,
                             int32_t max_ctx, void* stream);
 
-/* The same paged attention for callers that cannot allocate device memory when they run it -- a caller
- * recording a CUDA graph (cudaMalloc is not allowed while a stream is captured), a server that gave all free
- * HBM to its KV page pool, or a decode loop that forbids allocation after start-up.  No counterpart in the
+/* The same paged attention for callers that cannot allocate device memory when they run it -- a server that
+ * gave all free HBM to its KV page pool, or a host runtime whose decode loop forbids device allocation after
+ * start-up (cudaMalloc / cudaFree can synchronise the whole device).  No counterpart in the
  * reference (its managed fallback allocates nothing on a device).  Same arguments as zcu_paged_attention;
  * the split-K scratch is a fixed 1 MiB array inside the library (held by every GPU that loads it until the
  * process exits), so shapes needing more than 8,192 arrival counters (batch * hq) or 253,952 partial floats

@@ -65,3 +65,27 @@ def test_bad_arguments_are_refused_before_any_device_work():
     assert L.zc_gemv_q4_0(None, ctypes.addressof(x), ctypes.addressof(y), 1, 32) == -2
     assert L.zc_register_weights(0, ctypes.addressof(w), 1, 32) == -4   # F32 tensors are not registered
     assert L.zc_register_weights(8, ctypes.addressof(w), 1, 48) == -2   # not a whole number of blocks
+
+
+def test_paged_attention_shapes_are_checked_before_any_device_work():
+    """Both device attention entries reject an impossible shape on the host before choosing a split count or
+    touching scratch: hkv == 0 (no division by zero), hq not a multiple of hkv, a non-positive page size or head
+    size (-2), and a head size the kernel has no form for (-4)."""
+    from zeroplatform_b200 import _lib
+    L = _lib.lib()
+    buf = (ctypes.c_float * 64)()
+    p = ctypes.addressof(buf)  # never dereferenced: every call below is refused first
+
+    def call(fn, hq=8, hkv=2, hd=64, page_size=16, max_pages=4, batch=1):
+        return fn(p, p, p, 1, p, p, p, batch, hq, hkv, hd, page_size, max_pages, 8, hkv * page_size * hd, hd,
+                  page_size * hd, 0.125, 64, None)
+
+    for fn in (L.zcu_paged_attention, L.zcu_paged_attention_noalloc):
+        assert call(fn, hkv=0) == -2
+        assert call(fn, hq=6, hkv=4) == -2
+        assert call(fn, page_size=0) == -2
+        assert call(fn, hd=0) == -2
+        assert call(fn, hd=-64) == -2
+        assert call(fn, max_pages=0) == -2
+        assert call(fn, hd=48) == -4
+        assert L.zc_cuda_last_error()

@@ -1,19 +1,21 @@
 """zcu_paged_attention_noalloc: paged decode attention that allocates no device memory.
 
-Some users of this library cannot call cudaMalloc at the moment they run attention: a caller that is
-recording a CUDA graph (device allocation is not allowed while a stream is being captured), a server that
-has already handed all free HBM to its KV page pool, or a decode loop whose owner forbids allocation after
-start-up (cudaFree stalls the whole device).  For them the library keeps the split-K scratch of the attention
-kernel in a fixed 1 MiB array compiled into libzero_tensor.so instead of a workspace it allocates on demand.
+Some users of this library cannot call cudaMalloc at the moment they run attention: a serving process that
+has already handed all free HBM to its KV page pool (a late allocation would fail or fragment it), or a host
+runtime whose decode loop forbids device allocation after start-up because cudaMalloc and cudaFree can
+synchronise the whole device and stall every stream on it.  For them the library keeps the split-K scratch of
+the attention kernel in a fixed 1 MiB array compiled into libzero_tensor.so instead of a workspace it allocates
+on demand.
 
-These tests call the new entry point through the C ABI and check it against zcu_paged_attention (the
-allocating entry point) with the tolerance of the other attention tests, on two calls in a row, so that
-scratch left behind by the first call cannot leak into the second.  This file is collected last.
+These tests call the entry point through the C ABI and check it against zcu_paged_attention (the allocating
+entry point) and against the oracle, with the tolerance of the other attention tests, on two calls in a row, so
+that scratch left behind by the first call cannot leak into the second.  This file is collected last.
 """
 import numpy as np
 import pytest
 import torch
 
+import oracle as O
 from tests.conftest import rel_err
 
 pytestmark = pytest.mark.gpu
@@ -60,6 +62,14 @@ def test_no_alloc_matches_allocating_entry_point_on_two_calls_in_a_row():
         torch.cuda.synchronize()
         assert torch.isfinite(got).all()
         assert rel_err(got.cpu().numpy(), ref.cpu().numpy()) <= TOL
+        # and against the oracle (TensorOps.PagedAttention, slot-major fp32 pools) sequence by sequence
+        kf = c["k"].float().permute(0, 2, 1, 3).contiguous().cpu().numpy()
+        vf = c["v"].float().permute(0, 2, 1, 3).contiguous().cpu().numpy()
+        pt, ctx, q = c["pt"].cpu().numpy(), c["ctx"].cpu().numpy(), c["q"].cpu().numpy()
+        g = got.cpu().numpy()
+        for b in range(c["batch"]):
+            want = O.paged_attention(q[b], kf, vf, pt[b], int(ctx[b]))
+            assert rel_err(g[b], want) <= TOL
 
 
 def test_no_alloc_rejects_shapes_beyond_its_fixed_scratch():

@@ -300,25 +300,34 @@ size_t paged_attention_workspace_floats(int batch, int hq, int hd, int splits) {
   return splits <= 1 ? 0 : (size_t)batch * hq * splits * (hd + 2);
 }
 
-int paged_attention_choose_splits(int batch, int hkv, int max_ctx, int page_size) {
-  if (max_ctx <= 0 || page_size <= 0) return 1;
-  const int n_pages = (max_ctx + page_size - 1) / page_size;
-  const int ctas = batch * hkv;
-  // Enough CTAs to keep HBM busy: the fp16 kernel needs about 7 resident CTAs per SM (1000 on 148 SMs) once
-  // the batch itself supplies many (a tensor-parallel rank's share of the heads); small batches get at least
-  // two CTAs per SM
-  const int target = std::max(2 * 148, std::min(1000, 8 * ctas));
-  const int want = (target + ctas - 1) / ctas;
-  int splits = want < 1 ? 1 : want;
-  if (splits > n_pages) splits = n_pages;
-  if (splits > 64) splits = 64;
-  return splits < 1 ? 1 : splits;
-}
-
-int paged_attention(const PagedAttnArgs& a, cudaStream_t s) {
+int paged_attention_check(const PagedAttnArgs& a) {
   if (!a.q || !a.k_pool || !a.v_pool || !a.page_table || !a.ctx_len || !a.out) return kBadArgument;
   if (a.batch <= 0 || a.hq <= 0 || a.hkv <= 0 || a.hq % a.hkv || a.page_size <= 0 || a.max_pages <= 0)
     return kBadArgument;
+  if ((long long)a.batch * a.hq > 0x7fffffffLL) return kBadArgument;
+  switch (a.hd) {
+    case 8: case 16: case 32: case 64: case 128: case 256: return kOk;
+    default: return a.hd <= 0 ? kBadArgument : kUnsupported;
+  }
+}
+
+int paged_attention_choose_splits(int batch, int hkv, int max_ctx, int page_size) {
+  if (max_ctx <= 0 || page_size <= 0 || batch <= 0 || hkv <= 0) return 1;
+  const long long n_pages = ((long long)max_ctx + page_size - 1) / page_size;
+  const long long ctas = (long long)batch * hkv;
+  // Enough CTAs to keep HBM busy: the fp16 kernel needs about 7 resident CTAs per SM (1000 on 148 SMs) once
+  // the batch itself supplies many (a tensor-parallel rank's share of the heads); small batches get at least
+  // two CTAs per SM
+  const long long target = std::max(2LL * 148, std::min(1000LL, 8 * ctas));
+  const long long want = (target + ctas - 1) / ctas;
+  long long splits = want < 1 ? 1 : want;
+  if (splits > n_pages) splits = n_pages;
+  if (splits > 64) splits = 64;
+  return splits < 1 ? 1 : (int)splits;
+}
+
+int paged_attention(const PagedAttnArgs& a, cudaStream_t s) {
+  if (const int rc = paged_attention_check(a)) return rc;
   const int elem = a.kv_half ? 2 : 4;
   const long long vec = 16 / elem;  // elements per 16-byte load
   if (a.page_stride % vec || a.slot_stride % vec || a.head_stride % vec) return kUnsupported;

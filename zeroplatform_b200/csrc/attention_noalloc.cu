@@ -3,11 +3,10 @@
 // zcu_paged_attention_noalloc runs the same paged-attention kernel as zcu_paged_attention, but its split-K
 // scratch (the per-split partial results and the arrival counters that pick the CTA which merges them) lives
 // in one fixed array compiled into this library instead of a workspace the library allocates on demand.
-// It is for callers that cannot call cudaMalloc at the point where they run attention: a caller recording
-// a CUDA graph (cudaMalloc is not a stream operation and is not allowed while a stream is being captured),
-// a server that has handed all free HBM to its KV page pool (so a late allocation would fail or fragment
-// it), or a latency-critical decode loop whose owner forbids allocation after start-up (cudaFree
-// synchronises the whole device).
+// It is for callers that cannot call cudaMalloc at the point where they run attention: a serving process
+// that has handed all free HBM to its KV page pool (so a late allocation would fail or fragment it), or a
+// host runtime whose decode loop forbids device allocation after start-up because cudaMalloc and cudaFree
+// can synchronise the whole device and stall every stream on it.
 //
 // Limits and sharing:
 //   * the array holds kScratchBytes = 1 MiB: 8,192 int32 arrival counters (one per sequence x query head)
@@ -109,6 +108,12 @@ extern "C" int32_t zcu_paged_attention_noalloc(const float* q, const void* k_poo
   a.scale = scale;
   a.kv_half = kv_dtype == 1;
   a.max_ctx = max_ctx;
+  if (const int rc = paged_attention_check(a)) {
+    set_last_error(rc == kUnsupported ? "zcu_paged_attention_noalloc: head size must be 8, 16, 32, 64, 128 or 256"
+                                      : "zcu_paged_attention_noalloc: null pointer, or batch/hq/hkv/page_size/"
+                                        "max_pages not positive, or hq not a multiple of hkv");
+    return rc;
+  }
   a.splits = paged_attention_choose_splits(batch, hkv, max_ctx, page_size);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (a.splits > 1) {

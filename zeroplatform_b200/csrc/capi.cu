@@ -718,6 +718,10 @@ int32_t zcu_paged_attention(const float* q, const void* k_pool, const void* v_po
   a.scale = scale;
   a.kv_half = kv_dtype == 1;
   a.max_ctx = max_ctx;
+  if (const int rc = paged_attention_check(a))
+    return fail(rc, rc == kUnsupported ? "head size must be 8, 16, 32, 64, 128 or 256"
+                                       : "null pointer, or batch/hq/hkv/page_size/max_pages not positive, "
+                                         "or hq not a multiple of hkv");
   return attention_device(a, as_stream(stream));
 }
 

@@ -422,27 +422,53 @@ __device__ __forceinline__ float transposed_sum8(const float (&p)[8], int lane) 
   return q1 + __shfl_xor_sync(0xffffffffu, q1, 1);
 }
 
-// 16 int8 weights (one 16-byte chunk) . 16 fp32 activations, exact conversion, packed FMAs
-__device__ __forceinline__ float dot16_regs(const int4& w, const float2 (&x)[8]) {
-  const float2 bias = f2(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
-  const uint32_t* wv = reinterpret_cast<const uint32_t*>(&w);
-  float2 s = f2(0.f, 0.f);
+// This lane's 16 activations as int16, packed two to a register (element 2j in the low half), with the scale
+// of their 32-value block: lanes 2i and 2i + 1 hold the two halves of one block and agree on its maximum with one
+// shuffle.  q = rint(x * 32767 / max|x|), so |x - s q| <= s / 2 with s = max|x| / 32767 (2^-16 of the block's
+// largest value).  Rounding uses the magic number 1.5 * 2^23: v * inv + 1.5 * 2^23 (one packed FMA for two values,
+// a single round-to-nearest-even) leaves rint(v * inv) in the low 16 bits of the float's encoding, and one PRMT
+// packs two of them.
+struct XLane16 {
+  int v[8];
+  float s;
+};
+
+__device__ __forceinline__ void lane_quantize16(const float (&x)[16], XLane16& r) {
+  float amax = 0.f;
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    float2 p01, p23;
-    bytes_to_f2(wv[j] ^ 0x80808080u, bias, p01, p23);
-    s = __ffma2_rn(p01, x[2 * j], s);
-    s = __ffma2_rn(p23, x[2 * j + 1], s);
+  for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(x[j]));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  const float inv = amax > 0.f ? 32767.0f / amax : 0.f;
+  r.s = amax * (1.0f / 32767.0f);
+  const float2 inv2 = f2(inv, inv), mg2 = f2(12582912.0f, 12582912.0f);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float2 a = __ffma2_rn(f2(x[2 * j], x[2 * j + 1]), inv2, mg2);
+    r.v[j] = (int)__byte_perm(__float_as_uint(a.x), __float_as_uint(a.y), 0x5410);
   }
-  return s.x + s.y;
+}
+
+// 16 int8 weights . this lane's 16 int16 activations, exact in int32 (DP2A: two int16 x int8 products a step)
+__device__ __forceinline__ int dot16_i16(const int4& w, const XLane16& x) {
+  int s = dp2a_lo(x.v[0], w.x, 0);
+  s = dp2a_hi(x.v[1], w.x, s);
+  s = dp2a_lo(x.v[2], w.y, s);
+  s = dp2a_hi(x.v[3], w.y, s);
+  s = dp2a_lo(x.v[4], w.z, s);
+  s = dp2a_hi(x.v[5], w.z, s);
+  s = dp2a_lo(x.v[6], w.w, s);
+  return dp2a_hi(x.v[7], w.w, s);
 }
 
 // Slab form of the decode-chain Q8_0 GEMV for K == 4096 (d_model of the 7B-class shapes).  Warp w owns the
 // columns [512 w, 512 w + 512) of every row of its CTA, so each lane keeps its 16 activations in registers (x is
-// never staged in shared memory).  A CTA owns SLAB_ROWS = 7 rows: SLAB_REG = 4 stream into registers (one 16-byte
-// load per lane and row) and SLAB_SMEM = 3 are bulk-copied into shared memory by one thread, all issued before
-// griddepcontrol.wait.  Row sums leave each warp through the transposed butterfly and the 8 warps' slab sums
-// are added in warp order in shared memory.  At most 64 registers: four CTAs per SM.
+// never staged in shared memory), as int16 with a per-block scale (lane_quantize16).  A CTA owns SLAB_ROWS = 7
+// rows: SLAB_REG = 4 stream into registers (one 16-byte load per lane and row) and SLAB_SMEM = 3 are bulk-copied
+// into shared memory by one thread, all issued before griddepcontrol.wait.  Each row chunk is 8 DP2A
+// instructions, one conversion and one multiply by d_w * s_x: about a third of the instructions of the fp32 form,
+// and the work after the wait is what bounds back-to-back launches (the next launch's weight stream starts only
+// as this one's CTAs retire).  Row sums leave each warp through the transposed butterfly and the 8 warps' slab
+// sums are added in warp order in shared memory.  At most 64 registers: four CTAs per SM.
 constexpr int SLAB_K = 4096, SLAB_REG = 4, SLAB_SMEM = 3, SLAB_ROWS = SLAB_REG + SLAB_SMEM;
 
 template <class XP>
@@ -487,22 +513,29 @@ __global__ void __launch_bounds__(GEMV_THREADS, 4)
   }
   pdl_wait();  // x (and y when accumulating) may come from the previous kernel
   xp.prepare(xred);
-  float2 xr[8];
+  XLane16 xq;
+  {
+    float xv[16];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const float4 v = xp.get4(c * 16 + 4 * j, xred);
-    xr[2 * j] = f2(v.x, v.y);
-    xr[2 * j + 1] = f2(v.z, v.w);
+    for (int j = 0; j < 4; ++j) {
+      const float4 v = xp.get4(c * 16 + 4 * j, xred);
+      xv[4 * j] = v.x;
+      xv[4 * j + 1] = v.y;
+      xv[4 * j + 2] = v.z;
+      xv[4 * j + 3] = v.w;
+    }
+    lane_quantize16(xv, xq);
   }
   float p[8];
 #pragma unroll
-  for (int r = 0; r < SLAB_REG; ++r) p[r] = sc[r] * dot16_regs(w[r], xr);
+  for (int r = 0; r < SLAB_REG; ++r) p[r] = (sc[r] * xq.s) * (float)dot16_i16(w[r], xq);
   const bool ok = nsm == 0 || mbar_wait(smem_u32(&bar), 0, &abort_flag, &g_gemv_status, 31);
 #pragma unroll
   for (int j = 0; j < SLAB_SMEM; ++j) {
     p[SLAB_REG + j] = 0.f;
     if (ok && j < nsm)
-      p[SLAB_REG + j] = h2f(ssc[j][c >> 1]) * dot16_regs(*reinterpret_cast<const int4*>(&srow[j][c * 16]), xr);
+      p[SLAB_REG + j] =
+          (h2f(ssc[j][c >> 1]) * xq.s) * (float)dot16_i16(*reinterpret_cast<const int4*>(&srow[j][c * 16]), xq);
   }
 #pragma unroll
   for (int r = SLAB_ROWS; r < 8; ++r) p[r] = 0.f;

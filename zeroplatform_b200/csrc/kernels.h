@@ -82,6 +82,9 @@ struct PagedAttnArgs {
   long long pt_stride = -1;   // elements between page-table rows (-1: max_pages; 0: all queries share row 0)
   const int32_t* pt_rows = nullptr;  // optional page-table row per query (default: the query index)
 };
+// kOk when the arguments describe a launchable shape: non-null pointers, batch, hq, hkv, page_size and max_pages
+// positive, hq a multiple of hkv, hd one of 8/16/32/64/128/256 (else kBadArgument / kUnsupported).
+int paged_attention_check(const PagedAttnArgs& a);
 size_t paged_attention_workspace_floats(int batch, int hq, int hd, int splits);
 int paged_attention_choose_splits(int batch, int hkv, int max_ctx, int page_size);
 int paged_attention(const PagedAttnArgs& a, cudaStream_t s);
