@@ -37,9 +37,17 @@ ALGO_BYTES = QBYTES + COLS * 4 + ROWS * 4        # + x read + y written
 AOS_BYTES = ROWS * (COLS // 32) * 34             # the reference's packed weight bytes
 # Published CPU figure for this exact GEMV (ZeroTensor/README.md:198-203): 3.79 ms for the 17.8 MB weight.
 PUBLISHED_GBS = AOS_BYTES / 3.79e-3 / 1e9
-# dram__bytes_read.sum + dram__bytes_write.sum of one gemv_slab_kernel launch of this workload, from the ncu
-# capture summarised in profiles/gemv_slab_q8_0_4096x4096.md (17,856,000 read + 0 written).
+# dram__bytes_read.sum + dram__bytes_write.sum of one gemv_slab_kernel launch of this workload (17,856,000 read +
+# 0 written), from an ncu capture of this command; reported as the roofline's traffic with that source named.
 NCU_TRAFFIC_BYTES = 17856000
+
+
+def workload_config(world):
+    """The workload both arms report (the GPU arm and the reference arm run the same one)."""
+    return {"workload": f"q8_0_gemv_{ROWS}x{COLS}", "rows": ROWS, "cols": COLS, "weight_copies": N_COPIES,
+            "step": f"one GEMV over each of the {N_COPIES} weight copies",
+            "l2": f"inputs larger than L2: {N_COPIES} rotating weight copies, "
+                  f"{N_COPIES * QBYTES / 1e6:.0f} MB", "parallelism": f"replicas x{world}"}
 
 
 def _peaks():
@@ -140,41 +148,49 @@ def cpu_baseline(seconds=10.0):
 
 
 def run_reference(args):
-    """`--impl reference`: the reference's CPU path (oracle restatement of the C#) on all host cores.
-    Each step is one MatVecMulQ8_0 call on the next of 8 rotating weight copies (143 MB, above the host LLC),
-    a bounded sample of the GPU arm's 16-copy step with the same per-byte metric."""
+    """`--impl reference`: the reference's CPU path (the oracle's C++ restatement of the C#) on all host cores.
+    Each step is what a GPU step is: one MatVecMulQ8_0 call on each of the 16 weight copies.  The K timed steps
+    are repeated until at least --ref-min-s seconds have been timed (a 20-step region is ~80 ms on the CPU); value
+    = weight bytes of every timed call / total timed seconds."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     import oracle as O
-    ws, x = _cpu_weights(8)
+    ws, x = _cpu_weights(N_COPIES)
     y = np.empty(ROWS, np.float32)
+    xp, yp = x.ctypes.data_as(O._f32p), y.ctypes.data_as(O._f32p)
+    wps = [w.ctypes.data_as(O._u8p) for w in ws]
 
-    def step(i):
-        w = ws[i % 8]
-        O.lib().orc_matvec_q8_0(w.ctypes.data_as(O._u8p), x.ctypes.data_as(O._f32p), y.ctypes.data_as(O._f32p),
-                                ROWS, COLS, 0, 0)
+    def step():
+        for w in wps:
+            O.lib().orc_matvec_q8_0(w, xp, yp, ROWS, COLS, 0, 0)
 
-    for i in range(args.warmup):
-        step(i)
-    t0 = time.perf_counter()
-    for i in range(args.steps):
-        step(i)
-    el = time.perf_counter() - t0
-    gbs = args.steps * QBYTES / el / 1e9
+    for _ in range(args.warmup):
+        step()
+    el, reps = 0.0, 0
+    while reps == 0 or el < args.ref_min_s:
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            step()
+        el += time.perf_counter() - t0
+        reps += 1
+    steps = args.steps * reps
+    gbs = steps * N_COPIES * QBYTES / el / 1e9
     cores = O.lib().orc_num_threads()
     line = {"impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 4),
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / steps * 1e3, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": round(gbs / PUBLISHED_GBS, 3),
             "dtype": "int8xfp32", "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
-            "config": {"workload": f"q8_0_gemv_{ROWS}x{COLS}", "rows": ROWS, "cols": COLS, "weight_copies": 8,
-                       "parallelism": "host threads"},
+            "config": workload_config(world),
+            "execution": "host threads: C++ restatement of MatVecMulQ8_0 (AVX2 order, one row per task)",
+            "timed_repeats": reps, "timed_s": round(el, 3),
             "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
-                             "sample": f"{args.steps} MatVecMulQ8_0 {ROWS}x{COLS} calls rotating 8 weight copies "
-                                       "(C++ restatement of the reference C#, AVX2 order, one row per task)"},
+                             "sample": f"{reps} x {args.steps} steps of {N_COPIES} MatVecMulQ8_0 {ROWS}x{COLS} calls "
+                                       f"({steps * N_COPIES} calls in {el:.2f} s; C++ restatement of the "
+                                       "reference C#, AVX2 order, one row per task)"},
             "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
-
 
 
 # ----------------------------------------------------------------------------------------------------------
@@ -188,14 +204,30 @@ def _peak_tflops():
         return 1590.0, "fallback"
 
 
-def prefill_gemm_leg(dev, L, iters=20):
-    """Batched prefill GEMM (the 512-token prefill workload): X fp32 [512, 4096] ~ N(0,1), W Q8_0 [11008, 4096] ~ N(0,0.02)."""
+def _cpu_loop(fn, seconds):
+    """Calls fn() until `seconds` have passed (at least twice after one untimed call); returns (calls, seconds)."""
+    fn()
+    calls, t0 = 0, time.perf_counter()
+    while True:
+        fn()
+        calls += 1
+        el = time.perf_counter() - t0
+        if el >= seconds and calls >= 2:
+            return calls, el
+
+
+def prefill_gemm_leg(dev, L, iters=20, with_cpu=False, cpu_tokens=64, cpu_s=5.0):
+    """Batched prefill GEMM (the 512-token prefill workload): X fp32 [512, 4096] ~ N(0,1), W Q8_0 [11008, 4096]
+    ~ N(0,0.02).  Device timing with X and Y resident; `e2e` adds the copy of X from pinned host memory and of Y
+    back, every step; `cpu` is the oracle's PrefillPrompt loop (token-parallel MatVecMulQ8_0) on a bounded sample
+    of the same tokens, checked against the device result for those tokens."""
     import torch
     from zeroplatform_b200.ops import QuantizedWeight, quantize
     M, N, K = 512, 11008, 4096
     g = torch.Generator(device=dev)
     g.manual_seed(7)
-    w = QuantizedWeight.upload(8, quantize(8, torch.randn((N, K), generator=g, device=dev) * 0.02), N, K, device=dev)
+    blocks = quantize(8, torch.randn((N, K), generator=g, device=dev) * 0.02)
+    w = QuantizedWeight.upload(8, blocks, N, K, device=dev)
     x = torch.randn((M, K), generator=g, device=dev)
     y = torch.empty((M, N), device=dev)
     s = torch.cuda.current_stream()
@@ -204,25 +236,62 @@ def prefill_gemm_leg(dev, L, iters=20):
         if L.zcu_gemm_q8_0(w.qs.data_ptr(), w.d.data_ptr(), x.data_ptr(), y.data_ptr(), M, N, K, 0, s.cuda_stream):
             raise RuntimeError("zcu_gemm_q8_0 failed")
 
-    for _ in range(3):
-        run()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(s)
-    for _ in range(iters):
-        run()
-    e1.record(s)
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / iters
+    def timed(fn, n):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(n):
+            fn()
+        e1.record(s)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    ms = timed(run, iters)
     flops = 2.0 * M * N * K
     peak, src = _peak_tflops()
     tf = flops / (ms * 1e-3) / 1e12
     status = L.zcu_device_status(1)
-    return {"ms": round(ms, 4), "tflops": round(tf, 1), "weight_GBs": round(w.nbytes / (ms * 1e-3) / 1e9, 1),
-            "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak, "unit": "TFLOP/s",
-                         "frac": round(tf / peak, 3), "peak_source": src},
-            "note": "tcgen05 kind::f16 on fp16 hi/lo pairs of q*d and x (three MMAs per k-step), fp32 "
-                    "accumulate; includes the fp32 -> fp16 hi/lo activation conversion kernel", "device_status": status}
+    hx = torch.empty((M, K), dtype=torch.float32, pin_memory=True)
+    hx.copy_(x)
+    hy = torch.empty((M, N), dtype=torch.float32, pin_memory=True)
+
+    def e2e_call():
+        x.copy_(hx, non_blocking=True)
+        run()
+        hy.copy_(y, non_blocking=True)
+
+    ms_e2e = timed(e2e_call, max(3, iters // 2))
+    out = {"ms": round(ms, 4), "tflops": round(tf, 1), "weight_GBs": round(w.nbytes / (ms * 1e-3) / 1e9, 1),
+           "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak, "unit": "TFLOP/s",
+                        "frac": round(tf / peak, 3), "peak_source": src,
+                        "what": "algorithmic 2*M*N*K / device time (the kernel issues three fp16 products per "
+                                "k-step: hi/lo pairs of q*d and x)"},
+           "e2e": {"value": round(flops / (ms_e2e * 1e-3) / 1e12, 1), "unit": "TFLOP/s", "ms": round(ms_e2e, 4),
+                   "h2d_bytes_per_step": M * K * 4, "d2h_bytes_per_step": M * N * 4,
+                   "api": "zcu_gemm_q8_0 with X copied from pinned host memory and Y copied back, every step"},
+           "note": "tcgen05 kind::f16 on fp16 hi/lo pairs of q*d and x (three MMAs per k-step), fp32 "
+                   "accumulate; includes the fp32 -> fp16 hi/lo activation conversion kernel", "device_status": status}
+    if with_cpu:  # the oracle's PrefillPrompt loop on the first cpu_tokens tokens (test infrastructure)
+        import oracle as O
+        wb = np.ascontiguousarray(blocks.cpu().numpy())
+        xs = np.ascontiguousarray(x[:cpu_tokens].cpu().numpy())
+        ys = np.empty((cpu_tokens, N), np.float32)
+
+        def cpu_call():
+            O.lib().orc_matmul_q8_0(wb.ctypes.data_as(O._u8p), xs.ctypes.data_as(O._f32p),
+                                    ys.ctypes.data_as(O._f32p), cpu_tokens, N, K, 0, 0)
+
+        calls, el = _cpu_loop(cpu_call, cpu_s)
+        ref = y[:cpu_tokens].cpu().numpy().astype(np.float64)
+        err = float(np.max(np.abs(ys - ref)) / max(float(np.max(np.abs(ys))), 1e-30))
+        out["cpu"] = {"value": round(2.0 * cpu_tokens * N * K * calls / el / 1e12, 4), "unit": "TFLOP/s",
+                      "cores": O.lib().orc_num_threads(), "kind": "port",
+                      "sample": f"{calls} passes of PrefillPrompt's token-parallel MatVecMulQ8_0 loop over "
+                                f"{cpu_tokens} of the {M} tokens in {el:.1f} s (C++ restatement of the C#)",
+                      "max_rel_err_vs_device": err}
+    return out
 
 
 def decode_12l_leg(dev, with_cpu, n_prompt=512, n_new=128):
@@ -254,10 +323,25 @@ def decode_12l_leg(dev, with_cpu, n_prompt=512, n_new=128):
     e.close()
     # packed Q8_0 bytes streamed per decode token (every projection and the LM head; one embedding row)
     weight_bytes = sum(int(np.prod(m[k].shape)) for k in ("lm_head", "wq", "wk", "wv", "wo", "wgate", "wup", "wdown"))
+    # K/V bytes read per decode token: every layer reads K and V (fp16) of its attended context; token i of the
+    # n_new attends to n_prompt + i positions (the reference's last-layer length; one fewer below it, ignored)
+    hd = dim // heads
+    mean_ctx = n_prompt + (n_new - 1) / 2.0
+    kv_bytes = layers * 2 * heads * hd * 2 * mean_ctx
+    emb_bytes = dim // 32 * 34
+    per_tok = weight_bytes + kv_bytes + emb_bytes
+    tok_s = n_new / (dec_ms * 1e-3)
+    peak, src = _peaks()
+    gbs = per_tok * tok_s / 1e9
     out = {"prefill_ms": round(pre_ms, 3), "decode_ms": round(dec_ms, 3),
-           "decode_tok_s": round(n_new / (dec_ms * 1e-3), 1), "prompt_tok_s": round(n_prompt / (pre_ms * 1e-3), 1),
+           "decode_tok_s": round(tok_s, 1), "us_per_token": round(dec_ms * 1e3 / n_new, 2),
+           "prompt_tok_s": round(n_prompt / (pre_ms * 1e-3), 1),
            "tokens": int(len(toks)), "weight_bytes_per_token": int(weight_bytes),
-           "decode_weight_GBs": round(weight_bytes * n_new / (dec_ms * 1e-3) / 1e9, 1)}
+           "kv_bytes_per_token_mean": int(kv_bytes),
+           "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                        "frac": round(gbs / peak, 3), "peak_source": src,
+                        "what": "Q8_0 weights (every projection and the LM head) + mean K/V bytes + one embedding "
+                                "row per decode token x tokens/s"}}
     if with_cpu:  # the oracle LlmEngine (C++ restatement of the reference C#) on the host cores, bounded sample
         import oracle as O
         ref = O.Engine(m, total_pages=64, page_size=16)
@@ -271,12 +355,14 @@ def decode_12l_leg(dev, with_cpu, n_prompt=512, n_new=128):
             tok = int(np.argmax(logits))
         t2 = time.perf_counter()
         ref.close()
-        out["cpu"] = {"decode_tok_s": round(n_cpu / (t2 - t1), 2), "prompt_tok_s": round(64 / (t1 - t0), 2),
+        out["cpu"] = {"value": round(n_cpu / (t2 - t1), 2), "unit": "tok/s",
+                      "decode_tok_s": round(n_cpu / (t2 - t1), 2), "prompt_tok_s": round(64 / (t1 - t0), 2),
                       "cores": O.lib().orc_num_threads(), "kind": "port",
                       "sample": f"oracle LlmEngine: 64-token prompt then {n_cpu} greedy decode steps (context 64-80)"}
     return out
 
-def decode_7b_leg(dev, rank, world, batch=32, n_ctx=2048, n_new=128, n_warm=3, layers=32):
+def decode_7b_leg(dev, rank, world, batch=32, n_ctx=2048, n_new=128, n_warm=3, layers=32, with_cpu=False,
+                  cpu_layers=2, cpu_ctx=256, cpu_steps=8):
     """Tensor-parallel 7B decode workload: Llama-2-7B-shaped decoder (32 layers, d 4096, 32 heads, FFN 11008, vocab 32000, Q8_0
     from N(0,0.02)), decode batch 32, each sequence with a 2048-token context in 16-token fp16 pages, then 128
     greedy tokens per sequence; tensor parallel over the `world` GPUs of this job (one engine per rank).
@@ -309,13 +395,21 @@ def decode_7b_leg(dev, rank, world, batch=32, n_ctx=2048, n_new=128, n_warm=3, l
         return quantize(8, torch.randn((rows, cols), generator=g, device=dev) * 0.02)
 
     t0 = time.perf_counter()
-    e.set_weight("tok_emb", 0, q8(1, vocab, dim))
-    e.set_weight("lm_head", 0, q8(2, vocab, dim))
+    host = {}  # the first cpu_layers layers' packed blocks for the CPU slice (rank 0 of a one-GPU run)
+    cpu_layers = min(cpu_layers, layers)
+    for name, seed in (("tok_emb", 1), ("lm_head", 2)):
+        blk = q8(seed, vocab, dim)
+        e.set_weight(name, 0, blk)
+        if with_cpu:
+            host[name] = blk.cpu().numpy()
     shapes = {"wq": (dim, dim), "wk": (dim, dim), "wv": (dim, dim), "wo": (dim, dim), "wgate": (ffn, dim),
               "wup": (ffn, dim), "wdown": (dim, ffn)}
     for layer in range(layers):
         for j, (name, (r, c)) in enumerate(shapes.items()):
-            e.set_weight(name, layer, q8(1000 + 10 * layer + j, r, c))
+            blk = q8(1000 + 10 * layer + j, r, c)
+            e.set_weight(name, layer, blk)
+            if with_cpu and layer < cpu_layers:
+                host.setdefault(name, []).append(blk.cpu().numpy())
     t_weights = time.perf_counter() - t0
     # synthetic contexts: n_ctx - n_warm tokens per sequence (warm-up steps bring them to n_ctx)
     n_fill = n_ctx - n_warm
@@ -344,6 +438,30 @@ def decode_7b_leg(dev, rank, world, batch=32, n_ctx=2048, n_new=128, n_warm=3, l
     kv_rank = batch * mean_ctx * layers * 2 * sh["kv_heads"] * hd * 2
     peak, src = _peaks()
     gbs = (w_rank + kv_rank) / step_s / 1e9
+    cpu = None
+    if with_cpu:  # the oracle LlmEngine on a reduced slice of the same weights (test infrastructure)
+        import oracle as O
+        m = dict(vocab=vocab, dim=dim, layers=cpu_layers, heads=heads, kv_heads=heads, ffn=ffn, context_length=4096,
+                 eps=1e-5, rope_base=10000.0, tok_emb=host["tok_emb"], lm_head=host["lm_head"],
+                 attn_norm=np.ones((cpu_layers, dim), np.float32), ffn_norm=np.ones((cpu_layers, dim), np.float32),
+                 final_norm=np.ones(dim, np.float32))
+        for name in shapes:
+            m[name] = np.stack(host[name])
+        ref = O.Engine(m, total_pages=(cpu_ctx + cpu_steps) // 16 + 2, page_size=16)
+        prompt = np.random.default_rng(9).integers(0, vocab, cpu_ctx).astype(np.int32)
+        logits = ref.prefill(0, prompt, 0)
+        tok = int(np.argmax(logits))
+        t1 = time.perf_counter()
+        for i in range(cpu_steps):
+            tok = int(np.argmax(ref.forward_token(0, tok, cpu_ctx + i)))
+        el = time.perf_counter() - t1
+        ref.close()
+        cpu = {"value": round(cpu_steps / el, 3), "unit": "tok/s", "cores": O.lib().orc_num_threads(),
+               "kind": "port", "ms_per_token_slice": round(el / cpu_steps * 1e3, 2),
+               "sample": f"oracle LlmEngine on a reduced slice: {cpu_layers} of {layers} layers (LM head and "
+                         f"embedding in full), 1 sequence, {cpu_ctx}-token context, {cpu_steps} greedy decode "
+                         f"steps; the full step ({layers} layers x batch {batch} x {n_ctx}-token contexts) is "
+                         "infeasible on the CPU"}
     return {"decode_tok_s": round(batch * n_new / (ms * 1e-3), 1), "ms_per_step": round(ms / n_new, 4),
             "n_gpus": world, "parallelism": f"tp{world}", "layers": layers, "batch": batch, "context_at_start": n_ctx,
             "new_tokens": n_new, "weight_bytes_per_step_per_gpu": int(w_rank),
@@ -355,10 +473,11 @@ def decode_7b_leg(dev, rank, world, batch=32, n_ctx=2048, n_new=128, n_warm=3, l
             "data": "synthetic: weights N(0,0.02) -> Q8_0 on device; contexts are N(0,1) fp16 K/V written with "
                     "zcu_engine_append_kv, not prefilled; greedy tokens from random first ids",
             "timing": "device events around 128 replays of the captured batch step (NCCL all-reduces inside), "
-                      "max over ranks"}
+                      "max over ranks", "cpu": cpu}
 
 
-def moe_leg(dev, rank, world, iters=10, tokens=256, n_experts=8, top_k=2, dim=4096, ffn=14336):
+def moe_leg(dev, rank, world, iters=10, tokens=256, n_experts=8, top_k=2, dim=4096, ffn=14336, with_cpu=False,
+            cpu_s=5.0):
     """Expert-parallel MoE workload: MoE FFN layer, 8 experts x SwiGLU FFN 14336 at d_model 4096, Q4_0 (group 32, fp16 scales)
     from N(0,0.02); 256 tokens of N(0,1) activations, router logits N(0,1), softmax over the top 2.  Expert
     parallel over the `world` GPUs of this job: each rank holds n_experts / world experts and 256 / world of the
@@ -382,15 +501,21 @@ def moe_leg(dev, rank, world, iters=10, tokens=256, n_experts=8, top_k=2, dim=40
                        nccl_id=uid, stream=s.cuda_stream)
     g = torch.Generator(device=dev)
     per = n_experts // world
+    host = {"gate": [], "up": [], "down": []}  # packed Q4_0 blocks for the CPU leg (one-GPU runs)
     for e in range(rank * per, (rank + 1) * per):  # other ranks' experts are ignored by set_expert anyway
         for j, (name, (r, c)) in enumerate((("gate", (ffn, dim)), ("up", (ffn, dim)), ("down", (dim, ffn)))):
             g.manual_seed(7000 + 10 * e + j)
-            m.set_expert(e, name, quantize(4, torch.randn((r, c), generator=g, device=dev) * 0.02))
+            blk = quantize(4, torch.randn((r, c), generator=g, device=dev) * 0.02)
+            m.set_expert(e, name, blk)
+            if with_cpu:
+                host[name].append(blk.cpu().numpy().reshape(-1))
     g.manual_seed(99 + rank)
     x = torch.randn((t_local, dim), generator=g, device=dev)
     logits = torch.randn((t_local, n_experts), generator=g, device=dev)
     res = torch.zeros((t_local, dim), device=dev)
-    for _ in range(3):
+    m.forward(x, res, logits)  # one forward from a zero residual: the values the CPU leg checks
+    res_once = res.cpu().numpy()
+    for _ in range(2):
         m.forward(x, res, logits)
     torch.cuda.synchronize()
     if world > 1:
@@ -411,13 +536,30 @@ def moe_leg(dev, rank, world, iters=10, tokens=256, n_experts=8, top_k=2, dim=40
     peak, src = _peaks()
     gbs_rank = (w_bytes / world) / (ms * 1e-3) / 1e9
     flops = 2.0 * tokens * top_k * 3 * dim * ffn
+    cpu = None
+    if with_cpu:  # the oracle's SparseMoeLayer.Forward token by token on a bounded sample (test infrastructure)
+        import oracle as O
+        eg, eu, ed = (np.ascontiguousarray(np.concatenate(host[k])) for k in ("gate", "up", "down"))
+        xs, lg = x.cpu().numpy(), logits.cpu().numpy()
+        n_done, worst = 0, 0.0
+        t0 = time.perf_counter()
+        while n_done < t_local and (n_done < 2 or time.perf_counter() - t0 < cpu_s):
+            r = np.zeros(dim, np.float32)
+            O.moe_forward(xs[n_done], 4, eg, eu, ed, dim, ffn, n_experts, top_k, r, router_logits=lg[n_done])
+            worst = max(worst, float(np.max(np.abs(r - res_once[n_done])) / max(float(np.max(np.abs(r))), 1e-30)))
+            n_done += 1
+        el = time.perf_counter() - t0
+        cpu = {"value": round(n_done / el, 2), "unit": "tokens/s", "ms_per_layer_256_tokens":
+               round(el / n_done * tokens * 1e3, 1), "cores": O.lib().orc_num_threads(), "kind": "port",
+               "sample": f"SparseMoeLayer.Forward (C++ restatement) for {n_done} of the {tokens} tokens, one at a "
+                         f"time, in {el:.1f} s", "max_rel_err_vs_device": worst}
     return {"ms": round(ms, 4), "tokens_per_s": round(tokens / (ms * 1e-3), 1), "n_gpus": world,
             "parallelism": f"ep{world}", "tokens": tokens, "experts": n_experts, "top_k": top_k, "dim": dim,
             "ffn": ffn, "weight_bytes": w_bytes, "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
             "roofline": {"bound": "hbm", "achieved": round(gbs_rank, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(gbs_rank / peak, 3), "peak_source": src,
                          "what": "Q4_0 expert weight bytes one rank streams per forward / device time"},
-            "data": "synthetic: experts N(0,0.02) -> Q4_0 on device, x and router logits N(0,1)"}
+            "data": "synthetic: experts N(0,0.02) -> Q4_0 on device, x and router logits N(0,1)", "cpu": cpu}
 
 
 # ----------------------------------------------------------------------------------------------------------
@@ -472,14 +614,18 @@ def run_ours(args):
     sampler = ClockSampler(local)
     # graph.replay() launches on torch's current stream: every replay and both events go to `stream`
     with sampler, torch.cuda.stream(stream):
-        # warm-up: at least W steps and at least --min-warmup-s of load so the clock samples cover a busy GPU
+        # clock soak: the timed region of a short run lasts about a millisecond, less than the sampler's period, so
+        # the GPU is first kept busy for --clock-soak-s (replays reported as clock_soak_replays); then exactly W
+        # warm-up steps
         t_w = time.perf_counter()
-        n_w = 0
-        while n_w < args.warmup or time.perf_counter() - t_w < args.min_warmup_s:
+        n_soak = 0
+        while time.perf_counter() - t_w < args.clock_soak_s:
             graph.replay()
-            n_w += 1
-            if n_w % 200 == 0:
+            n_soak += 1
+            if n_soak % 200 == 0:
                 stream.synchronize()
+        for _ in range(args.warmup):
+            graph.replay()
         stream.synchronize()
         barrier()
         torch.cuda.synchronize()
@@ -562,36 +708,40 @@ def run_ours(args):
 
     extra = {}
     if not args.no_extra:
+        with_cpu = rank == 0 and world == 1 and not args.no_cpu
         try:
-            extra["prefill_gemm_512x11008x4096"] = prefill_gemm_leg(dev, L)
+            extra["prefill_gemm_512x11008x4096"] = prefill_gemm_leg(dev, L, with_cpu=with_cpu)
         except Exception as ex:
             extra["prefill_gemm_512x11008x4096"] = {"error": str(ex)[:200]}
         try:
-            extra["decode_12l_d768"] = decode_12l_leg(dev, rank == 0 and world == 1 and not args.no_cpu)
+            extra["decode_12l_d768"] = decode_12l_leg(dev, with_cpu)
         except Exception as ex:
             extra["decode_12l_d768"] = {"error": str(ex)[:200]}
         try:
             extra[f"decode_7b_b32_tp{world}"] = decode_7b_leg(dev, rank, world, layers=args.layers,
-                                                              n_new=args.new_tokens)
+                                                              n_new=args.new_tokens, with_cpu=with_cpu)
         except Exception as ex:
             extra[f"decode_7b_b32_tp{world}"] = {"error": str(ex)[:300]}
         try:
-            extra[f"moe_8x14336_top2_ep{world}"] = moe_leg(dev, rank, world)
+            extra[f"moe_8x14336_top2_ep{world}"] = moe_leg(dev, rank, world, with_cpu=with_cpu)
         except Exception as ex:
             extra[f"moe_8x14336_top2_ep{world}"] = {"error": str(ex)[:300]}
     cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu) else None
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-                "warmup": max(args.warmup, n_w), "ms_per_step": round(ms_per_step, 6), "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": round(value / PUBLISHED_GBS, 2), "dtype": "int8xfp32",
+                "warmup": args.warmup, "clock_soak_replays": n_soak, "ms_per_step": round(ms_per_step, 6),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": round(value / PUBLISHED_GBS, 2),
+                "dtype": "int8xfp32",
                 "data": "synthetic (seeded N(0,0.02) weights quantized on device, N(0,1) activations)",
-                "config": {"workload": f"q8_0_gemv_{ROWS}x{COLS}", "rows": ROWS, "cols": COLS,
-                           "weight_copies": N_COPIES, "l2": "inputs larger than L2: 16 rotating weight copies, 286 MB",
-                           "parallelism": f"replicas x{world}", "graph": "one CUDA graph of 16 GEMV launches per step"},
+                "config": workload_config(world),
+                "execution": f"one CUDA graph of {N_COPIES} GEMV launches (programmatic dependent launch) per step",
                 "pct_hbm_peak": round(100.0 * per_rank_gbs / peak, 1),
                 "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                              "frac": round(achieved / peak, 3), "peak_source": peak_kind,
-                             "traffic": NCU_TRAFFIC_BYTES, "algorithmic_bytes_per_launch": ALGO_BYTES,
+                             "traffic": NCU_TRAFFIC_BYTES,
+                             "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch of "
+                                               "this kernel on this workload (a capture of this command, not this run)",
+                             "algorithmic_bytes_per_launch": ALGO_BYTES,
                              "kernel": "gemv_slab_kernel<XPlain>", "launch_us": round(launch_s * 1e6, 3)},
                 "e2e": e2e, "e2e_weights_copied_per_call": e2e_copy, "gpu_launches": launches,
                 "clocks": sampler.summary(), "cpu_baseline": cpu, "extra_configs": extra}
@@ -675,8 +825,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-extra", action="store_true", help="skip the prefill-GEMM and decoder legs")
-    ap.add_argument("--min-warmup-s", type=float, default=1.0,
-                    help="keep warming up for at least this long (clock samples under load)")
+    ap.add_argument("--clock-soak-s", type=float, default=1.0,
+                    help="keep the GPU busy this long before the warm-up steps (clock samples under load)")
+    ap.add_argument("--ref-min-s", type=float, default=2.0,
+                    help="reference arm: repeat the K timed steps until at least this many seconds are timed")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -238,6 +238,18 @@ typedef struct {
 } zcu_moe_config;
 ZC_API int32_t zcu_moe_create(const zcu_moe_config* cfg, int32_t ep_size, int32_t ep_rank, const uint8_t* nccl_id,
                               void* stream, void** moe);
+/* The expert-parallel exchange plan zcu_moe_forward follows on rank ep_rank (host only, no GPU needed).
+ * counts_all [ep_size][n_experts] are the all-gathered routing counts (rows rank src sends to expert e; expert e
+ * lives on rank e / (n_experts / ep_size)).  Out (each may be NULL): send_rows [ep_size] rows this rank sends to
+ * each peer (its rows leave in expert order, one contiguous run per peer), recv_rows [ep_size] rows it receives
+ * from each, recv_cnt [ep_size][n_experts / ep_size] rows per (source, local expert), perm [total] the position of
+ * each received row (arrival order: by source, then local expert) in the [local expert][source] order the expert
+ * GEMMs read.  Returns the total received (>= 0), -2 for bad arguments (n_experts % ep_size, negative counts) or
+ * -6 when perm_cap is below the total.  No counterpart in the reference (SparseMoeLayer runs every expert
+ * locally, SparseMoeLayer.cs:32-125). */
+ZC_API int32_t zcu_moe_ep_plan(int32_t n_experts, int32_t ep_size, int32_t ep_rank, const int32_t* counts_all,
+                               int32_t* send_rows, int32_t* recv_rows, int32_t* recv_cnt, int32_t* perm,
+                               int32_t perm_cap);
 ZC_API int32_t zcu_moe_destroy(void* moe);
 ZC_API const char* zcu_moe_last_error(void* moe);
 /* Expert `expert`'s gate (which 0, [ffn][dim]), up (1, [ffn][dim]) or down (2, [dim][ffn]) projection as the

@@ -20,13 +20,17 @@ def _check(line, n_gpus):
         assert key in line, key
     assert line["n_gpus"] == n_gpus and line["higher_is_better"] is True and line["unit"] == "GB/s"
     assert line["value"] > 0 and line["config"]["workload"] == "q8_0_gemv_4096x4096"
+    sys.path.insert(0, ROOT)
+    import bench
+    assert line["config"] == bench.workload_config(n_gpus)  # the GPU arm reports the same config
+    assert line["warmup"] == 3 and line["timed_s"] >= 0.5
     cb = line["cpu_baseline"]
     assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == line["value"] and cb["sample"]
     assert line["e2e"] == {"value": line["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
 
 
 def test_reference_arm_prints_one_contract_line():
-    out = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "2", "--warmup", "3"],
+    out = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "2", "--warmup", "3", "--ref-min-s", "0.5"],
                          cwd=ROOT, capture_output=True, text=True, timeout=600, check=True).stdout
     lines = _lines(out)
     assert len(lines) == 1

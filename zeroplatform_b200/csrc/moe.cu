@@ -222,6 +222,7 @@ struct Moe {
   float* yl = nullptr;      // local expert outputs [recv rows][dim]
   float* ys = nullptr;      // outputs back in this rank's pair order [pairs][dim]
   int32_t* perm = nullptr;  // receive order -> local expert order
+  int32_t* cnt_all = nullptr;  // [1 + ep_size][E]: this rank's counts, then every rank's (all-gather)
   size_t cap_rows = 0;      // rows the per-expert buffers hold
   void* gemm_ws = nullptr;
   size_t gemm_ws_bytes = 0;
@@ -229,6 +230,48 @@ struct Moe {
   int timeout_ms = 120000;
   std::string err;
 };
+
+// Expert-parallel exchange plan of one forward on rank `rank` of W (host only).  counts_all[src * E + e] is the
+// number of (token, slot) rows rank src routes to expert e; expert e lives on rank e / (E / W).  A rank's rows
+// leave in expert order, so the rows for peer p are one contiguous run (send_rows[p] of them); the rows it
+// receives arrive grouped by source and, within a source, by local expert (recv_cnt[src][le]).  perm[i] is the
+// position of received row i in the expert-contiguous order [local expert][source][row] that the expert GEMMs
+// read; local_cnt[le] is each local expert's row total.
+struct EpPlan {
+  std::vector<int> send_rows, recv_rows, recv_cnt, local_cnt, perm;
+  int total_recv = 0;
+};
+
+int moe_ep_plan(int E, int W, int rank, const int32_t* counts_all, EpPlan* p) {
+  if (E <= 0 || W <= 0 || E % W || rank < 0 || rank >= W || !counts_all || !p) return kBadArgument;
+  const int epr = E / W, e_begin = rank * epr;
+  for (size_t i = 0; i < (size_t)W * E; ++i)
+    if (counts_all[i] < 0) return kBadArgument;
+  p->send_rows.assign(W, 0);
+  p->recv_rows.assign(W, 0);
+  p->recv_cnt.assign((size_t)W * epr, 0);
+  p->local_cnt.assign(epr, 0);
+  for (int e = 0; e < E; ++e) p->send_rows[e / epr] += counts_all[(size_t)rank * E + e];
+  long long total = 0;
+  for (int src = 0; src < W; ++src)
+    for (int le = 0; le < epr; ++le) {
+      const int n = counts_all[(size_t)src * E + e_begin + le];
+      p->recv_cnt[(size_t)src * epr + le] = n;
+      p->recv_rows[src] += n;
+      p->local_cnt[le] += n;
+      total += n;
+    }
+  if (total > 0x7fffffffLL) return kTooLarge;
+  p->total_recv = (int)total;
+  p->perm.assign(p->total_recv, 0);
+  std::vector<int> base(epr, 0), filled(epr, 0);
+  for (int le = 1; le < epr; ++le) base[le] = base[le - 1] + p->local_cnt[le - 1];
+  int i = 0;
+  for (int src = 0; src < W; ++src)
+    for (int le = 0; le < epr; ++le)
+      for (int r = 0; r < p->recv_cnt[(size_t)src * epr + le]; ++r) p->perm[i++] = base[le] + filled[le]++;
+  return kOk;
+}
 
 #define M_CUDA(call)                                             \
   do {                                                           \
@@ -324,6 +367,21 @@ using zc::Moe;
 
 extern "C" {
 
+int32_t zcu_moe_ep_plan(int32_t n_experts, int32_t ep_size, int32_t ep_rank, const int32_t* counts_all,
+                        int32_t* send_rows, int32_t* recv_rows, int32_t* recv_cnt, int32_t* perm, int32_t perm_cap) {
+  using namespace zc;
+  EpPlan p;
+  const int rc = moe_ep_plan(n_experts, ep_size, ep_rank, counts_all, &p);
+  if (rc != kOk) return rc;
+  if (perm_cap < p.total_recv || (p.total_recv > 0 && !perm)) return kTooLarge;
+  const int epr = n_experts / ep_size;
+  if (send_rows) std::copy(p.send_rows.begin(), p.send_rows.end(), send_rows);
+  if (recv_rows) std::copy(p.recv_rows.begin(), p.recv_rows.end(), recv_rows);
+  if (recv_cnt) std::copy(p.recv_cnt.begin(), p.recv_cnt.begin() + (size_t)ep_size * epr, recv_cnt);
+  if (p.total_recv > 0) std::copy(p.perm.begin(), p.perm.end(), perm);
+  return p.total_recv;
+}
+
 int32_t zcu_moe_create(const zcu_moe_config* cfg, int32_t ep_size, int32_t ep_rank, const uint8_t* nccl_id,
                        void* stream, void** out) {
   using namespace zc;
@@ -378,6 +436,7 @@ int32_t zcu_moe_create(const zcu_moe_config* cfg, int32_t ep_size, int32_t ep_ra
   step(malloc_into(M, &M->xs, pairs * 2 * c.dim));
   step(malloc_into(M, &M->ys, pairs * c.dim));
   step(malloc_into(M, &M->status, 1));
+  step(malloc_into(M, &M->cnt_all, (size_t)(ep_size + 1) * c.n_experts));
   if (rc == kOk) rc = ensure_rows(M, std::max<size_t>(pairs, 64));
   if (rc == kOk && cudaMemset(M->status, 0, sizeof(int)) != cudaSuccess) rc = kCudaError;
   if (rc != kOk) {
@@ -477,61 +536,42 @@ int32_t zcu_moe_forward(void* moe, const float* xnorm, const float* router_logit
   std::vector<int> cnt(E, 0);
   if (T > 0) M_CUDA(cudaMemcpyAsync(cnt.data(), M->counts, E * sizeof(int), cudaMemcpyDeviceToHost, s));
   M_RC(wait_stream(M));
-  // rows this rank sends to each peer (expert-sorted rows are already grouped by owner rank)
   const int epr = M->e_count;
-  std::vector<int> send_rows(W, 0), recv_rows(W, 0);
-  for (int e = 0; e < E; ++e) send_rows[e / epr] += cnt[e];
   const size_t row_bytes = (size_t)2 * c.dim * sizeof(__half);  // one hi / lo row
-  std::vector<int> local_cnt(epr, 0);  // rows per local expert over all sources
-  std::vector<int> recv_cnt((size_t)W * epr, 0);  // [source][local expert]
   if (W == 1) {
-    for (int le = 0; le < epr; ++le) local_cnt[le] = cnt[le];
+    std::vector<int> local_cnt(cnt.begin(), cnt.begin() + epr);
     M_RC(ensure_rows(M, std::max<size_t>(P, 1)));
     if (P > 0) M_RC(run_local_experts(M, M->xs, local_cnt, M->ys));
   } else {
     // exchange per-expert counts: every rank learns how many rows of each of its experts each peer sends
-    int32_t* dcnt = nullptr;
-    M_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&dcnt), (size_t)(W + 1) * E * sizeof(int32_t), s));
+    int32_t* dcnt = M->cnt_all;
     M_CUDA(cudaMemcpyAsync(dcnt, cnt.data(), E * sizeof(int32_t), cudaMemcpyHostToDevice, s));
-    int rc = comm_allgather_bytes(M->comm, dcnt, dcnt + E, E * sizeof(int32_t), s, &M->err);
+    M_RC(comm_allgather_bytes(M->comm, dcnt, dcnt + E, E * sizeof(int32_t), s, &M->err));
     std::vector<int> all((size_t)W * E);
-    if (rc == kOk && cudaMemcpyAsync(all.data(), dcnt + E, all.size() * sizeof(int32_t), cudaMemcpyDeviceToHost, s) != cudaSuccess)
-      rc = kCudaError;
-    cudaFreeAsync(dcnt, s);
-    if (rc != kOk) return rc;
+    M_CUDA(cudaMemcpyAsync(all.data(), dcnt + E, all.size() * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
     M_RC(wait_stream(M));
-    for (int src = 0; src < W; ++src)
-      for (int le = 0; le < epr; ++le) {
-        recv_cnt[(size_t)src * epr + le] = all[(size_t)src * E + M->e_begin + le];
-        recv_rows[src] += recv_cnt[(size_t)src * epr + le];
-        local_cnt[le] += recv_cnt[(size_t)src * epr + le];
-      }
-    int total_recv = 0;
-    for (int r : recv_rows) total_recv += r;
+    EpPlan plan;
+    if (moe_ep_plan(E, W, M->ep_rank, all.data(), &plan) != kOk) {
+      M->err = "inconsistent expert counts";
+      return kBadArgument;
+    }
+    const int total_recv = plan.total_recv;
+    const std::vector<int>& local_cnt = plan.local_cnt;
+    const std::vector<int32_t>& perm = plan.perm;
     M_RC(ensure_rows(M, std::max(total_recv, 1)));
     // dispatch: my expert-sorted rows to their owners; received rows land in [source][local expert] order
     std::vector<size_t> sb(W), so(W), rb(W), ro(W);
     size_t a = 0, b = 0;
     for (int p = 0; p < W; ++p) {
-      sb[p] = (size_t)send_rows[p] * row_bytes;
+      sb[p] = (size_t)plan.send_rows[p] * row_bytes;
       so[p] = a;
       a += sb[p];
-      rb[p] = (size_t)recv_rows[p] * row_bytes;
+      rb[p] = (size_t)plan.recv_rows[p] * row_bytes;
       ro[p] = b;
       b += rb[p];
     }
     M_RC(comm_alltoallv_bytes(M->comm, M->xs, sb.data(), so.data(), M->xr, rb.data(), ro.data(), s, &M->err));
     // [source][local expert] -> [local expert][source] so that each expert's rows are contiguous
-    std::vector<int32_t> perm(total_recv);
-    {
-      std::vector<int> base(epr, 0);
-      for (int le = 1; le < epr; ++le) base[le] = base[le - 1] + local_cnt[le - 1];
-      std::vector<int> filled(epr, 0);
-      int i = 0;
-      for (int src = 0; src < W; ++src)
-        for (int le = 0; le < epr; ++le)
-          for (int r = 0; r < recv_cnt[(size_t)src * epr + le]; ++r) perm[i++] = base[le] + filled[le]++;
-    }
     if (total_recv > 0) {
       M_CUDA(cudaMemcpyAsync(M->perm, perm.data(), perm.size() * sizeof(int32_t), cudaMemcpyHostToDevice, s));
       // xr -> expert-contiguous copy in hbuf's place is not possible (different widths): use gu as scratch
