@@ -89,11 +89,45 @@ def test_moe_with_router_weights_and_uneven_expert_load():
     m.set_router(router)
     res = torch.from_numpy(res0.copy()).cuda()
     idx, _ = m.forward(torch.from_numpy(x).cuda(), res)
-    agree = float(np.mean(idx == ref_idx))
-    assert agree >= 0.99, agree  # fp32 router sums in another order: only exact near-ties could flip
-    if agree == 1.0:
-        assert _rel(res.cpu().numpy(), ref, res0) <= TOL
+    same = np.all(idx == ref_idx, axis=1)  # tokens whose routing agrees with the oracle's
+    flips = int(T - same.sum())
+    print(f"router-weight routing: {flips} of {T} tokens routed differently")
+    assert flips <= max(1, T // 100)  # fp32 router sums in another order: only exact near-ties could flip
+    got = res.cpu().numpy()
+    assert _rel(got[same], ref[same], res0[same]) <= TOL  # every token that routed alike matches the oracle
     m.close()
+
+
+def test_moe_layer_at_the_benchmark_shape_matches_oracle():
+    """The benchmarked layer itself: 8 experts x SwiGLU FFN 14336 at d_model 4096, top-2, Q4_0 (group 32, fp16
+    scales) from N(0,0.02), N(0,1) activations and router logits -- checked on 32 tokens (the expert weights are
+    quantized on the device, bit-identical to the oracle's quantizer, then copied to the host for the oracle)."""
+    from zeroplatform_b200.moe import SparseMoeLayer
+    from zeroplatform_b200.ops import quantize
+    E, k, dim, ffn, T = 8, 2, 4096, 14336, 32
+    g = torch.Generator(device="cuda")
+    m = SparseMoeLayer(E, k, dim, ffn, qtype=4, max_tokens=T)
+    host = {"gate": [], "up": [], "down": []}
+    for e in range(E):
+        for j, (name, (r, c)) in enumerate((("gate", (ffn, dim)), ("up", (ffn, dim)), ("down", (dim, ffn)))):
+            g.manual_seed(7000 + 10 * e + j)
+            blk = quantize(4, torch.randn((r, c), generator=g, device="cuda") * 0.02)
+            m.set_expert(e, name, blk)
+            host[name].append(blk.cpu().numpy().reshape(-1))
+            del blk
+    eg, eu, ed = (np.stack(host[n]) for n in ("gate", "up", "down"))
+    rng = np.random.default_rng(12)
+    x = rng.standard_normal((T, dim), dtype=np.float32)
+    logits = rng.standard_normal((T, E), dtype=np.float32)
+    res0 = rng.standard_normal((T, dim), dtype=np.float32)
+    ref, ref_idx = _oracle(4, eg, eu, ed, x, res0, E, k, dim, ffn, logits=logits)
+    res = torch.from_numpy(res0.copy()).cuda()
+    idx, w = m.forward(torch.from_numpy(x).cuda(), res, torch.from_numpy(logits).cuda())
+    m.close()
+    assert np.array_equal(idx, ref_idx)
+    err = _rel(res.cpu().numpy(), ref, res0)
+    print(f"moe 8x14336 d4096 top-2 Q4_0: max-rel err {err:.3e}")
+    assert err <= TOL
 
 
 def _free_port():
@@ -135,10 +169,12 @@ def _ep_worker(rank, world, port, out_dir):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_expert_parallel_2_matches_oracle():
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_expert_parallel_matches_oracle(world):
+    """EP over `world` GPUs (8 experts: 4, 2 or 1 per rank), each rank routing its own 24 tokens."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
-    world = 2
     with tempfile.TemporaryDirectory() as d:
         mp.start_processes(_ep_worker, args=(world, _free_port(), d), nprocs=world, join=True, start_method="spawn")
         out = [json.load(open(os.path.join(d, f"rank{r}.json"))) for r in range(world)]

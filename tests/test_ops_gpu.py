@@ -133,3 +133,31 @@ def test_bridge_gemm_f32_strided(m, n, k, trans):
 
 def test_flash_attention_is_not_handled():
     assert L().zc_flash_attention_f32(1, 1, 1, 8, 8, 1.0, 0, 1, 1, 1, None, None, None, None, None) == -1
+
+
+def test_bounded_peer_wait_runs_out_and_reports():
+    """The tensor-parallel all-reduce's reduce kernel waits (bounded) for every peer's epoch flag.  Here it runs on
+    one GPU against a receive area of 2 (and 8) ranks where no peer ever publishes: the wait must give up after
+    the shortened limit, record code 21 with what it saw (it needed epoch 1; rank 0's flag is 1, the others 0),
+    and return -- and the context must stay usable for the next kernel."""
+    import time
+    from zeroplatform_b200 import _lib
+    from zeroplatform_b200.ops import QuantizedWeight
+    L = _lib.lib()
+    for ranks in (2, 8):
+        seen = (ctypes.c_uint32 * 16)()
+        t0 = time.perf_counter()
+        rc = L.zcu_peer_wait_selftest(ranks, 200, seen)
+        el = time.perf_counter() - t0
+        assert rc == 21, rc
+        assert 0.15 < el < 5.0, el
+        assert seen[4] == 1 and seen[5] == 1 and all(seen[5 + q] == 0 for q in range(1, ranks))
+    assert L.zcu_peer_wait_selftest(1, 200, None) == -2 and L.zcu_peer_wait_selftest(2, 0, None) == -2
+    rng = np.random.default_rng(0)
+    w = rng.standard_normal((64, 256), dtype=np.float32) * np.float32(0.02)
+    blocks = O.quantize_q8_0(w)
+    x = rng.standard_normal(256, dtype=np.float32)
+    y = QuantizedWeight.upload(8, blocks, 64, 256).gemv(torch.from_numpy(x).cuda())
+    torch.cuda.synchronize()
+    assert rel_err(y.cpu().numpy(), O.matvec(8, blocks, x, 64, 256)) <= 1e-5
+    assert L.zcu_device_status(1) == 0  # the self-test used its own status word

@@ -116,6 +116,7 @@ SIGNATURES.update({
     "zcu_moe_set_router": (i32, [vp, vp, sz]),
     "zcu_moe_forward": (i32, [vp, vp, vp, vp, i32, vp, vp]),
     "zcu_moe_ep_plan": (i32, [i32, i32, i32, vp, vp, vp, vp, vp, i32]),
+    "zcu_peer_wait_selftest": (i32, [i32, i32, vp]),
 })
 
 

@@ -120,14 +120,14 @@ __global__ void arp_push_kernel(const float* __restrict__ src, int splits, size_
 // Thread 0 of the calling CTA waits (bounded) until every rank's flag in this rank's area carries at least the
 // epoch e; returns 0 (and records the failure) when the wait ran out.
 __device__ __forceinline__ int wait_flags(const unsigned int* flags, int W, unsigned int e, unsigned int* state,
-                                          int* status) {
+                                          int* status, uint64_t wait_ns) {
   const uint64_t t0 = now_ns();
   for (int r = 0; r < W; ++r) {
     uint32_t polls = 0;
     // a peer may already have published e + 1 (it finished this all-reduce and pushed the next one into the
     // other buffer), so wait for "at least e", wrap-around safe
     while ((int)(ld_acquire_sys(flags + r) - e) < 0) {
-      if (++polls > AR_WAIT_POLLS || now_ns() - t0 > AR_WAIT_NS) {
+      if (++polls > AR_WAIT_POLLS || now_ns() - t0 > wait_ns) {
         atomicExch(status, 21);
         // what the wait saw, for the host's error message: the epoch it needed and every rank's flag
         state[4] = e;
@@ -162,7 +162,7 @@ __global__ void arp_reduce_rmsnorm_kernel(float* __restrict__ x, int dim, size_t
   __shared__ int ok;
   __shared__ float red[32];
   const unsigned int e = *reinterpret_cast<volatile unsigned int*>(epoch) + 1;
-  if (threadIdx.x == 0) ok = wait_flags(flags, W, e, epoch, status);
+  if (threadIdx.x == 0) ok = wait_flags(flags, W, e, epoch, status, AR_WAIT_NS);
   __syncthreads();
   if (ok) {
     const float* buf = area + (size_t)(e & 1) * W * cap + (size_t)blockIdx.x * dim;
@@ -192,10 +192,10 @@ __global__ void arp_reduce_rmsnorm_kernel(float* __restrict__ x, int dim, size_t
 
 __global__ void arp_reduce_kernel(float* __restrict__ x, size_t n, size_t cap, const float* __restrict__ area,
                                   const unsigned int* __restrict__ flags, int W, unsigned int* __restrict__ epoch,
-                                  unsigned int* __restrict__ departures, int* __restrict__ status) {
+                                  unsigned int* __restrict__ departures, int* __restrict__ status, uint64_t wait_ns) {
   __shared__ int ok;
   const unsigned int e = *reinterpret_cast<volatile unsigned int*>(epoch) + 1;
-  if (threadIdx.x == 0) ok = wait_flags(flags, W, e, epoch, status);
+  if (threadIdx.x == 0) ok = wait_flags(flags, W, e, epoch, status, wait_ns);
   __syncthreads();
   if (ok) {
     const float* buf = area + (size_t)(e & 1) * W * cap;
@@ -332,8 +332,49 @@ int arp_allreduce_sum(P2pAllReduce* A, float* x, size_t n, cudaStream_t s) {
   arp_push_kernel<false><<<grid, 256, 0, s>>>(x, 1, 0, (const float*)nullptr, n, A->cap, A->peers, A->W, A->me,
                                               A->state, A->state + 1);
   if (cudaPeekAtLastError() != cudaSuccess) return kCudaError;
-  arp_reduce_kernel<<<grid, 256, 0, s>>>(x, n, A->cap, A->area, A->flags, A->W, A->state, A->state + 2, A->status);
+  arp_reduce_kernel<<<grid, 256, 0, s>>>(x, n, A->cap, A->area, A->flags, A->W, A->state, A->state + 2, A->status,
+                                         AR_WAIT_NS);
   return cudaPeekAtLastError() == cudaSuccess ? kOk : kCudaError;
+}
+
+int arp_wait_selftest(int W, int wait_ms, unsigned int* seen, std::string* err) {
+  if (W < 2 || W > ARP_MAX_RANKS || wait_ms < 1 || wait_ms > 5000 || !seen) {
+    if (err) *err = "peer wait self-test: W must be 2 .. 8, wait_ms 1 .. 5000";
+    return kBadArgument;
+  }
+  constexpr size_t cap = 256;
+  const size_t area_bytes = 2 * (size_t)W * cap * sizeof(float);
+  // one allocation: [area][flags: 16 words][state: 16 words][status: 4 words][x: cap floats]
+  const size_t total = area_bytes + 64 + 64 + 16 + cap * sizeof(float);
+  char* base = nullptr;
+  if (cudaMalloc(&base, total) != cudaSuccess) {
+    cudaGetLastError();
+    if (err) *err = "peer wait self-test: allocation failed";
+    return kOutOfMemory;
+  }
+  float* area = reinterpret_cast<float*>(base);
+  unsigned int* flags = reinterpret_cast<unsigned int*>(base + area_bytes);
+  unsigned int* state = reinterpret_cast<unsigned int*>(base + area_bytes + 64);
+  int* status = reinterpret_cast<int*>(base + area_bytes + 128);
+  float* x = reinterpret_cast<float*>(base + area_bytes + 144);
+  int rc = cudaMemset(base, 0, total) == cudaSuccess ? kOk : kCudaError;
+  const unsigned int one = 1;  // rank 0 has published epoch 1; no peer ever does
+  if (rc == kOk && cudaMemcpy(flags, &one, sizeof(one), cudaMemcpyHostToDevice) != cudaSuccess) rc = kCudaError;
+  int code = 0;
+  if (rc == kOk) {
+    arp_reduce_kernel<<<1, 256>>>(x, cap, cap, area, flags, W, state, state + 2, status,
+                                  (uint64_t)wait_ms * 1000000ull);
+    if (cudaDeviceSynchronize() != cudaSuccess) rc = kCudaError;
+  }
+  if (rc == kOk && (cudaMemcpy(&code, status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess ||
+                    cudaMemcpy(seen, state, 16 * sizeof(unsigned int), cudaMemcpyDeviceToHost) != cudaSuccess))
+    rc = kCudaError;
+  cudaFree(base);
+  if (rc != kOk) {
+    if (err) *err = std::string("peer wait self-test: ") + cudaGetErrorString(cudaGetLastError());
+    return rc;
+  }
+  return code;
 }
 
 int arp_push_partials(P2pAllReduce* A, const float* part, int splits, size_t n, const float* resid, cudaStream_t s) {

@@ -20,6 +20,7 @@
 
 #include "../../include/zero_tensor.h"
 #include "../../include/zero_tensor_cuda.h"
+#include "allreduce_p2p.h"
 #include "common.cuh"
 #include "kernels.h"
 
@@ -677,6 +678,16 @@ int32_t zcu_gemm_q4_0(const uint8_t* qs, const uint16_t* d, const float* x, floa
   ZC_RC(stream_scratch(s, 2, bytes, false, &ws));
   ZC_RC(device_status_ptr(&status));
   return gemm_q4_0_tc(qs, d, x, y, (int)m, (int)n_rows, (int)k_cols, accumulate, ws, bytes, status, s);
+}
+
+int32_t zcu_peer_wait_selftest(int32_t ranks, int32_t wait_ms, uint32_t* seen) {
+  t_last_error.clear();
+  unsigned int st[16] = {};
+  std::string err;
+  const int rc = arp_wait_selftest(ranks, wait_ms, st, &err);
+  if (rc < 0) return fail(rc, err.c_str());
+  if (seen) std::memcpy(seen, st, sizeof(st));
+  return rc;
 }
 
 int32_t zcu_device_status(int32_t reset) {
