@@ -209,6 +209,11 @@ ZC_API int32_t zcu_engine_decode(void* engine, const int32_t* seq_ids, const int
 ZC_API int32_t zcu_engine_generate(void* engine, int32_t seq_id, const int32_t* prompt, int32_t n_prompt,
                                    int32_t n_new, float repetition_penalty, int32_t eos_token, int32_t* out_tokens,
                                    float* timing_ms);
+/* Which form zcu_engine_generate runs a generation step in: 1 = one cooperative kernel per token (one GPU, shapes
+ * that fit it: head size 64 or 128, dim / ffn / heads*hd multiples of 256, heads x dim <= 65536), 0 = the captured
+ * graph of per-operator kernels (ZCU_FUSED_DECODE=0 in the environment forces it), -1 = not decided yet (no
+ * generate call so far).  `why` (may be NULL) receives the reason the one-kernel form is not used. */
+ZC_API int32_t zcu_engine_step_kind(void* engine, char* why, int32_t cap);
 /* Batched greedy generation (GenerateStreamAsync for `batch` live sequences at once, repetition penalty 1):
  * tokens[b] is fed at position seq_len(seq_ids[b]); each of n_new steps runs ForwardToken for every sequence
  * and samples greedily, replayed from one captured CUDA graph (collectives included).  out_tokens[b * n_new + i]

@@ -117,6 +117,7 @@ SIGNATURES.update({
     "zcu_moe_forward": (i32, [vp, vp, vp, vp, i32, vp, vp]),
     "zcu_moe_ep_plan": (i32, [i32, i32, i32, vp, vp, vp, vp, vp, i32]),
     "zcu_peer_wait_selftest": (i32, [i32, i32, vp]),
+    "zcu_engine_step_kind": (i32, [vp, vp, i32]),
 })
 
 

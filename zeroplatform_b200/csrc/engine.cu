@@ -34,6 +34,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <map>
@@ -161,6 +162,12 @@ struct Engine {
   std::vector<int> free_stack;
   std::vector<int> free_rows;
   std::map<int, Seq> seqs;
+  // one-kernel generation step (decode_fused.cu) for one sequence on one GPU, set up at the first generate
+  bool fused_tried = false, fused_ok = false;
+  FusedStepArgs fused{};
+  size_t fused_smem = 0;
+  int fused_sms = 0;
+  std::string fused_why;
   std::map<int, cudaGraphExec_t> step_graphs;   // decode step graphs (B = 1 generation)
   std::map<int, cudaGraphExec_t> batch_graphs;  // batched generation step graphs, by batch size
   std::string err;
@@ -480,6 +487,94 @@ int upload_q8(Engine* E, DevW& dst, size_t dst_row, const void* src, int full_bl
   E_RC(repack_q8_0(static_cast<const uint8_t*>(aos), dst.qs + dst_row * dst.k, dst.d + dst_row * (dst.k / QK), nr,
                    dst.k, E->stream));
   E_CUDA(cudaStreamSynchronize(E->stream));
+  return kOk;
+}
+
+// Sets up the one-kernel generation step when this engine's shapes fit it (tp_size 1; ZCU_FUSED_DECODE=0 in the
+// environment keeps the captured multi-kernel step instead).  Leaves E->fused_ok false otherwise.
+int setup_fused(Engine* E) {
+  if (E->fused_tried) return kOk;
+  E->fused_tried = true;
+  const char* env = std::getenv("ZCU_FUSED_DECODE");
+  if (env && env[0] == '0') {
+    E->fused_why = "disabled by ZCU_FUSED_DECODE=0";
+    return kOk;
+  }
+  if (E->tp_size != 1) {
+    E->fused_why = "tensor parallel";
+    return kOk;
+  }
+  const zcu_engine_config& c = E->cfg;
+  FusedStepArgs& a = E->fused;
+  a.dim = c.dim;
+  a.layers = c.layers;
+  a.hq = E->hq;
+  a.hkv = E->hkv;
+  a.hd = E->hd;
+  a.ffn = E->ffn;
+  a.vocab = E->vocab;
+  a.q_dim = E->q_dim;
+  a.kv_dim = E->kv_dim;
+  a.qkv_dim = E->qkv_dim;
+  a.eps = c.eps;
+  int sms = 0;
+  E_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, E->device));
+  const char* why = nullptr;
+  if (fused_step_plan(a, sms, c.max_pages_per_seq * c.page_size, &E->fused_smem, &why) != kOk) {
+    E->fused_why = why ? why : "unsupported shape";
+    return kOk;
+  }
+  std::vector<FusedLayerW> lw(c.layers);
+  for (int l = 0; l < c.layers; ++l)
+    lw[l] = FusedLayerW{E->wqkv[l].qs, E->wqkv[l].d, E->wo[l].qs, E->wo[l].d,
+                        E->wgu[l].qs,  E->wgu[l].d,  E->wdown[l].qs, E->wdown[l].d};
+  FusedLayerW* dlw = nullptr;
+  E_RC(dalloc(E, &dlw, lw.size()));
+  E_CUDA(cudaMemcpy(dlw, lw.data(), lw.size() * sizeof(FusedLayerW), cudaMemcpyHostToDevice));
+  float* scratch = nullptr;
+  E_RC(dalloc(E, &scratch, fused_step_scratch_floats(a, sms)));
+  unsigned* ctl = nullptr;
+  E_RC(dalloc(E, &ctl, (size_t)(2 + a.hq)));
+  E_CUDA(cudaMemset(ctl, 0, (2 + a.hq) * sizeof(unsigned)));
+  a.part = scratch;
+  a.P = a.part + (size_t)a.hq * a.splits * (a.hd + 2);
+  a.qbuf = a.P + (size_t)a.hq * a.dim;
+  a.hbuf = a.qbuf + a.q_dim;
+  a.x = a.hbuf + a.ffn;
+  a.pairs = reinterpret_cast<int2*>(a.x + ((a.dim + 3) / 4 * 4));
+  a.ctl = ctl;
+  a.lw = dlw;
+  a.emb_qs = E->tok_emb.qs;
+  a.emb_d = E->tok_emb.d;
+  a.attn_norm = E->attn_norm;
+  a.ffn_norm = E->ffn_norm;
+  a.final_norm = E->final_norm;
+  a.lm_qs = E->lm_head.qs;
+  a.lm_d = E->lm_head.d;
+  a.cos_t = E->cos_t;
+  a.sin_t = E->sin_t;
+  a.max_pos = E->max_pos;
+  a.kpool = E->kpool;
+  a.vpool = E->vpool;
+  a.layer_pool_elems = E->layer_pool_elems;
+  a.page_size = c.page_size;
+  a.max_pages = c.max_pages_per_seq;
+  a.num_pages = c.total_pages;
+  a.page_table = E->page_table;
+  a.rows = E->rows;
+  a.pos = E->pos;
+  a.quirk = c.reference_causal_quirk ? 1 : 0;
+  a.logits = E->logits;
+  a.tokens = E->tokens;
+  a.gen_out = E->gen_out;
+  a.gen_step = E->gen_step;
+  a.past = E->gen_past;
+  a.past_len = E->gen_past_len;
+  a.done = E->gen_done;
+  a.past_cap = E->gen_cap;
+  a.status = E->status;
+  E->fused_sms = sms;
+  E->fused_ok = true;
   return kOk;
 }
 
@@ -892,7 +987,19 @@ int32_t zcu_engine_generate(void* engine, int32_t seq_id, const int32_t* prompt,
   E_CUDA(cudaMemcpyAsync(E->rows, &row, 4, cudaMemcpyHostToDevice, E->stream));
   E_RC(wait(E));
   E_CUDA(cudaEventRecord(ev[1], E->stream));
-  if (n_new > 0) {
+  if (n_new > 0) E_RC(setup_fused(E));
+  if (n_new > 0 && E->fused_ok) {
+    // one cooperative kernel per generated token (decode_fused.cu)
+    E->fused.penalty = repetition_penalty;
+    E->fused.eos = eos_token;
+    for (int i = 0; i < n_new; ++i) {
+      const int rc = fused_step_launch(E->fused, E->fused_sms, E->fused_smem, E->stream);
+      if (rc != kOk) {
+        E->err = std::string("fused generation step launch failed: ") + cudaGetErrorString(cudaGetLastError());
+        return rc;
+      }
+    }
+  } else if (n_new > 0) {
     // one graph per (penalty, eos) setting; the captured pointers are the engine's fixed buffers
     const int key = (int)(repetition_penalty * 1000.0f) * 1000003 + eos_token;
     auto it = E->step_graphs.find(key);
@@ -923,6 +1030,16 @@ int32_t zcu_engine_generate(void* engine, int32_t seq_id, const int32_t* prompt,
     return kCudaError;
   }
   return produced;
+}
+
+int32_t zcu_engine_step_kind(void* engine, char* why, int32_t cap) {
+  Engine* E = static_cast<Engine*>(engine);
+  if (!E) return zc::kBadArgument;
+  if (why && cap > 0) {
+    std::snprintf(why, (size_t)cap, "%s", E->fused_why.c_str());
+  }
+  if (!E->fused_tried) return -1;
+  return E->fused_ok ? 1 : 0;
 }
 
 int32_t zcu_engine_free_sequence(void* engine, int32_t seq_id) {

@@ -2,6 +2,7 @@
 // include/zero_tensor_cuda.h and capi.cu).  All pointers are device pointers unless stated.
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -135,6 +136,55 @@ int causal_lengths(const int32_t* pos, int B, int32_t* ctx_excl, int32_t* ctx_in
 // past_len++; pos[0]++; (*step)++ -- unless a stop token was already produced.
 int advance_generation(const int32_t* tok, int32_t* pos, int32_t* out, int32_t* step, int32_t* past,
                        int32_t* past_len, int past_cap, int eos, int32_t* done, cudaStream_t s);
+
+// ---- one greedy generation step of one sequence as a single cooperative kernel (decode_fused.cu) ----
+struct FusedLayerW {
+  const int8_t* qkv_qs;
+  const uint16_t* qkv_d;
+  const int8_t* o_qs;
+  const uint16_t* o_d;
+  const int8_t* gu_qs;
+  const uint16_t* gu_d;
+  const int8_t* dn_qs;
+  const uint16_t* dn_d;
+};
+struct FusedStepArgs {
+  int dim, layers, hq, hkv, hd, ffn, vocab, q_dim, kv_dim, qkv_dim;
+  float eps;
+  const int8_t* emb_qs;
+  const uint16_t* emb_d;
+  const FusedLayerW* lw;  // [layers], device memory
+  const float *attn_norm, *ffn_norm, *final_norm;
+  const int8_t* lm_qs;
+  const uint16_t* lm_d;
+  const float *cos_t, *sin_t;
+  int max_pos;
+  __half *kpool, *vpool;  // [layers][pages][hkv][page_size][hd]
+  size_t layer_pool_elems;
+  int page_size, max_pages, num_pages;
+  const int32_t* page_table;
+  const int32_t* rows;  // rows[0]: the sequence's page-table row
+  int32_t* pos;         // pos[0]: position of the token fed this step (advanced by the step)
+  int quirk;            // the reference's causal rule (non-final layers attend to [0, pos))
+  float* logits;        // [vocab]: read (sampled) at the start, written at the end
+  int32_t* tokens;      // tokens[0] = the sampled token
+  int32_t *gen_out, *gen_step, *past, *past_len, *done;
+  int past_cap, eos;
+  float penalty;
+  // device scratch (fused_step_scratch_floats) and control words [2 + hq] (cleared by the launcher)
+  float *x, *qbuf, *hbuf, *part, *P;
+  int2* pairs;
+  unsigned* ctl;
+  int* status;
+  // filled by fused_step_plan
+  int splits, score_cap, dim_pad, vec_pad, row_cap;
+  float scale_log2;
+};
+// kOk when the shapes fit the fused step on `sms` SMs (fills the plan fields and the shared-memory size), else
+// kUnsupported with the reason in *why.
+int fused_step_plan(FusedStepArgs& a, int sms, int max_ctx, size_t* smem, const char** why);
+size_t fused_step_scratch_floats(const FusedStepArgs& a, int sms);
+int fused_step_launch(const FusedStepArgs& a, int sms, size_t smem, cudaStream_t s);
 
 int rope_tensorops(float* x, int heads, int seq, int hd, int pos0, float theta, cudaStream_t s);
 int sgemm(int m, int n, int k, float alpha, const float* a, const float* b, float beta, float* c, cudaStream_t s);

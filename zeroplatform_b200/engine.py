@@ -138,6 +138,13 @@ class LlmEngine:
                                                   eos_token, out.ctypes.data, timing), "generate")
         return out[:n].copy(), float(timing[0]), float(timing[1])
 
+    def step_kind(self):
+        """(1, "") when generation runs one cooperative kernel per token, (0, reason) for the per-operator graph,
+        (-1, "") before the first generate call."""
+        buf = C.create_string_buffer(256)
+        k = lib().zcu_engine_step_kind(self._h, buf, 256)
+        return k, buf.value.decode(errors="replace")
+
     def free_sequence(self, seq_id: int):
         lib().zcu_engine_free_sequence(self._h, seq_id)
 
