@@ -797,6 +797,9 @@ def run_leg(args):
     if args.leg == "moe":
         res = moe_leg(dev, rank, world)
         name = f"moe_8x14336_top2_ep{world}"
+    elif args.leg == "decode_12l":
+        res = decode_12l_leg(dev, False)
+        name = "decode_12l_d768"
     elif args.leg == "gemm":
         m, n, k = (int(v) for v in args.shape.split(","))
         res = gemm_leg(dev, m, n, k)
@@ -813,7 +816,7 @@ def run_leg(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--leg", choices=["all", "decode_7b", "moe", "gemm"], default="all",
+    ap.add_argument("--leg", choices=["all", "decode_7b", "decode_12l", "moe", "gemm"], default="all",
                     help="all: the headline and every extra leg; decode_7b: only the 7B tensor-parallel decode; "
                          "moe: only the expert-parallel MoE layer; gemm: one GEMM shape (--shape)")
     ap.add_argument("--shape", default="512,11008,4096", help="gemm: M,N,K")
@@ -834,7 +837,7 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
-    elif args.leg in ("decode_7b", "moe", "gemm"):
+    elif args.leg in ("decode_7b", "decode_12l", "moe", "gemm"):
         run_leg(args)
     else:
         run_ours(args)

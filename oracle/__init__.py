@@ -89,6 +89,8 @@ def lib():
         "orc_moe_forward": (None, [_f32p, _f32p, _f32p, C.c_int, C.c_int, C.c_int, _u8p, _u8p, _u8p,
                                    C.c_int, C.c_int, _f32p, _i32p, _f32p]),
         "orc_sample_greedy": (C.c_int32, [_f32p, sz, _i32p, sz, C.c_float]),
+        "orc_sample": (C.c_int32, [_f32p, sz, _i32p, sz, C.c_float, C.c_float, C.c_float, C.c_int32, C.c_float,
+                                   C.c_float, _i32p, _f32p, _i32p, C.c_int32]),
         "orc_engine_create": (C.c_void_p, [C.POINTER(OrcModel), C.c_int, C.c_int, C.c_int, C.c_int]),
         "orc_engine_destroy": (None, [C.c_void_p]),
         "orc_engine_prefill": (C.c_int, [C.c_void_p, C.c_int, _i32p, C.c_int, C.c_int, _f32p]),
@@ -296,6 +298,21 @@ def sample_greedy(logits, past=(), penalty=1.0) -> int:
     past = np.ascontiguousarray(np.asarray(past, dtype=np.int32))
     return int(lib().orc_sample_greedy(_p(lg, _f32p), lg.size, _p(past, _i32p) if past.size else None,
                                        past.size, penalty))
+
+
+def sample(logits, past=(), temperature=0.7, top_p=0.9, min_p=0.0, top_k=40, penalty=1.1, u=0.5, cap=65536):
+    """LlmSampler.Sample with the random draw given (u for (float)random.NextDouble()).  Returns (token, kept
+    candidate ids, their renormalised probabilities, logits after the in-place updates)."""
+    lg = np.array(logits, dtype=np.float32, copy=True)
+    past = np.ascontiguousarray(np.asarray(past, dtype=np.int32))
+    ci = np.zeros(cap, np.int32)
+    cp = np.zeros(cap, np.float32)
+    n = np.zeros(1, np.int32)
+    tok = int(lib().orc_sample(_p(lg, _f32p), lg.size, _p(past, _i32p) if past.size else None, past.size,
+                               temperature, top_p, min_p, top_k, penalty, u, _p(ci, _i32p), _p(cp, _f32p),
+                               _p(n, _i32p), cap))
+    k = int(n[0])
+    return tok, ci[:k].copy(), cp[:k].copy(), lg
 
 
 # ---- model + engine ----------------------------------------------------------------------

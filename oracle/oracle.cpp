@@ -10,6 +10,7 @@
 #include <immintrin.h>
 
 #include <algorithm>
+#include <limits>
 #include <atomic>
 #include <cmath>
 #include <condition_variable>
@@ -686,6 +687,87 @@ int32_t orc_sample_greedy(float* logits, size_t vocab, const int32_t* past, size
       best = i;
     }
   return static_cast<int32_t>(best);
+}
+
+// ---- LlmSampler.Sample, all branches (LlmSampler.cs:21-172), the random draw given as u ----
+int32_t orc_sample(float* logits, size_t vocab, const int32_t* past, size_t n_past, float temperature, float top_p,
+                   float min_p, int32_t top_k, float penalty, float u, int32_t* cand_idx, float* cand_p,
+                   int32_t* n_cand, int32_t cap) {
+  if (n_cand) *n_cand = 0;
+  if (vocab == 0) return 0;
+  if (penalty > 1.0f && n_past > 0) {  // 1. repetition penalty, occurrence by occurrence (:39-57)
+    for (size_t i = 0; i < n_past; ++i) {
+      uint32_t tok = static_cast<uint32_t>(past[i]);
+      if (tok < vocab) {
+        if (logits[tok] > 0)
+          logits[tok] /= penalty;
+        else
+          logits[tok] *= penalty;
+      }
+    }
+  }
+  if (temperature <= 0.001f || top_k == 1) {  // 2. greedy (:60-73)
+    size_t best = 0;
+    float best_val = logits[0];
+    for (size_t i = 1; i < vocab; ++i)
+      if (logits[i] > best_val) {
+        best_val = logits[i];
+        best = i;
+      }
+    return static_cast<int32_t>(best);
+  }
+  const float inv_temp = 1.0f / temperature;  // 3. temperature (:76-80)
+  for (size_t i = 0; i < vocab; ++i) logits[i] *= inv_temp;
+  float max_logit = -std::numeric_limits<float>::infinity();  // 4. softmax (:83-101)
+  for (size_t i = 0; i < vocab; ++i)
+    if (logits[i] > max_logit) max_logit = logits[i];
+  float sum_exp = 0.0f;
+  for (size_t i = 0; i < vocab; ++i) {
+    const float e = static_cast<float>(std::exp(static_cast<double>(logits[i] - max_logit)));
+    logits[i] = e;
+    sum_exp += e;
+  }
+  const float inv_sum = sum_exp > 0 ? 1.0f / sum_exp : 0.0f;
+  for (size_t i = 0; i < vocab; ++i) logits[i] *= inv_sum;
+  std::vector<std::pair<int, float>> cand;  // 5. candidates p > 1e-6, by probability descending (:104-113)
+  for (size_t i = 0; i < vocab; ++i)
+    if (logits[i] > 1e-6f) cand.emplace_back(static_cast<int>(i), logits[i]);
+  std::stable_sort(cand.begin(), cand.end(), [](const std::pair<int, float>& a, const std::pair<int, float>& b) {
+    return a.second > b.second;
+  });
+  if (top_k > 0 && cand.size() > static_cast<size_t>(top_k)) cand.resize(top_k);  // Top-K (:116-119)
+  if (min_p > 0.0f && !cand.empty()) {                                               // Min-P (:122-132)
+    const float thr = cand[0].second * min_p;
+    for (size_t i = cand.size(); i-- > 1;)
+      if (cand[i].second < thr) cand.erase(cand.begin() + static_cast<long>(i));
+  }
+  float cumulative = 0.0f;  // Top-P (:135-150)
+  size_t cutoff = cand.size();
+  for (size_t i = 0; i < cand.size(); ++i) {
+    cumulative += cand[i].second;
+    if (cumulative >= top_p) {
+      cutoff = i + 1;
+      break;
+    }
+  }
+  if (cutoff < cand.size()) cand.resize(cutoff);
+  float total = 0.0f;  // renormalise (:153-155)
+  for (const auto& c : cand) total += c.second;
+  const float inv_total = total > 0 ? 1.0f / total : 1.0f;
+  if (cand_idx && cand_p && n_cand) {
+    const int n = static_cast<int>(std::min<size_t>(cand.size(), static_cast<size_t>(std::max(cap, 0))));
+    for (int i = 0; i < n; ++i) {
+      cand_idx[i] = cand[i].first;
+      cand_p[i] = cand[i].second * inv_total;
+    }
+    *n_cand = static_cast<int32_t>(cand.size());
+  }
+  float running = 0.0f;  // 6. CDF walk (:158-171)
+  for (const auto& c : cand) {
+    running += c.second * inv_total;
+    if (u <= running) return c.first;
+  }
+  return cand.empty() ? 0 : cand[0].first;
 }
 
 int orc_num_threads(void) { return pool().size(); }

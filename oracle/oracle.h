@@ -107,6 +107,16 @@ void orc_moe_forward(const float* xnorm, const float* router_w, const float* rou
  * (repetition penalty). Returns the argmax (first index wins ties). */
 int32_t orc_sample_greedy(float* logits, size_t vocab, const int32_t* past, size_t n_past, float repetition_penalty);
 
+/* LlmSampler.Sample, every branch (Sampling/LlmSampler.cs:21-172) with the random draw supplied: `u` stands for
+ * (float)random.NextDouble().  Modifies logits in place as the reference does (penalty, temperature, then
+ * probabilities).  The candidates (p > 1e-6) are sorted by probability, descending; .NET's List.Sort leaves the
+ * order of exactly equal probabilities unspecified, this restatement puts the lower token id first.  When
+ * cand_idx / cand_p are given (capacity cap), they receive the candidates kept after Top-K, Min-P and Top-P and
+ * their renormalised probabilities (value * invTotal), *n_cand their count (0 on the greedy branch). */
+int32_t orc_sample(float* logits, size_t vocab, const int32_t* past, size_t n_past, float temperature, float top_p,
+                   float min_p, int32_t top_k, float repetition_penalty, float u, int32_t* cand_idx, float* cand_p,
+                   int32_t* n_cand, int32_t cap);
+
 /* ---- Model + engine (Engine/LlmEngine.cs:157-461, Memory/PagedKvCache.cs:47-286, Memory/KvBlock.cs) ----
  * All projection weights are Q8_0 AoS blocks, concatenated over layers:
  *   wq [L][hq*hd][dim], wk/wv [L][hkv*hd][dim], wo [L][dim][hq*hd],

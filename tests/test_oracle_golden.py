@@ -249,3 +249,68 @@ def test_causal_quirk_first_token_non_final_layers_see_nothing():
     e.forward_token(1, 3, 0)
     assert e.seq_len(1) == 1
     e.close()
+
+
+def test_sampler_reference_known_answers():
+    """LlmSamplerTests (ZeroLlm/tests/ZeroLlm.Tests/LlmSamplerTests.cs:9-61): greedy picks the maximum (:10-17);
+    a penalty of 2 on past token 1 turns {2.0, 2.1} into a win for token 0 (:20-31); a token masked to -inf loses
+    (:34-46, the mask applied to the input); Min-P 0.1 keeps only token 0 of {10, 5, 0.1} whatever the draw
+    (:49-61, SamplingConfig defaults otherwise: Top-K 40, penalty 1.1)."""
+    greedy = dict(temperature=0.0, top_p=1.0, top_k=1, penalty=1.0)
+    assert O.sample([1.2, 5.8, 0.4, 3.1], **greedy)[0] == 1
+    assert O.sample([2.0, 2.1], past=[1], temperature=0.0, penalty=2.0)[0] == 0
+    assert O.sample([2.0, -np.inf, 4.0], **greedy)[0] == 2
+    for u in (0.0, 0.3, 0.999999):
+        tok, ids, ps, _ = O.sample([10.0, 5.0, 0.1], temperature=1.0, top_p=1.0, min_p=0.1, u=u)
+        assert tok == 0 and list(ids) == [0] and ps[0] == 1.0
+
+
+def test_sampler_restatement_against_numpy():
+    """The oracle's stochastic branch against an independent numpy restatement of LlmSampler.cs:75-171 (float32
+    arithmetic in the reference's order): the same candidates, probabilities and token for a grid of draws."""
+    rng = np.random.default_rng(3)
+    for trial in range(6):
+        V = 500
+        logits = (rng.standard_normal(V) * 3).astype(np.float32)
+        past = rng.integers(0, V, 20).astype(np.int32)
+        T, top_p, min_p, top_k, pen = [(0.7, 0.9, 0.0, 40, 1.1), (1.3, 0.95, 0.02, 0, 1.0), (0.5, 0.8, 0.0, 5, 1.3),
+                                       (1.0, 1.0, 0.05, 100, 1.05), (2.0, 0.5, 0.0, 0, 1.0),
+                                       (0.9, 0.99, 0.01, 300, 1.2)][trial]
+        lg = logits.copy()
+        for t in past:  # penalty, occurrence by occurrence
+            lg[t] = lg[t] / np.float32(pen) if lg[t] > 0 else lg[t] * np.float32(pen)
+        lg = lg * (np.float32(1.0) / np.float32(T))
+        m = lg.max()
+        e = np.array([np.float32(np.exp(np.float64(v - m))) for v in lg], np.float32)
+        s = np.float32(0)
+        for v in e:
+            s = np.float32(s + v)
+        p = e * (np.float32(1.0) / s)
+        cand = sorted([(i, p[i]) for i in range(V) if p[i] > np.float32(1e-6)], key=lambda c: (-c[1], c[0]))
+        if top_k > 0:
+            cand = cand[:top_k]
+        if min_p > 0:
+            thr = np.float32(cand[0][1] * np.float32(min_p))
+            cand = [cand[0]] + [c for c in cand[1:] if not c[1] < thr]
+        cum, cut = np.float32(0), len(cand)
+        for i, (_, v) in enumerate(cand):
+            cum = np.float32(cum + v)
+            if cum >= np.float32(top_p):
+                cut = i + 1
+                break
+        cand = cand[:cut]
+        tot = np.float32(0)
+        for _, v in cand:
+            tot = np.float32(tot + v)
+        inv = np.float32(1.0) / tot
+        for u in np.linspace(0.0, 1.0, 23, dtype=np.float32):
+            tok, ids, ps, _ = O.sample(logits, past, T, top_p, min_p, top_k, pen, float(u))
+            assert list(ids) == [c[0] for c in cand]
+            assert np.array_equal(ps, np.array([np.float32(v * inv) for _, v in cand], np.float32))
+            run, want = np.float32(0), cand[0][0]
+            for i, v in cand:
+                run = np.float32(run + np.float32(v * inv))
+                if u <= run:
+                    want = i
+                    break
+            assert tok == want

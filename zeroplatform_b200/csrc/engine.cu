@@ -517,6 +517,7 @@ int setup_fused(Engine* E) {
   a.kv_dim = E->kv_dim;
   a.qkv_dim = E->qkv_dim;
   a.eps = c.eps;
+  a.page_size = c.page_size;
   int sms = 0;
   E_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, E->device));
   const char* why = nullptr;
