@@ -4,32 +4,35 @@
 // embedding (LlmEngine.cs:317-345) and LlmEngine.ForwardToken (LlmEngine.cs:347-461) over the paged fp16 KV cache.
 //
 // Why one kernel: at batch 1 a small model's step is a chain of ~80 dependent launches whose weight reads are a
-// few hundred KB each, so the chain's latency, not HBM, sets the step time.  Here one CTA per SM runs the whole
-// step, and the points where a vector must be complete before anyone reads it become grid barriers (an arrival
-// counter in global memory, polled by one thread per CTA, bounded by a time limit after which every CTA stops and
-// the status word records code 41):
+// few hundred KB each, so latency, not HBM, sets the step time.  Here one CTA per SM runs the whole step, and the
+// points where a vector must be complete before anyone reads it become grid barriers (an arrival counter plus a
+// release flag in global memory; one thread per CTA polls the flag, bounded by a time limit after which every CTA
+// stops and the status word records code 41):
 //
-//   0  sample     each CTA: arg-max of its vocabulary slice of the previous logits, with the repetition penalty
-//                 applied occurrence by occurrence to the past tokens in the slice  -> pairs   | barrier
-//                 every CTA merges the pairs (largest value, lowest index); CTA 0 records the token (eos, output,
-//                 past list); every CTA dequantizes the token's embedding row into shared memory
+//   0  sample     each CTA: arg-max of its vocabulary slice of the previous logits, the repetition penalty applied
+//                 occurrence by occurrence to the past tokens in the slice                               | barrier
+//                 every CTA merges the slices' (value, index) pairs (largest value, lowest index); CTA 0 records
+//                 the token (stop token, output, past list); every CTA dequantizes its embedding row
 //   per layer:
 //   A  qkv        every CTA: RmsNorm of x (redundantly, x in shared memory); its pairs of Wqkv rows; RoPE on q and
-//                 k pairs; q -> qbuf, k and v -> the layer's fp16 pages at the token's slot          | barrier
-//   B  attention  CTA (head h, split s) for h < hq, s < S: online-softmax partial over its slice of the context
-//                 (the reference's causal rule: non-final layers attend to [0, pos)); the last split of a head to
-//                 arrive (atomic counter) merges the partials in split order and multiplies the head's output by
-//                 its 32-block columns of Wo: P[h] = Wo[:, head h] . attn_h                       | barrier
+//                 k pairs; q -> qbuf, k and v -> the layer's fp16 pages at the token's slot                | barrier
+//   B  attention  CTA (head h, split s): softmax partial over its slice of the context (the reference's causal
+//                 rule: non-final layers attend to [0, pos)); the last split of a head to arrive (atomic counter)
+//                 merges the partials in split order and multiplies the head's output by its 32-block columns of
+//                 Wo: P[h] = Wo[:, head h] . attn_h                                                          | barrier
 //   C  ffn up     every CTA: x += sum over h of P[h] (head order; the same in every CTA), RmsNorm, its units of
-//                 Wgate and Wup, SwiGLU -> hbuf                                                     | barrier
-//   D  ffn down   every CTA: its rows of x_new = x + Wdown . hbuf -> global x                        | barrier
+//                 Wgate and Wup, SwiGLU -> hbuf                                                               | barrier
+//   D  ffn down   every CTA: its rows of x_new = x + Wdown . hbuf -> global x                                  | barrier
 //   LM head       every CTA: RmsNorm with the final norm, its rows of the LM head -> logits; CTA 0 advances pos
 //
-// Every weight byte is read once per step.  While a phase runs, each CTA asks L2 (cp.async.bulk.prefetch.L2) for
-// the weight rows it needs in later phases, so the barrier waits overlap the HBM reads.  Data written in this
-// kernel by another CTA (qbuf, K/V pages, partials, P, hbuf, x, pairs) is read through L2 (ld.global.cg); weights
-// through the non-coherent path.  Projections compute in fp32 on exactly converted int8 values (as the GEMV's
-// fp32 forms); Wo is summed per head and then over heads, another fp32 order than one MatVecAdd over all columns.
+// Memory: every weight byte is read once per step.  A CTA's rows of Wqkv, Wgate|Wup, Wdown and the LM head are
+// contiguous, so one thread bulk-copies them (cp.async.bulk with mbarrier completion, no multicast) into shared
+// memory well before they are used -- a layer's rows right after the previous layer consumed that region -- and the
+// GEMVs read shared memory.  Wo, read by columns of a head in phase B, is prefetched into L2 by row shares.  Loads
+// that depend on a barrier (K/V, partials, Wo slices, the heads' partial sums) are issued all at once.  Data
+// written in this kernel by another CTA (qbuf, K/V pages, partials, P, hbuf, x, pairs) is read through L2
+// (ld.global.cg); weights through the non-coherent path.  Projections compute in fp32 on exactly converted int8
+// values; Wo is summed per head and then over heads, another fp32 order than one MatVecAdd over all columns.
 
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -39,6 +42,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "sync.cuh"
 
 namespace zc {
 
@@ -46,16 +50,11 @@ namespace {
 
 constexpr int FS_THREADS = 512;
 constexpr int FS_WARPS = FS_THREADS / 32;
-constexpr int FS_G = 16;                      // lanes per weight row
+constexpr int FS_G = 16;  // lanes per weight row
 constexpr int FS_ROWS_PER_PASS = FS_THREADS / FS_G;
 constexpr uint64_t FS_WAIT_NS = 2000000000ull;  // a grid barrier that waits longer than 2 s gives up
 constexpr float FS_LOG2E = 1.4426950408889634f;
-
-__device__ __forceinline__ uint64_t fs_now() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
+constexpr int FS_WAVE = 4096;  // floats of the attention reduction area (tokens of a wave x hd)
 
 __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
   unsigned v;
@@ -63,27 +62,33 @@ __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
   return v;
 }
 
-// Grid barrier: every CTA arrives once; `target` counts arrivals expected so far.  Returns false when the wait
-// ran out or another CTA gave up (then every thread of the CTA returns from the kernel).
-__device__ __forceinline__ bool grid_sync(unsigned* ctl, unsigned& target, int* status, int* sh_ok) {
+__device__ __forceinline__ int4 ldcg4(const void* p) { return __ldcg(reinterpret_cast<const int4*>(p)); }
+__device__ __forceinline__ float ldcg(const float* p) { return __ldcg(p); }
+
+// Grid barrier number k (1, 2, ...): ctl[0] counts arrivals; one thread per CTA adds its arrival and polls the
+// count (acquire) until it reaches k * grid.  Returns false when the wait ran out or another CTA gave up (ctl[1]).
+__device__ __forceinline__ bool grid_sync(unsigned* ctl, unsigned& k, int* status, volatile int* sh_ok) {
   __syncthreads();
-  target += gridDim.x;
+  ++k;
   if (threadIdx.x == 0) {
     int ok = 1;
     __threadfence();
     atomicAdd(ctl, 1u);
-    const uint64_t t0 = fs_now();
+    const unsigned target = k * gridDim.x;
+    const uint64_t t0 = global_ns();
     uint32_t polls = 0;
     while (ld_acquire_gpu(ctl) < target) {
-      if (*reinterpret_cast<volatile unsigned*>(ctl + 1)) {
-        ok = 0;
-        break;
-      }
-      if ((++polls & 63) == 0 && fs_now() - t0 > FS_WAIT_NS) {
-        atomicExch(ctl + 1, 1u);
-        atomicExch(status, 41);
-        ok = 0;
-        break;
+      if ((++polls & 31) == 0) {
+        if (*reinterpret_cast<volatile unsigned*>(ctl + 1)) {
+          ok = 0;
+          break;
+        }
+        if (global_ns() - t0 > FS_WAIT_NS) {
+          atomicExch(ctl + 1, 1u);
+          atomicExch(status, 41);
+          ok = 0;
+          break;
+        }
       }
     }
     __threadfence();
@@ -93,22 +98,31 @@ __device__ __forceinline__ bool grid_sync(unsigned* ctl, unsigned& target, int* 
   return *sh_ok != 0;
 }
 
-__device__ __forceinline__ float ldcg(const float* p) { return __ldcg(p); }
-
 // units [b, e) of `n` balanced over the grid
 __device__ __forceinline__ void share(int n, int& b, int& e) {
   b = (int)((long long)n * blockIdx.x / gridDim.x);
   e = (int)((long long)n * (blockIdx.x + 1) / gridDim.x);
 }
 
+__device__ __forceinline__ uint32_t row_bytes(int K, int r0, int r1) {
+  return r1 > r0 ? (uint32_t)(r1 - r0) * (uint32_t)(K + K / 16) : 0u;
+}
+
+// One thread: bulk-copies rows [r0, r1) of a Q8_0 matrix (K columns) into shared memory (int8 rows at dst_q,
+// fp16 scales at dst_d), completion counted on `bar` (armed by the caller with the byte count).
+__device__ __forceinline__ void copy_rows(uint8_t* dst_q, uint16_t* dst_d, const int8_t* qs, const uint16_t* d, int K,
+                                          int r0, int r1, uint32_t bar) {
+  if (r1 <= r0) return;
+  const uint32_t n = (uint32_t)(r1 - r0);
+  bulk_g2s(smem_u32(dst_q), qs + (size_t)r0 * K, n * (uint32_t)K, bar);
+  bulk_g2s(smem_u32(dst_d), d + (size_t)r0 * (K / QK), n * (uint32_t)(K / 16), bar);
+}
+
 __device__ __forceinline__ void prefetch_rows(const int8_t* qs, const uint16_t* d, int K, int r0, int r1) {
   if (r1 <= r0) return;
-  const size_t n = (size_t)(r1 - r0);
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(qs + (size_t)r0 * K), "r"((unsigned)(n * K))
-               : "memory");
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(d + (size_t)r0 * (K / QK)),
-               "r"((unsigned)(n * (K / QK) * 2))
-               : "memory");
+  const uint32_t n = (uint32_t)(r1 - r0);
+  bulk_prefetch_l2(qs + (size_t)r0 * K, n * (uint32_t)K);
+  bulk_prefetch_l2(d + (size_t)r0 * (K / QK), n * (uint32_t)(K / 16));
 }
 
 // 16 int8 weights . 16 fp32 activations (shared memory), exact conversion, packed FMAs
@@ -133,40 +147,53 @@ __device__ __forceinline__ float dot16_s(const int4& w, const float* xs) {
   return s.x + s.y;
 }
 
-// Rows [r0, r1) of a Q8_0 matrix (SoA, K columns) times x (shared memory): FS_G lanes per row, chunks strided
-// over the lanes, a shuffle reduction over the FS_G lanes; emit(row, value) runs on the group's first lane.
+// The same product with the four 4-value groups visited in the order r, r+1, r+2, r+3 (mod 4): with r = (chunk / 2)
+// % 4 the 8 lanes of a 128-bit shared-memory phase, which read chunks 64 bytes apart, hit 8 distinct bank groups.
+__device__ __forceinline__ float dot16_rot(const int4& w, const float* xs, int r) {
+  const float2 bias = make_float2(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
+  const float4* x4 = reinterpret_cast<const float4*>(xs);
+  float2 s = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int jj = (j + r) & 3;
+    const uint32_t word = jj == 0 ? (uint32_t)w.x : jj == 1 ? (uint32_t)w.y : jj == 2 ? (uint32_t)w.z : (uint32_t)w.w;
+    const uint32_t b = word ^ 0x80808080u;
+    const float4 xv = x4[jj];
+    const float2 p01 = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(b, 0x4B000000u, 0x7650)),
+                                              __uint_as_float(__byte_perm(b, 0x4B000000u, 0x7651))),
+                                  bias);
+    const float2 p23 = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(b, 0x4B000000u, 0x7652)),
+                                              __uint_as_float(__byte_perm(b, 0x4B000000u, 0x7653))),
+                                  bias);
+    s = __ffma2_rn(p01, make_float2(xv.x, xv.y), s);
+    s = __ffma2_rn(p23, make_float2(xv.z, xv.w), s);
+  }
+  return s.x + s.y;
+}
+
+// nrows rows staged in shared memory (int8 rows of K at sq, fp16 scales at sd) times x (shared memory): FS_G
+// lanes per row, chunks strided over the lanes, a shuffle reduction; emit(local row, value) on the group's first
+// lane.  The loop is uniform over each warp (its two row groups iterate together; a missing row computes zeros), so
+// the full-warp shuffles always have all 32 lanes.
 template <class Emit>
-__device__ __forceinline__ void gemv_rows(const int8_t* __restrict__ qs, const uint16_t* __restrict__ d, int K,
-                                          const float* xs, int r0, int r1, Emit emit) {
+__device__ __forceinline__ void gemv_smem(const uint8_t* sq, const uint16_t* sd, int K, const float* xs, int nrows,
+                                          Emit emit) {
   const int gi = threadIdx.x / FS_G, li = threadIdx.x % FS_G;
-  const int warp = threadIdx.x >> 5, sub = gi & 1;  // a warp holds two row groups
+  const int warp = threadIdx.x >> 5, sub = gi & 1;
   const int nch = K / 16, kb = K / QK;
-  // the loop is uniform over the warp (both groups iterate together, a missing row computes zeros), so the
-  // full-warp shuffles below always have all 32 lanes
-  for (int base = r0 + 2 * warp; base < r1; base += FS_ROWS_PER_PASS) {
-    const int row = base + sub;
-    const bool valid = row < r1;
-    const int8_t* wr = qs + (size_t)(valid ? row : r0) * K;
-    const uint16_t* dr = d + (size_t)(valid ? row : r0) * kb;
+  for (int base = 2 * warp; base < nrows; base += FS_ROWS_PER_PASS) {
+    const int r = base + sub;
+    const bool valid = r < nrows;
+    const uint8_t* wr = sq + (size_t)(valid ? r : 0) * K;
+    const uint16_t* dr = sd + (size_t)(valid ? r : 0) * kb;
     float acc = 0.f;
-    for (int c0 = li; c0 < nch; c0 += 4 * FS_G) {
-      int4 w[4];
-      float sc[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int c = c0 + u * FS_G;
-        w[u] = c < nch ? ld_stream_v4(wr + (size_t)c * 16) : make_int4(0, 0, 0, 0);
-        sc[u] = c < nch ? h2f(__ldg(dr + (c >> 1))) : 0.f;
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int c = c0 + u * FS_G;
-        if (c < nch) acc = fmaf(sc[u], dot16_s(w[u], xs + c * 16), acc);
-      }
-    }
+    for (int c = li; c < nch; c += FS_G)
+      acc = fmaf(h2f(dr[c >> 1]), dot16_rot(*reinterpret_cast<const int4*>(wr + (size_t)c * 16), xs + c * 16,
+                                             (c >> 1) & 3),
+                 acc);
 #pragma unroll
     for (int o = FS_G / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (valid && li == 0) emit(row, acc);
+    if (valid && li == 0) emit(r, acc);
   }
 }
 
@@ -192,30 +219,114 @@ __device__ __forceinline__ void rmsnorm_s(const float* x, const float* __restric
 
 __device__ __forceinline__ bool better(float v, int i, float best, int bi) { return v > best || (v == best && i < bi); }
 
+// 8 fp16 values (one 16-byte word) to fp32
+__device__ __forceinline__ void h8(const int4& w, float (&f)[8]) {
+  const __half2* h = reinterpret_cast<const __half2*>(&w);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 v = __half22float2(h[j]);
+    f[2 * j] = v.x;
+    f[2 * j + 1] = v.y;
+  }
+}
+
 __global__ void __launch_bounds__(FS_THREADS, 1) fused_step_kernel(FusedStepArgs a) {
-  extern __shared__ __align__(16) float sm[];
-  float* xs = sm;                         // residual x [dim]
-  float* xn = xs + a.dim_pad;             // normed x / attention output [max(dim, ffn) padded]
-  float* rowbuf = xn + a.vec_pad;         // projection results of this CTA [row_cap]
-  float* scores = rowbuf + a.row_cap;     // attention probabilities [score_cap]; sampling counts reuse it
-  float* red = scores + a.score_cap;      // reductions [64]
-  float* qh = red + 64;                   // one query head, pre-scaled [128]
-  __shared__ int sh_ok;
+  extern __shared__ __align__(128) float sm[];
+  float* xs = sm;                        // residual x [dim_pad]
+  float* xn = xs + a.dim_pad;            // normed x, SwiGLU input [vec_pad]
+  float* rowbuf = xn + a.vec_pad;        // projection results of this CTA [row_cap]
+  float* scores = rowbuf + a.row_cap;    // attention probabilities [score_cap]; sampling counts reuse it
+  float* red = scores + a.score_cap;     // reductions [64]
+  float* qh = red + 64;                  // one query head, pre-scaled [128]
+  float* cs = qh + 128;                  // cos [0, 64) and sin [64, 128) of the step's position
+  float* wave = cs + 128;                // attention reductions [FS_WAVE]
+  int32_t* pts = reinterpret_cast<int32_t*>(wave + FS_WAVE);  // the sequence's page-table row [pt_pad]
+  uint8_t* wts = reinterpret_cast<uint8_t*>(pts + a.pt_pad);  // staged weight rows
+  __shared__ __align__(8) uint64_t bars[4];                   // staging of A, C, D, LM head
+  __shared__ volatile int sh_ok;
+  __shared__ volatile int sh_abort;
   __shared__ int sh_tok;
-  unsigned target = 0;
+  __shared__ int sh_last;
+  unsigned k_bar = 0;
   const int tid = threadIdx.x;
   const int pos = *reinterpret_cast<volatile int32_t*>(a.pos);
   const int row_pt = a.rows[0];
   const int L = a.layers;
+  const int half = a.hd / 2;
+
+  // this CTA's share of every phase
+  int u0, u1, j0, j1, n0, n1, v0, v1;
+  share(a.qkv_dim / 2, u0, u1);  // pairs of Wqkv rows
+  share(a.ffn, j0, j1);          // FFN units
+  share(a.dim, n0, n1);          // rows of Wdown (and of Wo, prefetched into L2)
+  share(a.vocab, v0, v1);        // rows of the LM head
+  const int nA = 2 * (u1 - u0), nC = j1 - j0, nD = n1 - n0, nV = v1 - v0;
+  // staging regions: A | C (gate rows, up rows, gate scales, up scales) | D;  the LM head's rows reuse them all
+  uint8_t* wA = wts;
+  uint8_t* wC = wA + (size_t)nA * (a.dim + a.dim / 16);
+  uint8_t* wD = wC + (size_t)2 * nC * (a.dim + a.dim / 16);
+  const uint32_t bA = smem_u32(&bars[0]), bC = smem_u32(&bars[1]), bD = smem_u32(&bars[2]), bL = smem_u32(&bars[3]);
+  auto stage_A = [&](int l) {
+    const FusedLayerW W = a.lw[l];
+    mbar_arrive_tx(bA, row_bytes(a.dim, 2 * u0, 2 * u1));
+    copy_rows(wA, reinterpret_cast<uint16_t*>(wA + (size_t)nA * a.dim), W.qkv_qs, W.qkv_d, a.dim, 2 * u0, 2 * u1,
+              bA);
+  };
+  auto stage_C = [&](int l) {
+    const FusedLayerW W = a.lw[l];
+    mbar_arrive_tx(bC, 2 * row_bytes(a.dim, j0, j1));
+    uint16_t* dC = reinterpret_cast<uint16_t*>(wC + (size_t)2 * nC * a.dim);
+    copy_rows(wC, dC, W.gu_qs, W.gu_d, a.dim, j0, j1, bC);
+    copy_rows(wC + (size_t)nC * a.dim, dC + (size_t)nC * (a.dim / QK), W.gu_qs, W.gu_d, a.dim, a.ffn + j0,
+              a.ffn + j1, bC);
+  };
+  auto stage_D = [&](int l) {
+    const FusedLayerW W = a.lw[l];
+    mbar_arrive_tx(bD, row_bytes(a.ffn, n0, n1));
+    copy_rows(wD, reinterpret_cast<uint16_t*>(wD + (size_t)nD * a.ffn), W.dn_qs, W.dn_d, a.ffn, n0, n1, bD);
+  };
+  if (tid == 0) {
+    sh_abort = 0;
+    for (int i = 0; i < 4; ++i) mbar_init(smem_u32(&bars[i]), 1);
+    fence_mbar_init();
+    stage_A(0);
+    stage_C(0);
+    stage_D(0);
+    prefetch_rows(a.lw[0].o_qs, a.lw[0].o_d, a.q_dim, n0, n1);
+  }
+  // the step's constants: the sequence's page-table row, RoPE angles of its position
+  for (int i = tid; i < a.max_pages; i += FS_THREADS) pts[i] = a.page_table[(size_t)row_pt * a.max_pages + i];
+  {
+    const int pc = min(max(pos, 0), a.max_pos - 1);
+    for (int i = tid; i < half; i += FS_THREADS) {
+      cs[i] = a.cos_t[(size_t)pc * half + i];
+      cs[64 + i] = a.sin_t[(size_t)pc * half + i];
+    }
+  }
+  // parity of each staging barrier's next phase, and whether that phase is armed and not yet waited for; a CTA
+  // that stops early first waits (bounded) for those copies
+  uint32_t parA = 0, parC = 0, parD = 0;
+  bool pA = true, pC = true, pD = true, pL = false;
+  auto drain = [&]() {
+    const uint32_t bs[4] = {bA, bC, bD, bL};
+    const uint32_t pars[4] = {parA, parC, parD, 0u};
+    const bool pend[4] = {pA, pC, pD, pL};
+    for (int i = 0; i < 4; ++i) {
+      if (!pend[i]) continue;
+      const uint32_t par = pars[i];
+      const uint64_t t0 = global_ns();
+      while (!mbar_try(bs[i], par) && global_ns() - t0 < 100000000ull) {
+      }
+    }
+  };
 
   // ---------------- 0: sample the previous step's logits ----------------
   {
-    int v0, v1;
-    share(a.vocab, v0, v1);
     int* cnt = reinterpret_cast<int*>(scores);  // occurrences of each token of the slice in the past list
     const bool pen = a.penalty > 1.0f && a.past_len;
+    __syncthreads();
     if (pen) {
-      for (int i = tid; i < v1 - v0; i += FS_THREADS) cnt[i] = 0;
+      for (int i = tid; i < nV; i += FS_THREADS) cnt[i] = 0;
       __syncthreads();
       const int n = min(*a.past_len, a.past_cap);
       for (int i = tid; i < n; i += FS_THREADS) {
@@ -261,36 +372,47 @@ __global__ void __launch_bounds__(FS_THREADS, 1) fused_step_kernel(FusedStepArgs
       a.pairs[blockIdx.x] = make_int2(__float_as_int(b), i0);
     }
   }
-  if (!grid_sync(a.ctl, target, a.status, &sh_ok)) return;
-  if (tid == 0) {
-    float b = -INFINITY;
-    int bi = 0x7fffffff;
-    for (int k = 0; k < (int)gridDim.x; ++k) {
-      const int2 p = __ldcg(a.pairs + k);
-      if (p.y == 0x7fffffff) continue;
-      if (better(__int_as_float(p.x), p.y, b, bi)) {
-        b = __int_as_float(p.x);
-        bi = p.y;
+  if (!grid_sync(a.ctl, k_bar, a.status, &sh_ok)) return drain();
+  {
+    // every CTA merges the pairs: lanes of warp 0 take strided shares, then a shuffle merge (value, then index)
+    if (tid < 32) {
+      float b = -INFINITY;
+      int bi = 0x7fffffff;
+      for (int q = tid; q < (int)gridDim.x; q += 32) {
+        const int2 p = __ldcg(a.pairs + q);
+        if (p.y != 0x7fffffff && better(__int_as_float(p.x), p.y, b, bi)) {
+          b = __int_as_float(p.x);
+          bi = p.y;
+        }
       }
-    }
-    const int tok = bi == 0x7fffffff ? 0 : bi;  // an all-NaN row keeps index 0, as the reference's scan does
-    sh_tok = tok;
-    if (blockIdx.x == 0) {
-      a.tokens[0] = tok;
-      if (!*a.done) {
-        if (a.eos >= 0 && tok == a.eos) {
-          *a.done = 1;
-        } else {
-          a.gen_out[*a.gen_step] = tok;
-          if (*a.past_len < a.past_cap) a.past[*a.past_len] = tok;
-          *a.past_len += 1;
-          *a.gen_step += 1;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, b, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (oi != 0x7fffffff && better(ob, oi, b, bi)) {
+          b = ob;
+          bi = oi;
+        }
+      }
+      if (tid == 0) {
+        const int tok = bi == 0x7fffffff ? 0 : bi;  // an all-NaN row keeps index 0, as the reference's scan does
+        sh_tok = tok;
+        if (blockIdx.x == 0) {
+          a.tokens[0] = tok;
+          if (!*a.done) {
+            if (a.eos >= 0 && tok == a.eos) {
+              *a.done = 1;
+            } else {
+              a.gen_out[*a.gen_step] = tok;
+              if (*a.past_len < a.past_cap) a.past[*a.past_len] = tok;
+              *a.past_len += 1;
+              *a.gen_step += 1;
+            }
+          }
         }
       }
     }
-  }
-  __syncthreads();
-  {
+    __syncthreads();
     int tok = sh_tok;
     if (tok < 0 || tok >= a.vocab) tok = 0;  // unknown ids read row 0 (LlmEngine.cs:321)
     const int8_t* er = a.emb_qs + (size_t)tok * a.dim;
@@ -298,57 +420,54 @@ __global__ void __launch_bounds__(FS_THREADS, 1) fused_step_kernel(FusedStepArgs
     for (int i = tid; i < a.dim; i += FS_THREADS) xs[i] = (float)er[i] * h2f(ed[i / QK]);
   }
 
-  const int half = a.hd / 2;
   const int group = a.hq / a.hkv;
   const int S = a.splits;
+  const int lp_pos = pos / a.page_size;
+  const int page_pos = (pos >= 0 && lp_pos < a.max_pages) ? pts[lp_pos] : -1;
   for (int l = 0; l < L; ++l) {
     const FusedLayerW W = a.lw[l];
     __half* kpool = a.kpool + (size_t)l * a.layer_pool_elems;
     __half* vpool = a.vpool + (size_t)l * a.layer_pool_elems;
-    int u0, u1, j0, j1, n0, n1;
-    share(a.qkv_dim / 2, u0, u1);  // pairs of Wqkv rows
-    share(a.ffn, j0, j1);          // FFN units
-    share(a.dim, n0, n1);          // rows of Wdown
-    // L2 prefetch of this CTA's later rows: Wo (a contiguous share, read column-wise in B), Wgate/Wup, Wdown
-    if (tid == 0) {
-      prefetch_rows(W.o_qs, W.o_d, a.q_dim, n0, n1);
-      prefetch_rows(W.gu_qs, W.gu_d, a.dim, j0, j1);
-      prefetch_rows(W.gu_qs, W.gu_d, a.dim, a.ffn + j0, a.ffn + j1);
-      prefetch_rows(W.dn_qs, W.dn_d, a.ffn, n0, n1);
-    }
     // ---------------- A: RmsNorm, Wqkv, RoPE, K/V append ----------------
     rmsnorm_s(xs, a.attn_norm + (size_t)l * a.dim, xn, a.dim, a.eps, red);
-    const int r0 = 2 * u0, r1 = 2 * u1;
-    gemv_rows(W.qkv_qs, W.qkv_d, a.dim, xn, r0, r1, [&](int row, float v) { rowbuf[row - r0] = v; });
+    if (!mbar_wait(bA, parA, &sh_abort, a.status, 42)) {
+      atomicExch(a.ctl + 1, 1u);
+      return drain();
+    }
+    pA = false;
+    parA ^= 1;
+    gemv_smem(wA, reinterpret_cast<const uint16_t*>(wA + (size_t)nA * a.dim), a.dim, xn, nA,
+              [&](int r, float v) { rowbuf[r] = v; });
     __syncthreads();
     for (int p = u0 + tid; p < u1; p += FS_THREADS) {
       const int row = 2 * p;
-      float x0 = rowbuf[row - r0], x1 = rowbuf[row + 1 - r0];
+      float x0 = rowbuf[row - 2 * u0], x1 = rowbuf[row + 1 - 2 * u0];
       const int pi = (row % a.hd) / 2;
       if (row < a.q_dim + a.kv_dim) {  // RoPE.ApplyInplace on q and k
-        const int pc = min(max(pos, 0), a.max_pos - 1);
-        const float c = a.cos_t[(size_t)pc * half + pi], s = a.sin_t[(size_t)pc * half + pi];
+        const float c = cs[pi], s = cs[64 + pi];
         const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
         const float y1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
         x0 = y0;
         x1 = y1;
       }
       if (row < a.q_dim) {
-        a.qbuf[row] = x0;
-        a.qbuf[row + 1] = x1;
+        *reinterpret_cast<float2*>(a.qbuf + row) = make_float2(x0, x1);
         continue;
       }
       const bool is_k = row < a.q_dim + a.kv_dim;
       const int r = is_k ? row - a.q_dim : row - a.q_dim - a.kv_dim;
-      const int kvh = r / a.hd;
-      const int lp = pos / a.page_size;
-      if (pos < 0 || lp >= a.max_pages) continue;
-      const int page = a.page_table[(size_t)row_pt * a.max_pages + lp];
-      if (page < 0 || page >= a.num_pages) continue;
-      const size_t off = (((size_t)page * a.hkv + kvh) * a.page_size + (pos % a.page_size)) * a.hd + (r % a.hd);
+      if (page_pos < 0 || page_pos >= a.num_pages) continue;
+      const size_t off =
+          (((size_t)page_pos * a.hkv + r / a.hd) * a.page_size + (pos % a.page_size)) * a.hd + (r % a.hd);
       *reinterpret_cast<__half2*>((is_k ? kpool : vpool) + off) = __floats2half2_rn(x0, x1);
     }
-    if (!grid_sync(a.ctl, target, a.status, &sh_ok)) return;
+    if (!grid_sync(a.ctl, k_bar, a.status, &sh_ok)) return drain();
+    if (l + 1 < L) pA = true;
+    if (tid == 0 && l + 1 < L) {  // region A is free: the next layer's Wqkv rows; its Wo share into L2
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      stage_A(l + 1);
+      prefetch_rows(a.lw[l + 1].o_qs, a.lw[l + 1].o_d, a.q_dim, n0, n1);
+    }
 
     // ---------------- B: attention partials, merge, per-head Wo ----------------
     if ((int)blockIdx.x < a.hq * S) {
@@ -356,39 +475,44 @@ __global__ void __launch_bounds__(FS_THREADS, 1) fused_step_kernel(FusedStepArgs
       const int kvh = h / group;
       const int n = (a.quirk && l != L - 1) ? pos : pos + 1;  // LlmEngine.cs:254, PagedKvCache.cs:139-142
       const int t0 = (int)((long long)n * s / S), t1 = (int)((long long)n * (s + 1) / S);
-      float* ob = xn;   // per-group output partials [groups][hd]
       for (int i = tid; i < a.hd; i += FS_THREADS) qh[i] = ldcg(a.qbuf + (size_t)h * a.hd + i) * a.scale_log2;
       __syncthreads();
-      // scores: one warp per token, lanes over the dimensions
-      const int warp = tid >> 5, lane = tid & 31;
-      const int dpl = a.hd / 32;  // 2 or 4 dims per lane
-      for (int t = t0 + warp; t < t1; t += FS_WARPS) {
-        const int lp = t / a.page_size;
-        const int page = a.page_table[(size_t)row_pt * a.max_pages + lp];
-        float sc = -INFINITY;
-        if (page >= 0 && page < a.num_pages) {
-          const __half* kr = kpool + (((size_t)page * a.hkv + kvh) * a.page_size + (t % a.page_size)) * a.hd;
-          float part = 0.f;
-          for (int e = 0; e < dpl; e += 2) {
-            const int dd = lane * dpl + e;
-            const unsigned raw = __ldcg(reinterpret_cast<const unsigned*>(kr + dd));
-            const float2 kv = __half22float2(*reinterpret_cast<const __half2*>(&raw));
-            part = fmaf(qh[dd], kv.x, part);
-            part = fmaf(qh[dd + 1], kv.y, part);
+      // waves of W tokens: TPT threads per token, 8 dims (one 16-byte word of K and of V) each
+      const int TPT = a.hd / 8, Wt = FS_THREADS / TPT;
+      const int tw = tid / TPT, g = tid % TPT;
+      const bool one_wave = t1 - t0 <= Wt;
+      float vreg[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int w0 = t0; w0 < t1; w0 += Wt) {
+        const int t = w0 + tw;
+        int4 kw = make_int4(0, 0, 0, 0), vw = make_int4(0, 0, 0, 0);
+        bool ok = false;
+        if (t < t1) {
+          const int page = pts[t / a.page_size];
+          if (page >= 0 && page < a.num_pages) {
+            const size_t off = (((size_t)page * a.hkv + kvh) * a.page_size + (t % a.page_size)) * a.hd + 8 * g;
+            kw = ldcg4(kpool + off);
+            if (one_wave) vw = ldcg4(vpool + off);
+            ok = true;
           }
-          sc = warp_sum(part);
         }
-        if (lane == 0) scores[t - t0] = sc;
+        float kf[8];
+        h8(kw, kf);
+        float part = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) part = fmaf(qh[8 * g + j], kf[j], part);
+        for (int o = TPT / 2; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+        if (t < t1 && g == 0) scores[t - t0] = ok ? part : -INFINITY;
+        if (one_wave) h8(vw, vreg);
       }
       __syncthreads();
+      const int warp = tid >> 5, lane = tid & 31;
       float m = -INFINITY;
       for (int i = tid; i < t1 - t0; i += FS_THREADS) m = fmaxf(m, scores[i]);
       m = warp_max(m);
-      __shared__ float wred[FS_WARPS];
-      if (lane == 0) wred[warp] = m;
+      if (lane == 0) red[warp] = m;
       __syncthreads();
-      m = wred[0];
-      for (int w = 1; w < FS_WARPS; ++w) m = fmaxf(m, wred[w]);
+      m = red[0];
+      for (int w = 1; w < FS_WARPS; ++w) m = fmaxf(m, red[w]);
       __syncthreads();
       float lsum = 0.f;
       for (int i = tid; i < t1 - t0; i += FS_THREADS) {
@@ -397,116 +521,206 @@ __global__ void __launch_bounds__(FS_THREADS, 1) fused_step_kernel(FusedStepArgs
         lsum += p;
       }
       lsum = warp_sum(lsum);
-      if (lane == 0) wred[warp] = lsum;
+      if (lane == 0) red[warp] = lsum;
       __syncthreads();
       lsum = 0.f;
-      for (int w = 0; w < FS_WARPS; ++w) lsum += wred[w];
-      // o[d] = sum_t p_t v_t[d]: token groups of hd threads, then a sum over the groups in order
-      const int ng = FS_THREADS / a.hd, g = tid / a.hd, dd = tid % a.hd;
-      float o = 0.f;
-      for (int t = t0 + g; t < t1; t += ng) {
-        const int lp = t / a.page_size;
-        const int page = a.page_table[(size_t)row_pt * a.max_pages + lp];
-        const float p = scores[t - t0];
-        if (page < 0 || page >= a.num_pages || p == 0.f) continue;
-        const __half* vr = vpool + (((size_t)page * a.hkv + kvh) * a.page_size + (t % a.page_size)) * a.hd;
-        const unsigned short raw = __ldcg(reinterpret_cast<const unsigned short*>(vr + dd));
-        o = fmaf(p, __half2float(__ushort_as_half(raw)), o);
+      for (int w = 0; w < FS_WARPS; ++w) lsum += red[w];
+      // o[d] = sum_t p_t v_t[d]: a wave's p * v words go to `wave` [Wt][hd]; thread (block b, dim d) sums 8 tokens
+      // of the wave, and the blocks' sums are added in order
+      float o_acc = 0.f;  // threads d < hd
+      const int blocks = FS_THREADS / a.hd, per = Wt / blocks;
+      const int dd = tid % a.hd, bb = tid / a.hd;
+      for (int w0 = t0; w0 < t1; w0 += Wt) {
+        const int t = w0 + tw;
+        float pv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (t < t1) {
+          const float p = scores[t - t0];
+          if (!one_wave) {
+            const int page = pts[t / a.page_size];
+            int4 vw = make_int4(0, 0, 0, 0);
+            if (page >= 0 && page < a.num_pages)
+              vw = ldcg4(vpool + (((size_t)page * a.hkv + kvh) * a.page_size + (t % a.page_size)) * a.hd + 8 * g);
+            h8(vw, vreg);
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) pv[j] = p * vreg[j];
+        }
+        __syncthreads();  // the previous wave's block sums have been read
+#pragma unroll
+        for (int j = 0; j < 8; ++j) wave[tw * a.hd + 8 * g + j] = pv[j];
+        __syncthreads();
+        float ps = 0.f;
+        for (int i = 0; i < per; ++i) ps += wave[(bb * per + i) * a.hd + dd];
+        __syncthreads();
+        wave[bb * a.hd + dd] = ps;
+        __syncthreads();
+        if (tid < a.hd) {
+          float ws = 0.f;
+          for (int q = 0; q < blocks; ++q) ws += wave[q * a.hd + tid];
+          o_acc += ws;
+        }
       }
-      ob[g * a.hd + dd] = o;
-      __syncthreads();
       float* part = a.part + ((size_t)h * S + s) * (a.hd + 2);
-      for (int i = tid; i < a.hd; i += FS_THREADS) {
-        float acc = 0.f;
-        for (int gg = 0; gg < ng; ++gg) acc += ob[gg * a.hd + i];
-        part[2 + i] = acc;
-      }
+      if (tid < a.hd) part[2 + tid] = o_acc;
       if (tid == 0) {
         part[0] = m;
         part[1] = lsum;
       }
+      // every split of head h waits (bounded) for the head's S partials -- all CTAs of a cooperative launch are
+      // resident, so the wait ends -- then merges them and computes its share of the head's Wo rows
       __threadfence();
       __syncthreads();
-      __shared__ int last;
-      if (tid == 0) last = atomicAdd(a.ctl + 2 + h, 1u) == (unsigned)(S - 1);
-      __syncthreads();
-      if (last) {
-        if (tid == 0) a.ctl[2 + h] = 0;
-        __threadfence();
-        // merge the S partials in split order (exp2 domain): out = sum_s o_s 2^(m_s - M) / sum_s l_s 2^(m_s - M)
-        float* attn = scores;  // [hd]
-        const float* ph = a.part + (size_t)h * S * (a.hd + 2);
-        for (int i = tid; i < a.hd; i += FS_THREADS) {
-          float M = -INFINITY;
-          for (int q = 0; q < S; ++q) M = fmaxf(M, ldcg(ph + (size_t)q * (a.hd + 2)));
-          float num = 0.f, den = 0.f;
-          if (M != -INFINITY)
-            for (int q = 0; q < S; ++q) {
-              const float* pq = ph + (size_t)q * (a.hd + 2);
-              const float mq = ldcg(pq);
-              if (mq == -INFINITY) continue;
-              const float f = exp2f(mq - M);
-              den = fmaf(ldcg(pq + 1), f, den);
-              num = fmaf(ldcg(pq + 2 + i), f, num);
-            }
-          attn[i] = den > 0.f ? num / den : 0.f;  // ctx 0 gives zeros (GqaAttention.cs:38-42)
+      if (tid == 0) {
+        atomicAdd(a.ctl + 3 + h, 1u);
+        const unsigned want = (unsigned)S * (unsigned)(l + 1);
+        const uint64_t tw0 = global_ns();
+        uint32_t polls = 0;
+        int ok = 1;
+        while (ld_acquire_gpu(a.ctl + 3 + h) < want) {
+          if ((++polls & 31) == 0 &&
+              (*reinterpret_cast<volatile unsigned*>(a.ctl + 1) || global_ns() - tw0 > FS_WAIT_NS)) {
+            atomicExch(a.ctl + 1, 1u);
+            atomicExch(a.status, 41);
+            ok = 0;
+            break;
+          }
         }
-        __syncthreads();
-        // P[h][row] = Wo[row, head h's columns] . attn_h: hd / 16 chunks and hd / 32 scales per row
-        const int cpr = a.hd / 16, kb = a.q_dim / QK;
-        for (int row = tid; row < a.dim; row += FS_THREADS) {
-          const int8_t* wr = W.o_qs + (size_t)row * a.q_dim + (size_t)h * a.hd;
-          const uint16_t* dr = W.o_d + (size_t)row * kb + (size_t)h * (a.hd / QK);
-          float acc = 0.f;
-          for (int c = 0; c < cpr; ++c) acc = fmaf(h2f(__ldg(dr + (c >> 1))), dot16_s(ld_stream_v4(wr + c * 16), attn + c * 16), acc);
-          a.P[(size_t)h * a.dim + row] = acc;
+        __threadfence();
+        sh_last = ok;
+      }
+      __syncthreads();
+      if (!sh_last) return drain();
+      // merge the S partials in split order (exp2 domain): out = sum_s o_s 2^(m_s - M) / sum_s l_s 2^(m_s - M)
+      const float* phd = a.part + (size_t)h * S * (a.hd + 2);
+      for (int i = tid; i < S * (a.hd + 2); i += FS_THREADS) wave[i] = ldcg(phd + i);
+      __syncthreads();
+      float* attn = scores;  // [hd]
+      for (int i = tid; i < a.hd; i += FS_THREADS) {
+        float M = -INFINITY;
+        for (int q = 0; q < S; ++q) M = fmaxf(M, wave[q * (a.hd + 2)]);
+        float num = 0.f, den = 0.f;
+        if (M != -INFINITY)
+          for (int q = 0; q < S; ++q) {
+            const float* pq = wave + q * (a.hd + 2);
+            if (pq[0] == -INFINITY) continue;
+            const float f = exp2f(pq[0] - M);
+            den = fmaf(pq[1], f, den);
+            num = fmaf(pq[2 + i], f, num);
+          }
+        attn[i] = den > 0.f ? num / den : 0.f;  // ctx 0 gives zeros (GqaAttention.cs:38-42)
+      }
+      __syncthreads();
+      // P[h][row] = Wo[row, head h's hd columns] . attn_h for this split's rows: items (row, 16-column chunk), a
+      // batch's loads all in flight; the cpr chunks of a row are adjacent lanes and meet in a shuffle reduction
+      const int cpr = a.hd / 16, kb = a.q_dim / QK;
+      const int rw0 = (int)((long long)a.dim * s / S), rw1 = (int)((long long)a.dim * (s + 1) / S);
+      const int items = (rw1 - rw0) * cpr;
+      for (int it0 = 0; it0 < items; it0 += 8 * FS_THREADS) {
+        int4 w[8];
+        float sc[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int it = it0 + j * FS_THREADS + tid;
+          const int row = rw0 + it / cpr, c = it % cpr;
+          const bool ok = it < items;
+          w[j] = ok ? ld_stream_v4(W.o_qs + (size_t)row * a.q_dim + (size_t)h * a.hd + c * 16) : make_int4(0, 0, 0, 0);
+          sc[j] = ok ? h2f(__ldg(W.o_d + (size_t)row * kb + (size_t)h * (a.hd / QK) + (c >> 1))) : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int it = it0 + j * FS_THREADS + tid;
+          const int c = it % cpr;
+          float v = it < items ? sc[j] * dot16_s(w[j], attn + c * 16) : 0.f;
+          for (int o = cpr / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+          if (it < items && c == 0) a.P[(size_t)h * a.dim + rw0 + it / cpr] = v;
         }
       }
     }
-    if (!grid_sync(a.ctl, target, a.status, &sh_ok)) return;
+    if (!grid_sync(a.ctl, k_bar, a.status, &sh_ok)) return drain();
 
     // ---------------- C: x += Wo . attn (summed over heads), RmsNorm, Wgate / Wup, SwiGLU ----------------
     for (int i = tid; i < a.dim; i += FS_THREADS) {
-      float acc = ldcg(a.P + i);
-      for (int h = 1; h < a.hq; ++h) acc += ldcg(a.P + (size_t)h * a.dim + i);
+      float acc = 0.f;
+      for (int h0 = 0; h0 < a.hq; h0 += 16) {
+        float v[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) v[u] = h0 + u < a.hq ? ldcg(a.P + (size_t)(h0 + u) * a.dim + i) : 0.f;
+#pragma unroll
+        for (int u = 0; u < 16; ++u)
+          if (h0 + u < a.hq) acc = (h0 + u == 0) ? v[u] : acc + v[u];
+      }
       xs[i] = xs[i] + acc;
     }
     __syncthreads();
     rmsnorm_s(xs, a.ffn_norm + (size_t)l * a.dim, xn, a.dim, a.eps, red);
-    if (l + 1 < L && tid == 0) {  // the next layer's Wqkv pairs of this CTA
-      const FusedLayerW Wn = a.lw[l + 1];
-      prefetch_rows(Wn.qkv_qs, Wn.qkv_d, a.dim, 2 * u0, 2 * u1);
-    } else if (tid == 0) {
-      int v0, v1;
-      share(a.vocab, v0, v1);
-      prefetch_rows(a.lm_qs, a.lm_d, a.dim, v0, v1);
+    if (!mbar_wait(bC, parC, &sh_abort, a.status, 42)) {
+      atomicExch(a.ctl + 1, 1u);
+      return drain();
     }
-    const int nu = j1 - j0;
-    gemv_rows(W.gu_qs, W.gu_d, a.dim, xn, j0, j1, [&](int row, float v) { rowbuf[row - j0] = v; });
-    gemv_rows(W.gu_qs, W.gu_d, a.dim, xn, a.ffn + j0, a.ffn + j1,
-              [&](int row, float v) { rowbuf[nu + row - a.ffn - j0] = v; });
+    pC = false;
+    parC ^= 1;
+    const uint16_t* dC = reinterpret_cast<const uint16_t*>(wC + (size_t)2 * nC * a.dim);
+    gemv_smem(wC, dC, a.dim, xn, 2 * nC, [&](int r, float v) { rowbuf[r] = v; });  // gate rows, then up rows
     __syncthreads();
-    for (int j = tid; j < nu; j += FS_THREADS) {  // SwiGLU.Forward (Layers/SwiGLU.cs:13-51)
-      const float g = rowbuf[j], u = rowbuf[nu + j];
+    for (int j = tid; j < nC; j += FS_THREADS) {  // SwiGLU.Forward (Layers/SwiGLU.cs:13-51)
+      const float g = rowbuf[j], u = rowbuf[nC + j];
       const float sg = 1.0f / (1.0f + expf(-g));
       a.hbuf[j0 + j] = __fmul_rn(__fmul_rn(g, sg), u);
     }
-    if (!grid_sync(a.ctl, target, a.status, &sh_ok)) return;
+    if (!grid_sync(a.ctl, k_bar, a.status, &sh_ok)) return drain();
+    if (l + 1 < L) pC = true;
+    if (tid == 0 && l + 1 < L) {  // region C is free: the next layer's Wgate / Wup rows
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      stage_C(l + 1);
+    }
 
     // ---------------- D: x_new = x + Wdown . SwiGLU (MatVecAddQ8_0), this CTA's rows ----------------
-    for (int i = tid; i < a.ffn; i += FS_THREADS) xn[i] = ldcg(a.hbuf + i);
+    for (int i0 = 0; i0 < a.ffn; i0 += 4 * FS_THREADS) {
+      float v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u * FS_THREADS + tid;
+        v[u] = i < a.ffn ? ldcg(a.hbuf + i) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u * FS_THREADS + tid;
+        if (i < a.ffn) xn[i] = v[u];
+      }
+    }
     __syncthreads();
-    gemv_rows(W.dn_qs, W.dn_d, a.ffn, xn, n0, n1, [&](int row, float v) { a.x[row] = xs[row] + v; });
-    if (!grid_sync(a.ctl, target, a.status, &sh_ok)) return;
+    if (!mbar_wait(bD, parD, &sh_abort, a.status, 42)) {
+      atomicExch(a.ctl + 1, 1u);
+      return drain();
+    }
+    pD = false;
+    parD ^= 1;
+    gemv_smem(wD, reinterpret_cast<const uint16_t*>(wD + (size_t)nD * a.ffn), a.ffn, xn, nD,
+              [&](int r, float v) { a.x[n0 + r] = xs[n0 + r] + v; });
+    if (!grid_sync(a.ctl, k_bar, a.status, &sh_ok)) return drain();
+    if (l + 1 < L) pD = true;
+    else pL = true;
+    if (tid == 0) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      if (l + 1 < L) {
+        stage_D(l + 1);
+      } else {  // after the last layer every region is free: the LM head's rows
+        mbar_arrive_tx(bL, row_bytes(a.dim, v0, v1));
+        copy_rows(wts, reinterpret_cast<uint16_t*>(wts + (size_t)nV * a.dim), a.lm_qs, a.lm_d, a.dim, v0, v1, bL);
+      }
+    }
     for (int i = tid; i < a.dim; i += FS_THREADS) xs[i] = ldcg(a.x + i);
     __syncthreads();
   }
 
   // ---------------- LM head ----------------
   rmsnorm_s(xs, a.final_norm, xn, a.dim, a.eps, red);
-  int v0, v1;
-  share(a.vocab, v0, v1);
-  gemv_rows(a.lm_qs, a.lm_d, a.dim, xn, v0, v1, [&](int row, float v) { a.logits[row] = v; });
+  if (!mbar_wait(bL, 0, &sh_abort, a.status, 42)) {
+    atomicExch(a.ctl + 1, 1u);
+    return drain();
+  }
+  gemv_smem(wts, reinterpret_cast<const uint16_t*>(wts + (size_t)nV * a.dim), a.dim, xn, nV,
+            [&](int r, float v) { a.logits[v0 + r] = v; });
   if (blockIdx.x == 0 && tid == 0) *a.pos = pos + 1;
 }
 
@@ -520,19 +734,28 @@ int fused_step_plan(FusedStepArgs& a, int sms, int max_ctx, size_t* smem, const 
   if (a.hd != 64 && a.hd != 128) return no("head size must be 64 or 128");
   if (a.dim % 256 || a.ffn % 256 || a.q_dim % 256) return no("dim, ffn and q_dim must be multiples of 256");
   if (a.hq % a.hkv || a.hq > sms) return no("heads must divide by kv heads and fit the grid");
-  if ((long long)a.hq * a.dim > 65536) return no("heads x dim above 65536");
-  if (a.page_size <= 0 || max_ctx <= 0) return no("no context capacity");
+  if (a.page_size <= 0 || max_ctx <= 0 || a.max_pages <= 0) return no("no context capacity");
+  if (a.max_pages > 4096) return no("page-table row above 4096 pages");
   a.splits = std::max(1, sms / a.hq);
+  if (a.splits * (a.hd + 2) > FS_WAVE) return no("too many attention splits for the merge area");
   const int score_cap = (max_ctx + a.splits - 1) / a.splits + 1;
   const int vocab_share = (a.vocab + sms - 1) / sms + 1;
   a.score_cap = (std::max(score_cap, std::max(vocab_share, a.hd)) + 3) / 4 * 4;
   a.dim_pad = (a.dim + 3) / 4 * 4;
-  a.vec_pad = (std::max(a.dim, std::max(a.ffn, (FS_THREADS / a.hd) * a.hd)) + 3) / 4 * 4;
+  a.vec_pad = (std::max(a.dim, a.ffn) + 3) / 4 * 4;
   const int qkv_rows = 2 * ((a.qkv_dim / 2 + sms - 1) / sms);
-  const int ffn_rows = 2 * ((a.ffn + sms - 1) / sms);
-  a.row_cap = (std::max(qkv_rows, ffn_rows) + 3) / 4 * 4;
-  const size_t bytes = (size_t)(a.dim_pad + a.vec_pad + a.row_cap + a.score_cap + 64 + 128) * sizeof(float);
-  if (bytes > 200 * 1024) return no("shared-memory plan above 200 KB");
+  const int ffn_units = (a.ffn + sms - 1) / sms;
+  const int down_rows = (a.dim + sms - 1) / sms;
+  const int lm_rows = (a.vocab + sms - 1) / sms;
+  a.row_cap = (std::max(qkv_rows, 2 * ffn_units) + 3) / 4 * 4;
+  a.pt_pad = (a.max_pages + 3) / 4 * 4;
+  const size_t rb_dim = (size_t)a.dim + a.dim / 16, rb_ffn = (size_t)a.ffn + a.ffn / 16;
+  const size_t layer_bytes = (size_t)qkv_rows * rb_dim + (size_t)2 * ffn_units * rb_dim + (size_t)down_rows * rb_ffn;
+  const size_t wt_bytes = std::max(layer_bytes, (size_t)lm_rows * rb_dim);
+  if (wt_bytes >= (1u << 20)) return no("a CTA's staged rows above 1 MB");
+  const size_t floats = (size_t)a.dim_pad + a.vec_pad + a.row_cap + a.score_cap + 64 + 128 + 128 + FS_WAVE + a.pt_pad;
+  const size_t bytes = floats * sizeof(float) + (wt_bytes + 15) / 16 * 16;
+  if (bytes > 220 * 1024) return no("shared-memory plan above 220 KB");
   a.scale_log2 = (1.0f / (float)std::sqrt((double)a.hd)) * FS_LOG2E;
   *smem = bytes;
   return kOk;
@@ -547,7 +770,7 @@ int fused_step_launch(const FusedStepArgs& a, int sms, size_t smem, cudaStream_t
   // per device (the attribute belongs to the current device's context); a host call of about a microsecond
   if (cudaFuncSetAttribute(fused_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return kCudaError;
-  if (cudaMemsetAsync(a.ctl, 0, (2 + a.hq) * sizeof(unsigned), s) != cudaSuccess) return kCudaError;
+  if (cudaMemsetAsync(a.ctl, 0, (3 + a.hq) * sizeof(unsigned), s) != cudaSuccess) return kCudaError;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(sms);
   cfg.blockDim = dim3(FS_THREADS);

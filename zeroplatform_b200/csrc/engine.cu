@@ -518,6 +518,8 @@ int setup_fused(Engine* E) {
   a.qkv_dim = E->qkv_dim;
   a.eps = c.eps;
   a.page_size = c.page_size;
+  a.max_pages = c.max_pages_per_seq;
+  a.num_pages = c.total_pages;
   int sms = 0;
   E_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, E->device));
   const char* why = nullptr;
@@ -535,8 +537,8 @@ int setup_fused(Engine* E) {
   float* scratch = nullptr;
   E_RC(dalloc(E, &scratch, fused_step_scratch_floats(a, sms)));
   unsigned* ctl = nullptr;
-  E_RC(dalloc(E, &ctl, (size_t)(2 + a.hq)));
-  E_CUDA(cudaMemset(ctl, 0, (2 + a.hq) * sizeof(unsigned)));
+  E_RC(dalloc(E, &ctl, (size_t)(3 + a.hq)));
+  E_CUDA(cudaMemset(ctl, 0, (3 + a.hq) * sizeof(unsigned)));
   a.part = scratch;
   a.P = a.part + (size_t)a.hq * a.splits * (a.hd + 2);
   a.qbuf = a.P + (size_t)a.hq * a.dim;

@@ -171,13 +171,13 @@ struct FusedStepArgs {
   int32_t *gen_out, *gen_step, *past, *past_len, *done;
   int past_cap, eos;
   float penalty;
-  // device scratch (fused_step_scratch_floats) and control words [2 + hq] (cleared by the launcher)
+  // device scratch (fused_step_scratch_floats) and control words [3 + hq] (cleared by the launcher)
   float *x, *qbuf, *hbuf, *part, *P;
   int2* pairs;
   unsigned* ctl;
   int* status;
   // filled by fused_step_plan
-  int splits, score_cap, dim_pad, vec_pad, row_cap;
+  int splits, score_cap, dim_pad, vec_pad, row_cap, pt_pad;
   float scale_log2;
 };
 // kOk when the shapes fit the fused step on `sms` SMs (fills the plan fields and the shared-memory size), else
