@@ -42,7 +42,7 @@ def _fused_tokens(m, prompt, n_new, penalty=1.0, eos=-1, fused=True, **kw):
 MODELS = {
     "d768_h12": dict(vocab=4096, dim=768, layers=3, heads=12, kv_heads=12, ffn=2048, seed=31),
     "d512_gqa4": dict(vocab=3000, dim=512, layers=4, heads=8, kv_heads=2, ffn=1024, seed=32),
-    "d1024_hd128": dict(vocab=2048, dim=1024, layers=2, heads=8, kv_heads=4, ffn=2816, seed=33),
+    "d1024_hd128": dict(vocab=2048, dim=1024, layers=2, heads=8, kv_heads=4, ffn=2560, seed=33),
 }
 
 

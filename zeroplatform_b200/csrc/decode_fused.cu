@@ -31,8 +31,10 @@
 // GEMVs read shared memory.  Wo, read by columns of a head in phase B, is prefetched into L2 by row shares.  Loads
 // that depend on a barrier (K/V, partials, Wo slices, the heads' partial sums) are issued all at once.  Data
 // written in this kernel by another CTA (qbuf, K/V pages, partials, P, hbuf, x, pairs) is read through L2
-// (ld.global.cg); weights through the non-coherent path.  Projections compute in fp32 on exactly converted int8
-// values; Wo is summed per head and then over heads, another fp32 order than one MatVecAdd over all columns.
+// (ld.global.cg); weights through the non-coherent path.  The staged projections take their activations as int16
+// per 32-block (each value within 2^-16 of its block's largest, the form of the 4096-column slab GEMV) and sum exact
+// int32 block products; Wo (in phase B) takes fp32 activations.  Wo is summed per head and then over heads, another
+// fp32 order than one MatVecAdd over all columns.
 
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -50,8 +52,6 @@ namespace {
 
 constexpr int FS_THREADS = 512;
 constexpr int FS_WARPS = FS_THREADS / 32;
-constexpr int FS_G = 16;  // lanes per weight row
-constexpr int FS_ROWS_PER_PASS = FS_THREADS / FS_G;
 constexpr uint64_t FS_WAIT_NS = 2000000000ull;  // a grid barrier that waits longer than 2 s gives up
 constexpr float FS_LOG2E = 1.4426950408889634f;
 constexpr int FS_WAVE = 4096;  // floats of the attention reduction area (tokens of a wave x hd)
@@ -147,54 +147,100 @@ __device__ __forceinline__ float dot16_s(const int4& w, const float* xs) {
   return s.x + s.y;
 }
 
-// The same product with the four 4-value groups visited in the order r, r+1, r+2, r+3 (mod 4): with r = (chunk / 2)
-// % 4 the 8 lanes of a 128-bit shared-memory phase, which read chunks 64 bytes apart, hit 8 distinct bank groups.
-__device__ __forceinline__ float dot16_rot(const int4& w, const float* xs, int r) {
-  const float2 bias = make_float2(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
-  const float4* x4 = reinterpret_cast<const float4*>(xs);
-  float2 s = make_float2(0.f, 0.f);
+// GEMV of rows staged in shared memory against x in shared memory.  Each lane owns CPL 16-value chunks of the K
+// columns (chunk c = lane-in-group + G * k) and keeps them in registers as int16 with a per-32-block scale
+// (q = rint(x * 32767 / max|x|): every value within 2^-16 of its block's largest), read and quantized once per
+// call; per row a lane then reads only its 16-byte weight chunks and the block scales from shared memory, and a
+// chunk is 8 DP2A instructions (two int16 x int8 products each, exact in int32), one conversion and one FMA.  G
+// lanes per row (G * CPL = K / 16), so a warp holds 32 / G row groups; the loop is uniform over the warp (a
+// missing row computes zeros) so the full-warp shuffles always have all 32 lanes.  emit(local row, value) runs on
+// the group's first lane.
+template <int CPL>
+struct XChunks {
+  int v[CPL][8];
+  float s[CPL];
+};
+
+template <int G, int CPL>
+__device__ __forceinline__ void quantize_chunks(const float* xs, XChunks<CPL>& xq) {
+  const int li = threadIdx.x % G;
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int jj = (j + r) & 3;
-    const uint32_t word = jj == 0 ? (uint32_t)w.x : jj == 1 ? (uint32_t)w.y : jj == 2 ? (uint32_t)w.z : (uint32_t)w.w;
-    const uint32_t b = word ^ 0x80808080u;
-    const float4 xv = x4[jj];
-    const float2 p01 = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(b, 0x4B000000u, 0x7650)),
-                                              __uint_as_float(__byte_perm(b, 0x4B000000u, 0x7651))),
-                                  bias);
-    const float2 p23 = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(b, 0x4B000000u, 0x7652)),
-                                              __uint_as_float(__byte_perm(b, 0x4B000000u, 0x7653))),
-                                  bias);
-    s = __ffma2_rn(p01, make_float2(xv.x, xv.y), s);
-    s = __ffma2_rn(p23, make_float2(xv.z, xv.w), s);
+  for (int k = 0; k < CPL; ++k) {
+    const float4* x4 = reinterpret_cast<const float4*>(xs + (li + G * k) * 16);
+    float v[16];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float4 f = x4[j];
+      v[4 * j] = f.x;
+      v[4 * j + 1] = f.y;
+      v[4 * j + 2] = f.z;
+      v[4 * j + 3] = f.w;
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(v[j]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));  // the other half of the 32-block
+    const float inv = amax > 0.f ? 32767.0f / amax : 0.f;
+    xq.s[k] = amax * (1.0f / 32767.0f);
+    const float2 inv2 = make_float2(inv, inv), mg2 = make_float2(12582912.0f, 12582912.0f);  // 1.5 * 2^23
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float2 r = __ffma2_rn(make_float2(v[2 * j], v[2 * j + 1]), inv2, mg2);
+      xq.v[k][j] = (int)__byte_perm(__float_as_uint(r.x), __float_as_uint(r.y), 0x5410);
+    }
   }
-  return s.x + s.y;
 }
 
-// nrows rows staged in shared memory (int8 rows of K at sq, fp16 scales at sd) times x (shared memory): FS_G
-// lanes per row, chunks strided over the lanes, a shuffle reduction; emit(local row, value) on the group's first
-// lane.  The loop is uniform over each warp (its two row groups iterate together; a missing row computes zeros), so
-// the full-warp shuffles always have all 32 lanes.
-template <class Emit>
-__device__ __forceinline__ void gemv_smem(const uint8_t* sq, const uint16_t* sd, int K, const float* xs, int nrows,
-                                          Emit emit) {
-  const int gi = threadIdx.x / FS_G, li = threadIdx.x % FS_G;
-  const int warp = threadIdx.x >> 5, sub = gi & 1;
-  const int nch = K / 16, kb = K / QK;
-  for (int base = 2 * warp; base < nrows; base += FS_ROWS_PER_PASS) {
+template <int G, int CPL, class Emit>
+__device__ __forceinline__ void gemv_q(const uint8_t* sq, const uint16_t* sd, const float* xs, int nrows, Emit emit) {
+  constexpr int K = G * CPL * 16, KB = K / QK, RPW = 32 / G;
+  XChunks<CPL> xq;
+  quantize_chunks<G, CPL>(xs, xq);
+  const int li = threadIdx.x % G, sub = (threadIdx.x & 31) / G, warp = threadIdx.x >> 5;
+  for (int base = RPW * warp; base < nrows; base += RPW * (FS_THREADS / 32)) {
     const int r = base + sub;
     const bool valid = r < nrows;
     const uint8_t* wr = sq + (size_t)(valid ? r : 0) * K;
-    const uint16_t* dr = sd + (size_t)(valid ? r : 0) * kb;
+    const uint16_t* dr = sd + (size_t)(valid ? r : 0) * KB;
     float acc = 0.f;
-    for (int c = li; c < nch; c += FS_G)
-      acc = fmaf(h2f(dr[c >> 1]), dot16_rot(*reinterpret_cast<const int4*>(wr + (size_t)c * 16), xs + c * 16,
-                                             (c >> 1) & 3),
-                 acc);
 #pragma unroll
-    for (int o = FS_G / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    for (int k = 0; k < CPL; ++k) {
+      const int c = li + G * k;
+      const int4 w = *reinterpret_cast<const int4*>(wr + (size_t)c * 16);
+      int d = __dp2a_lo(xq.v[k][0], w.x, 0);
+      d = __dp2a_hi(xq.v[k][1], w.x, d);
+      d = __dp2a_lo(xq.v[k][2], w.y, d);
+      d = __dp2a_hi(xq.v[k][3], w.y, d);
+      d = __dp2a_lo(xq.v[k][4], w.z, d);
+      d = __dp2a_hi(xq.v[k][5], w.z, d);
+      d = __dp2a_lo(xq.v[k][6], w.w, d);
+      d = __dp2a_hi(xq.v[k][7], w.w, d);
+      acc = fmaf(h2f(dr[c >> 1]) * xq.s[k], (float)d, acc);
+    }
+#pragma unroll
+    for (int o = G / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
     if (valid && li == 0) emit(r, acc);
   }
+}
+
+// K-dispatch of gemv_q (the K values fused_step_plan admits)
+template <class Emit>
+__device__ __forceinline__ void gemv_smem(const uint8_t* sq, const uint16_t* sd, int K, const float* xs, int nrows,
+                                          Emit emit) {
+  switch (K) {
+    case 512: gemv_q<16, 2>(sq, sd, xs, nrows, emit); break;
+    case 768: gemv_q<16, 3>(sq, sd, xs, nrows, emit); break;
+    case 1024: gemv_q<16, 4>(sq, sd, xs, nrows, emit); break;
+    case 2048: gemv_q<32, 4>(sq, sd, xs, nrows, emit); break;
+    case 2560: gemv_q<32, 5>(sq, sd, xs, nrows, emit); break;
+    case 3072: gemv_q<32, 6>(sq, sd, xs, nrows, emit); break;
+    case 4096: gemv_q<32, 8>(sq, sd, xs, nrows, emit); break;
+    default: break;
+  }
+}
+
+__host__ __device__ constexpr bool fused_k_ok(int K) {
+  return K == 512 || K == 768 || K == 1024 || K == 2048 || K == 2560 || K == 3072 || K == 4096;
 }
 
 // xn = RmsNorm(x) * w (RmsNorm.Forward, Layers/RmsNorm.cs:14-59): mean of squares in fp32,
@@ -733,6 +779,7 @@ int fused_step_plan(FusedStepArgs& a, int sms, int max_ctx, size_t* smem, const 
   };
   if (a.hd != 64 && a.hd != 128) return no("head size must be 64 or 128");
   if (a.dim % 256 || a.ffn % 256 || a.q_dim % 256) return no("dim, ffn and q_dim must be multiples of 256");
+  if (!fused_k_ok(a.dim) || !fused_k_ok(a.ffn)) return no("dim and ffn must be 512, 768, 1024, 2048, 2560, 3072 or 4096");
   if (a.hq % a.hkv || a.hq > sms) return no("heads must divide by kv heads and fit the grid");
   if (a.page_size <= 0 || max_ctx <= 0 || a.max_pages <= 0) return no("no context capacity");
   if (a.max_pages > 4096) return no("page-table row above 4096 pages");
