@@ -214,6 +214,36 @@ ZC_API int32_t zcu_engine_generate(void* engine, int32_t seq_id, const int32_t* 
  * graph of per-operator kernels (ZCU_FUSED_DECODE=0 in the environment forces it), -1 = not decided yet (no
  * generate call so far).  `why` (may be NULL) receives the reason the one-kernel form is not used. */
 ZC_API int32_t zcu_engine_step_kind(void* engine, char* why, int32_t cap);
+/* SamplingConfig (ZeroLlm/src/ZeroLlm.Core/Sampling/SamplingConfig.cs:8-26): Temperature, TopP, MinP, TopK
+ * (0 = no limit), RepetitionPenalty. */
+typedef struct {
+  float temperature, top_p, min_p;
+  int32_t top_k;
+  float repetition_penalty;
+} zcu_sampling_config;
+
+/* LlmSampler.Sample (Sampling/LlmSampler.cs:21-172) for `rows` rows of device logits [rows][vocab], modified in
+ * place as the reference modifies its span (penalty, temperature, probabilities).  past [rows][past_cap] with
+ * past_len [rows] (device, may be NULL) are the tokens the penalty applies to; uniforms [rows] (device) stand for
+ * (float)random.NextDouble() and are unused on the greedy branch (temperature <= 0.001 or top_k == 1).  out [rows]
+ * (device) receives the token, or -1 when more than 4096 candidates remain after Top-K (top_k 0 over a flat
+ * distribution).  cand_idx / cand_p [rows][cand_cap] and n_cand [rows] (device, may be NULL) receive the kept
+ * candidates by probability descending (the lower token id first among equal probabilities), their renormalised
+ * probabilities and their count.  Enqueues only. */
+ZC_API int32_t zcu_sample(float* logits, int32_t rows, int32_t vocab, const int32_t* past, const int32_t* past_len,
+                          int32_t past_cap, const zcu_sampling_config* cfg, const float* uniforms, int32_t* out,
+                          int32_t* cand_idx, float* cand_p, int32_t* n_cand, int32_t cand_cap, void* stream);
+/* The draw the engine's sampled generation uses for its i-th token: SplitMix64(seed + i), top 24 bits, in [0, 1)
+ * (host helper; no counterpart in the reference, whose System.Random draws cannot be reproduced). */
+ZC_API float zcu_sample_uniform(uint64_t seed, uint64_t i);
+/* GenerateStreamAsync with any SamplingConfig (LlmEngine.cs:71-150): prefill, then n_new steps of sample ->
+ * ForwardToken with the sampler on the device (the i-th token's draw is zcu_sample_uniform(seed, i)), replayed
+ * from one captured graph; a greedy config runs zcu_engine_generate.  One GPU (tp_size 1) only: -4 otherwise.
+ * Returns the tokens written to out_tokens (a token equal to eos_token >= 0 ends generation unwritten) or < 0;
+ * timing_ms[0] = prefill ms, timing_ms[1] = decode ms. */
+ZC_API int32_t zcu_engine_generate_sampled(void* engine, int32_t seq_id, const int32_t* prompt, int32_t n_prompt,
+                                           int32_t n_new, const zcu_sampling_config* cfg, uint64_t seed,
+                                           int32_t eos_token, int32_t* out_tokens, float* timing_ms);
 /* Batched greedy generation (GenerateStreamAsync for `batch` live sequences at once, repetition penalty 1):
  * tokens[b] is fed at position seq_len(seq_ids[b]); each of n_new steps runs ForwardToken for every sequence
  * and samples greedily, replayed from one captured CUDA graph (collectives included).  out_tokens[b * n_new + i]

@@ -4,6 +4,7 @@ import glob
 import os
 import re
 
+import numpy as np
 import pytest
 
 from tests.conftest import ROOT
@@ -89,3 +90,29 @@ def test_paged_attention_shapes_are_checked_before_any_device_work():
         assert call(fn, max_pages=0) == -2
         assert call(fn, hd=48) == -4
         assert L.zc_cuda_last_error()
+
+
+def test_sampler_draw_is_splitmix64():
+    """zcu_sample_uniform(seed, i) = the top 24 bits of SplitMix64(seed + i) over 2^24 (the sampled generation's
+    i-th draw), restated here in Python; the sampler refuses a null config or a negative Top-K on the host."""
+    from zeroplatform_b200 import _lib
+    L = _lib.lib()
+    M = (1 << 64) - 1
+
+    def splitmix(x):
+        z = (x + 0x9E3779B97F4A7C15) & M
+        z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & M
+        z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & M
+        z ^= z >> 31
+        return (z >> 40) / float(1 << 24)
+
+    for seed, i in [(0, 0), (1234567, 5), (2 ** 63 + 11, 999), (42, 2 ** 40)]:
+        assert L.zcu_sample_uniform(seed, i) == splitmix((seed + i) & M)
+    us = [L.zcu_sample_uniform(7, i) for i in range(4000)]
+    assert 0.0 <= min(us) and max(us) < 1.0 and abs(float(np.mean(us)) - 0.5) < 0.02
+    from zeroplatform_b200._lib import SamplingConfig
+    buf = (ctypes.c_float * 8)()
+    p = ctypes.addressof(buf)
+    assert L.zcu_sample(p, 1, 8, None, None, 0, None, p, p, None, None, None, 0, None) == -2
+    bad = SamplingConfig(1.0, 0.9, 0.0, -1, 1.0)
+    assert L.zcu_sample(p, 1, 8, None, None, 0, ctypes.byref(bad), p, p, None, None, None, 0, None) == -2

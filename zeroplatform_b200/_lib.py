@@ -86,6 +86,13 @@ SIGNATURES.update({
 })
 
 
+class SamplingConfig(C.Structure):
+    """zcu_sampling_config (include/zero_tensor_cuda.h): SamplingConfig's numeric fields."""
+
+    _fields_ = [("temperature", C.c_float), ("top_p", C.c_float), ("min_p", C.c_float), ("top_k", C.c_int32),
+                ("repetition_penalty", C.c_float)]
+
+
 class TpShard(C.Structure):
     """zcu_tp_shard (include/zero_tensor_cuda.h): one rank's slice of a tensor-parallel model."""
 
@@ -118,6 +125,10 @@ SIGNATURES.update({
     "zcu_moe_ep_plan": (i32, [i32, i32, i32, vp, vp, vp, vp, vp, i32]),
     "zcu_peer_wait_selftest": (i32, [i32, i32, vp]),
     "zcu_engine_step_kind": (i32, [vp, vp, i32]),
+    "zcu_sample": (i32, [vp, i32, i32, vp, vp, i32, C.POINTER(SamplingConfig), vp, vp, vp, vp, vp, i32, vp]),
+    "zcu_sample_uniform": (C.c_float, [C.c_uint64, C.c_uint64]),
+    "zcu_engine_generate_sampled": (i32, [vp, i32, vp, i32, i32, C.POINTER(SamplingConfig), C.c_uint64, i32, vp,
+                                          vp]),
 })
 
 

@@ -680,6 +680,24 @@ int32_t zcu_gemm_q4_0(const uint8_t* qs, const uint16_t* d, const float* x, floa
   return gemm_q4_0_tc(qs, d, x, y, (int)m, (int)n_rows, (int)k_cols, accumulate, ws, bytes, status, s);
 }
 
+int32_t zcu_sample(float* logits, int32_t rows, int32_t vocab, const int32_t* past, const int32_t* past_len,
+                   int32_t past_cap, const zcu_sampling_config* cfg, const float* uniforms, int32_t* out,
+                   int32_t* cand_idx, float* cand_p, int32_t* n_cand, int32_t cand_cap, void* stream) {
+  t_last_error.clear();
+  if (!cfg) return fail(kBadArgument, "null sampling config");
+  if (cfg->top_k < 0) return fail(kBadArgument, "top_k must be >= 0");
+  if ((cand_idx || cand_p) && cand_cap <= 0) return fail(kBadArgument, "cand_cap must be positive");
+  const SampleConfig c{cfg->temperature, cfg->top_p, cfg->min_p, cfg->top_k, cfg->repetition_penalty};
+  const int rc = sample_rows(logits, rows, vocab, past, past_len, past_cap, c, uniforms, out, cand_idx, cand_p, n_cand,
+                             cand_cap, as_stream(stream));
+  if (rc != kOk) return fail(rc, rc == kBadArgument ? "null buffer or non-positive rows / vocab (a non-greedy config "
+                                                      "needs uniforms)"
+                                                    : "sampler launch failed");
+  return kOk;
+}
+
+float zcu_sample_uniform(uint64_t seed, uint64_t i) { return splitmix_uniform(seed + i); }
+
 int32_t zcu_peer_wait_selftest(int32_t ranks, int32_t wait_ms, uint32_t* seen) {
   t_last_error.clear();
   unsigned int st[16] = {};

@@ -90,6 +90,16 @@ __device__ __forceinline__ void u4x4_to_f32(uint32_t v, float& f0, float& f1, fl
   f3 = __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7653)) - bias;
 }
 
+// SplitMix64 (Steele, Lea and Flood, "Fast splittable pseudorandom number generators", OOPSLA 2014) of x, its top
+// 24 bits as a float in [0, 1): the counter-based draw of the device sampler (one per generated token).
+__host__ __device__ inline float splitmix_uniform(uint64_t x) {
+  uint64_t z = x + 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  z ^= z >> 31;
+  return (float)(z >> 40) * (1.0f / 16777216.0f);
+}
+
 // Launches `kernel` with programmatic stream serialization, so it may overlap the tail of the previous
 // kernel in the stream (the kernel itself calls pdl_wait() before reading that kernel's outputs).
 template <typename... KArgs, typename... Args>

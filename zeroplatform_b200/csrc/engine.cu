@@ -157,6 +157,8 @@ struct Engine {
   // generation state (B = 1)
   int32_t *gen_out = nullptr, *gen_step = nullptr, *gen_past = nullptr, *gen_past_len = nullptr,
           *gen_done = nullptr;
+  int32_t* rng_ctr = nullptr;  // draws taken by sampled generation (allocated at its first call)
+  float* uni = nullptr;        // the step's draw
   int gen_cap = 0;
 
   std::vector<int> free_stack;
@@ -585,6 +587,33 @@ int capture_gen_step(Engine* E, float penalty, int eos, cudaGraphExec_t* out) {
   cudaGraph_t g;
   E_CUDA(cudaStreamBeginCapture(E->stream, cudaStreamCaptureModeThreadLocal));
   int rc = sample(E, 1, E->gen_past, E->gen_past_len, E->gen_cap, penalty, E->tokens);
+  if (rc == kOk)
+    rc = advance_generation(E->tokens, E->pos, E->gen_out, E->gen_step, E->gen_past, E->gen_past_len, E->gen_cap, eos,
+                            E->gen_done, E->stream);
+  if (rc == kOk) rc = embed_q8_0(E->tok_emb.qs, E->tok_emb.d, E->tokens, 1, E->cfg.vocab, E->cfg.dim, E->x, E->stream);
+  if (rc == kOk) rc = forward(E, 1, false);
+  if (rc == kOk) {
+    add_one_kernel<<<1, 32, 0, E->stream>>>(E->pos);
+    if (cudaPeekAtLastError() != cudaSuccess) rc = kCudaError;
+  }
+  cudaError_t ce = cudaStreamEndCapture(E->stream, &g);
+  if (rc != kOk) return rc;
+  E_CUDA(ce);
+  ce = cudaGraphInstantiate(out, g, 0);
+  cudaGraphDestroy(g);
+  E_CUDA(ce);
+  return kOk;
+}
+
+// One step of sampled generation (B = 1): draw -> LlmSampler.Sample on the previous logits -> advance -> embed ->
+// forward -> pos++.
+int capture_sampled_step(Engine* E, const SampleConfig& sc, uint64_t seed, int eos, cudaGraphExec_t* out) {
+  cudaGraph_t g;
+  E_CUDA(cudaStreamBeginCapture(E->stream, cudaStreamCaptureModeThreadLocal));
+  int rc = draw_uniforms(seed, E->rng_ctr, 1, E->uni, E->stream);
+  if (rc == kOk)
+    rc = sample_rows(E->logits, 1, E->vocab, E->gen_past, E->gen_past_len, E->gen_cap, sc, E->uni, E->tokens, nullptr,
+                     nullptr, nullptr, 0, E->stream);
   if (rc == kOk)
     rc = advance_generation(E->tokens, E->pos, E->gen_out, E->gen_step, E->gen_past, E->gen_past_len, E->gen_cap, eos,
                             E->gen_done, E->stream);
@@ -1043,6 +1072,80 @@ int32_t zcu_engine_step_kind(void* engine, char* why, int32_t cap) {
   }
   if (!E->fused_tried) return -1;
   return E->fused_ok ? 1 : 0;
+}
+
+int32_t zcu_engine_generate_sampled(void* engine, int32_t seq_id, const int32_t* prompt, int32_t n_prompt,
+                                    int32_t n_new, const zcu_sampling_config* cfg, uint64_t seed, int32_t eos_token,
+                                    int32_t* out_tokens, float* timing_ms) {
+  using namespace zc;
+  Engine* E = static_cast<Engine*>(engine);
+  if (!E || !cfg || !prompt || n_prompt <= 0 || n_new < 0 || !out_tokens || cfg->top_k < 0) return kBadArgument;
+  if (cfg->temperature <= 0.001f || cfg->top_k == 1)  // LlmSampler's greedy branch: the greedy generation path
+    return zcu_engine_generate(engine, seq_id, prompt, n_prompt, n_new, cfg->repetition_penalty, eos_token,
+                               out_tokens, timing_ms);
+  E->err.clear();
+  if (E->tp_size != 1) {
+    E->err = "sampled generation runs on one GPU (each tensor-parallel rank holds a vocabulary slice)";
+    return kUnsupported;
+  }
+  if (n_prompt + n_new + 1 > E->gen_cap) {
+    E->err = "prompt + generated tokens exceed the sequence capacity";
+    return kTooLarge;
+  }
+  if (!E->rng_ctr) {
+    E_RC(dalloc(E, &E->rng_ctr, 1));
+    E_RC(dalloc(E, &E->uni, 1));
+  }
+  cudaEvent_t ev[3];
+  for (auto& e : ev) E_CUDA(cudaEventCreate(&e));
+  E_CUDA(cudaEventRecord(ev[0], E->stream));
+  E_RC(zcu_engine_prefill(engine, seq_id, prompt, n_prompt, 0, nullptr));
+  Seq* s = nullptr;
+  E_RC(get_seq(E, seq_id, &s));
+  E_RC(ensure_pages(E, *s, n_prompt + n_new));
+  const int32_t zero = 0;
+  E_CUDA(cudaMemcpyAsync(E->gen_past, prompt, n_prompt * 4, cudaMemcpyHostToDevice, E->stream));
+  E_CUDA(cudaMemcpyAsync(E->gen_past_len, &n_prompt, 4, cudaMemcpyHostToDevice, E->stream));
+  E_CUDA(cudaMemcpyAsync(E->gen_step, &zero, 4, cudaMemcpyHostToDevice, E->stream));
+  E_CUDA(cudaMemcpyAsync(E->gen_done, &zero, 4, cudaMemcpyHostToDevice, E->stream));
+  E_CUDA(cudaMemcpyAsync(E->rng_ctr, &zero, 4, cudaMemcpyHostToDevice, E->stream));
+  E_CUDA(cudaMemcpyAsync(E->pos, &n_prompt, 4, cudaMemcpyHostToDevice, E->stream));
+  const int32_t row = s->row;
+  E_CUDA(cudaMemcpyAsync(E->rows, &row, 4, cudaMemcpyHostToDevice, E->stream));
+  E_RC(wait(E));
+  E_CUDA(cudaEventRecord(ev[1], E->stream));
+  if (n_new > 0) {
+    const SampleConfig sc{cfg->temperature, cfg->top_p, cfg->min_p, cfg->top_k, cfg->repetition_penalty};
+    cudaGraphExec_t ge;
+    E_RC(capture_sampled_step(E, sc, seed, eos_token, &ge));
+    for (int i = 0; i < n_new; ++i) {
+      const cudaError_t ce = cudaGraphLaunch(ge, E->stream);
+      if (ce != cudaSuccess) {
+        cudaGraphExecDestroy(ge);
+        E->err = std::string("cudaGraphLaunch: ") + cudaGetErrorString(ce);
+        return kCudaError;
+      }
+    }
+    E_CUDA(cudaStreamSynchronize(E->stream));
+    cudaGraphExecDestroy(ge);
+  }
+  E_CUDA(cudaEventRecord(ev[2], E->stream));
+  int32_t produced = 0;
+  E_CUDA(cudaMemcpyAsync(&produced, E->gen_step, 4, cudaMemcpyDeviceToHost, E->stream));
+  E_RC(wait(E));
+  E_CUDA(cudaMemcpy(out_tokens, E->gen_out, (size_t)std::max(produced, 0) * 4, cudaMemcpyDeviceToHost));
+  if (timing_ms) {
+    cudaEventElapsedTime(&timing_ms[0], ev[0], ev[1]);
+    cudaEventElapsedTime(&timing_ms[1], ev[1], ev[2]);
+  }
+  for (auto& e : ev) cudaEventDestroy(e);
+  s->len = n_prompt + n_new;
+  for (int i = 0; i < produced; ++i)
+    if (out_tokens[i] < 0) {
+      E->err = "more than 4096 sampling candidates after Top-K: use a Top-K of at most 4096";
+      return kUnsupported;
+    }
+  return produced;
 }
 
 int32_t zcu_engine_free_sequence(void* engine, int32_t seq_id) {

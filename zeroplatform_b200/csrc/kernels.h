@@ -137,6 +137,23 @@ int causal_lengths(const int32_t* pos, int B, int32_t* ctx_excl, int32_t* ctx_in
 int advance_generation(const int32_t* tok, int32_t* pos, int32_t* out, int32_t* step, int32_t* past,
                        int32_t* past_len, int past_cap, int eos, int32_t* done, cudaStream_t s);
 
+// ---- LlmSampler.Sample on the device (sampler.cu) ----
+constexpr int SAMPLE_MAX_CAND = 4096;  // candidates kept after Top-K that one row can sort
+struct SampleConfig {
+  float temperature, top_p, min_p;
+  int top_k;
+  float penalty;
+};
+// Samples `rows` logit rows in place (the reference mutates its logits span); uniforms[row] stands for
+// (float)random.NextDouble().  out[row] = token, or -1 when more than SAMPLE_MAX_CAND candidates survive Top-K.
+// cand_idx / cand_p [rows][cand_cap] and n_cand (each may be null) receive the kept candidates, their renormalised
+// probabilities and their count (0 on the greedy branch).
+int sample_rows(float* logits, int rows, int vocab, const int32_t* past, const int32_t* past_len, int past_cap,
+                const SampleConfig& cfg, const float* uniforms, int32_t* out, int32_t* cand_idx, float* cand_p,
+                int32_t* n_cand, int cand_cap, cudaStream_t s);
+// u[r] = splitmix_uniform(seed + *counter + r) for r < rows (<= 1024); *counter += rows.
+int draw_uniforms(uint64_t seed, int32_t* counter, int rows, float* u, cudaStream_t s);
+
 // ---- one greedy generation step of one sequence as a single cooperative kernel (decode_fused.cu) ----
 struct FusedLayerW {
   const int8_t* qkv_qs;

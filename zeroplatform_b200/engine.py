@@ -138,6 +138,19 @@ class LlmEngine:
                                                   eos_token, out.ctypes.data, timing), "generate")
         return out[:n].copy(), float(timing[0]), float(timing[1])
 
+    def generate_sampled(self, seq_id: int, prompt, n_new: int, temperature=0.7, top_p=0.9, min_p=0.0, top_k=40,
+                         repetition_penalty=1.1, seed=0, eos_token: int = -1):
+        """GenerateStreamAsync with a SamplingConfig (defaults: SamplingConfig's), the sampler on the device; the i-th
+        token's draw is zcu_sample_uniform(seed, i).  Returns (tokens, prefill_ms, decode_ms)."""
+        from ._lib import SamplingConfig
+        cfg = SamplingConfig(temperature, top_p, min_p, top_k, repetition_penalty)
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.empty(max(n_new, 1), dtype=np.int32)
+        timing = (C.c_float * 2)()
+        n = self._check(lib().zcu_engine_generate_sampled(self._h, seq_id, p.ctypes.data, p.size, n_new, C.byref(cfg),
+                                                          seed, eos_token, out.ctypes.data, timing), "generate_sampled")
+        return out[:n].copy(), float(timing[0]), float(timing[1])
+
     def step_kind(self):
         """(1, "") when generation runs one cooperative kernel per token, (0, reason) for the per-operator graph,
         (-1, "") before the first generate call."""

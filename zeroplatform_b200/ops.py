@@ -19,6 +19,8 @@ from __future__ import annotations
 import numpy as np
 import torch
 
+import ctypes as C
+
 from ._lib import ZcError, check, lib
 
 QK = 32
@@ -190,3 +192,33 @@ def paged_attention_batched(q, k_pool, v_pool, page_table, ctx_len, hkv: int, pa
                                     page_size, page_table.shape[1], num_pages, page_stride, slot_stride,
                                     head_stride, scale, max_ctx, _stream(stream)), "zcu_paged_attention")
     return out
+
+
+class LlmSampler:
+    """LlmSampler.Sample (ZeroLlm/src/ZeroLlm.Core/Sampling/LlmSampler.cs:21-172) on device logits."""
+
+    @staticmethod
+    def sample(logits: torch.Tensor, past=None, temperature=0.7, top_p=0.9, min_p=0.0, top_k=40,
+               repetition_penalty=1.1, u=None, stream=None) -> torch.Tensor:
+        """logits [rows][vocab] fp32 on the device (modified in place, as the reference modifies its span); past: a
+        list of token sequences, one per row (or None); u [rows]: the draws standing for (float)random.NextDouble()
+        (unused on the greedy branch).  Returns the tokens [rows] (int32, device)."""
+        from ._lib import SamplingConfig
+        lg = logits if logits.dim() == 2 else logits.view(1, -1)
+        rows, vocab = lg.shape
+        cfg = SamplingConfig(temperature, top_p, min_p, top_k, repetition_penalty)
+        past_t = plen_t = None
+        pcap = 0
+        if past is not None:
+            pcap = max(1, max(len(p) for p in past))
+            buf = np.zeros((rows, pcap), np.int32)
+            lens = np.zeros(rows, np.int32)
+            for r, p in enumerate(past):
+                buf[r, :len(p)] = p
+                lens[r] = len(p)
+            past_t, plen_t = torch.from_numpy(buf).to(lg.device), torch.from_numpy(lens).to(lg.device)
+        u_t = None if u is None else torch.as_tensor(u, dtype=torch.float32, device=lg.device).reshape(rows)
+        out = torch.empty(rows, dtype=torch.int32, device=lg.device)
+        check(lib().zcu_sample(lg.data_ptr(), rows, vocab, _ptr(past_t), _ptr(plen_t), pcap, C.byref(cfg), _ptr(u_t),
+                               out.data_ptr(), None, None, None, 0, _stream(stream)), "sample")
+        return out
