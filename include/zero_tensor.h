@@ -49,9 +49,11 @@ ZC_API int32_t zc_gemm_f32(size_t m, size_t n, size_t k, float alpha, const floa
                     const float* b, intptr_t rsb, intptr_t csb, float beta, float* c, intptr_t rsc, intptr_t csc,
                     int32_t parallel);
 
-/* zc_flash_attention_f32 (ZeroTensorNativeBridge.cs:96,290-302; caller TensorOps.Neural.cs:1062-1080).
- * Exported so that the bridge initialises; prefill attention is outside this library's scope and the
- * call returns -1 (not handled), so ZeroTensor runs its managed FlashAttention. */
+/* zc_flash_attention_f32 (ZeroTensorNativeBridge.cs:96,290-302; caller TensorOps.Neural.cs:1062-1080):
+ * TensorOps.FlashAttentionCpu on the device.  q [batch][sq][d], k [kv batch][sk][d], v [kv batch][sk][dv], out
+ * [batch][sq][dv]; kv batch of b = is_gqa ? (b / hq) * hkv + (b % hq) / group : b.  Handles mask == NULL, dv == d,
+ * d one of 16 / 32 / 64 / 128; returns -1 (not handled: the managed FlashAttention runs) for a mask, whose broadcast
+ * extent the ABI does not carry, and for other shapes.  sk == 0 gives zeros. */
 ZC_API int32_t zc_flash_attention_f32(size_t batch, size_t sq, size_t sk, size_t d, size_t dv, float scale, int32_t is_gqa,
                                size_t hq, size_t hkv, size_t group, const float* q, const float* k, const float* v,
                                const float* mask, float* out);

@@ -84,6 +84,8 @@ def lib():
         "orc_dot_f32": (C.c_float, [_f32p, _f32p, C.c_int]),
         "orc_gqa_attention": (None, [_f32p, _f32p, _f32p, _i32p, C.c_int, sz, C.c_int, C.c_int, C.c_int,
                                      C.c_int, _f32p]),
+        "orc_flash_attention": (None, [sz, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, C.c_int, C.c_int, C.c_int,
+                                       C.c_int, _f32p, _f32p, _f32p, _f32p, sz, _f32p]),
         "orc_paged_attention": (None, [_f32p, _f32p, _f32p, _i32p, C.c_int, C.c_int, C.c_int, C.c_int,
                                        C.c_int, C.c_float, _f32p]),
         "orc_moe_forward": (None, [_f32p, _f32p, _f32p, C.c_int, C.c_int, C.c_int, _u8p, _u8p, _u8p,
@@ -260,6 +262,32 @@ def gqa_attention(q, kpool, vpool, page_table, page_size, seq_len, hq, hkv, hd, 
     out = np.empty(hq * hd, dtype=np.float32)
     lib().orc_gqa_attention(_p(q, _f32p), _p(kpool, _f32p), _p(vpool, _f32p), _p(pt, _i32p), page_size,
                             page_stride, seq_len, hq, hkv, hd, _p(out, _f32p))
+    return out
+
+
+def flash_attention(q, k, v, mask=None, scale=None):
+    """TensorOps.FlashAttentionCpu on [..., s, d] tensors: rank-4 q [B, hq, sq, d] and k / v [B, hkv, sk, d|dv]
+    take the grouped-query form; lower ranks flatten the leading dimensions into the batch."""
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    k = np.ascontiguousarray(k, dtype=np.float32)
+    v = np.ascontiguousarray(v, dtype=np.float32)
+    sq, d = q.shape[-2:]
+    sk, dv = k.shape[-2], v.shape[-1]
+    hq = hkv = 1
+    if q.ndim == 4 and k.ndim == 4:
+        hq, hkv = q.shape[1], k.shape[1]
+    group = hq // hkv
+    batch = int(np.prod(q.shape[:-2], dtype=np.int64))
+    out = np.empty(q.shape[:-1] + (dv,), dtype=np.float32)
+    if mask is not None:
+        mask = np.ascontiguousarray(mask, dtype=np.float32)
+        mb = mask.size // (sq * sk) if sq * sk else 1
+        mp = _p(mask, _f32p)
+    else:
+        mb, mp = 1, None
+    sc = np.float32(1.0) / np.float32(np.sqrt(np.float64(d))) if scale is None else np.float32(scale)
+    lib().orc_flash_attention(batch, sq, sk, d, dv, float(sc), int(group > 1), hq, hkv, group, _p(q, _f32p),
+                              _p(k, _f32p), _p(v, _f32p), mp, mb, _p(out, _f32p))
     return out
 
 

@@ -559,6 +559,62 @@ void orc_gqa_attention(const float* q, const float* kpool, const float* vpool, c
   }
 }
 
+// ---- TensorOps.FlashAttentionCpu (TensorOps.Neural.cs:983-1180; row kernel :670-975) ----
+void orc_flash_attention(size_t batch, int sq, int sk, int d, int dv, float scale, int is_gqa, int hq, int hkv,
+                         int group, const float* q, const float* k, const float* v, const float* mask,
+                         size_t mask_batches, float* out) {
+  const int kBc = 32;
+  const size_t mask_stride = static_cast<size_t>(sq) * sk;
+  auto row = [&](size_t b, int i) {
+    const size_t bkv = is_gqa ? (b / hq) * hkv + (b % hq) / group : b;
+    const float* qi = q + (b * sq + i) * static_cast<size_t>(d);
+    const float* kb = k + bkv * static_cast<size_t>(sk) * d;
+    const float* vb = v + bkv * static_cast<size_t>(sk) * dv;
+    const float* mrow =
+        mask ? mask + (mask_stride > 0 ? (b % mask_batches) * mask_stride + static_cast<size_t>(i) * sk : 0) : nullptr;
+    float* o = out + (b * sq + i) * static_cast<size_t>(dv);
+    std::vector<float> acc(dv, 0.0f);
+    float scores[kBc], weights[kBc];
+    float max_score = -INFINITY, sum_exp = 0.0f;
+    for (int j0 = 0; j0 < sk; j0 += kBc) {
+      const int n = std::min(kBc, sk - j0);
+      for (int t = 0; t < n; ++t) scores[t] = orc_dot_f32(qi, kb + static_cast<size_t>(j0 + t) * d, d) * scale;
+      if (mrow)
+        for (int t = 0; t < n; ++t) scores[t] += mrow[j0 + t];
+      float m_block = -INFINITY;
+      for (int t = 0; t < n; ++t)
+        if (scores[t] > m_block) m_block = scores[t];
+      if (m_block == -INFINITY) continue;
+      float l_block = 0.0f;
+      for (int t = 0; t < n; ++t) {
+        if (scores[t] == -INFINITY) {
+          weights[t] = 0.0f;
+        } else {
+          weights[t] = static_cast<float>(std::exp(static_cast<double>(scores[t] - m_block)));
+          l_block += weights[t];
+        }
+      }
+      const float m_new = std::max(max_score, m_block);
+      const float alpha =
+          max_score == -INFINITY ? 0.0f : static_cast<float>(std::exp(static_cast<double>(max_score - m_new)));
+      const float beta = static_cast<float>(std::exp(static_cast<double>(m_block - m_new)));
+      sum_exp = sum_exp * alpha + l_block * beta;
+      max_score = m_new;
+      if (alpha != 1.0f)
+        for (int c = 0; c < dv; ++c) acc[c] *= alpha;
+      for (int t = 0; t < n; ++t) {
+        const float w = weights[t] * beta;
+        if (w == 0.0f) continue;
+        const float* vt = vb + static_cast<size_t>(j0 + t) * dv;
+        for (int c = 0; c < dv; ++c) acc[c] = std::fmaf(w, vt[c], acc[c]);
+      }
+    }
+    const float inv = sum_exp > 0.0f ? 1.0f / sum_exp : 0.0f;
+    for (int c = 0; c < dv; ++c) o[c] = acc[c] * inv;
+  };
+  pool().parallel_for(batch * sq, 1, 0, [&](size_t r) { row(r / sq, static_cast<int>(r % sq)); });
+}
+
 // ---- TensorOps.PagedAttention fallback (TensorOps.Neural.cs:2418-2473) ----
 void orc_paged_attention(const float* q, const float* kc, const float* vc, const int32_t* block_table, int hq,
                          int hkv, int hd, int block_size, int context_len, float scale, float* out) {

@@ -89,6 +89,16 @@ float orc_dot_f32(const float* a, const float* b, int len);
 void orc_gqa_attention(const float* q, const float* kpool, const float* vpool, const int32_t* page_table,
                        int page_size, size_t page_stride, int seq_len, int hq, int hkv, int hd, float* out);
 
+/* TensorOps.FlashAttentionCpu (ZeroTensor/src/ZeroTensor.Core/TensorOps.Neural.cs:983-1180) with its per-row
+ * FlashAttentionComputeRow (:670-975): q [batch][sq][d], k [kv batch][sk][d], v [kv batch][sk][dv], out
+ * [batch][sq][dv]; kv batch of b = is_gqa ? (b / hq) * hkv + (b % hq) / group : b.  Keys in blocks of 32: scores
+ * dot * scale (+ mask row), a block whose maximum is -inf skipped, weights exp(s - block max) (in double), merged
+ * with alpha = exp(old max - new max), beta = exp(block max - new max); out = acc / sum (zeros for sum 0).  mask
+ * may be null; else mask_batches blocks of [sq][sk] and batch b reads block b % mask_batches. */
+void orc_flash_attention(size_t batch, int sq, int sk, int d, int dv, float scale, int is_gqa, int hq, int hkv,
+                         int group, const float* q, const float* k, const float* v, const float* mask,
+                         size_t mask_batches, float* out);
+
 /* TensorOps.PagedAttention pure-C# fallback (ZeroTensor/src/ZeroTensor.Core/TensorOps.Neural.cs:2418-2473):
  * online softmax; K/V pools [num_blocks][block_size][hkv][hd]; q/out [hq][hd]. */
 void orc_paged_attention(const float* q, const float* kcache, const float* vcache, const int32_t* block_table,

@@ -131,8 +131,14 @@ def test_bridge_gemm_f32_strided(m, n, k, trans):
     assert rel_err(c, ref) <= 1e-5
 
 
-def test_flash_attention_is_not_handled():
-    assert L().zc_flash_attention_f32(1, 1, 1, 8, 8, 1.0, 0, 1, 1, 1, None, None, None, None, None) == -1
+def test_flash_attention_declines_what_it_does_not_run():
+    """zc_flash_attention_f32 answers -1 (the managed FlashAttention runs) for head size 8 and for a mask; null
+    buffers are a bad argument (-2).  The handled forms are in test_flash_attention_gpu.py."""
+    q = np.zeros(8, np.float32)
+    p = q.ctypes.data_as(ctypes.c_void_p)
+    assert L().zc_flash_attention_f32(1, 1, 1, 8, 8, 1.0, 0, 1, 1, 1, p, p, p, None, p) == -1
+    assert L().zc_flash_attention_f32(1, 1, 1, 8, 8, 1.0, 0, 1, 1, 1, p, p, p, p, p) == -1
+    assert L().zc_flash_attention_f32(1, 1, 1, 64, 64, 1.0, 0, 1, 1, 1, None, None, None, None, None) == -2
 
 
 def test_bounded_peer_wait_runs_out_and_reports():

@@ -314,3 +314,42 @@ def test_sampler_restatement_against_numpy():
                     want = i
                     break
             assert tok == want
+
+
+def test_flash_attention_restatement_on_the_reference_inputs():
+    """FlashAttentionCpu_MatchesStandardAttention and _GroupedQueryAttention_MatchesExpanded
+    (ZeroTensor/tests/ZeroTensor.Tests/NeuralOperatorsTests.cs:390-427, 660-723): the restatement agrees with plain
+    softmax attention within the tests' 1e-4, for a masked form too (mask batch broadcast b % mask batches), and a
+    row whose keys are all masked gives zeros."""
+    i = np.arange(8, dtype=np.float32)[:, None]
+    d = np.arange(16, dtype=np.float32)[None, :]
+    q = np.stack([(i + d) * np.float32(0.1), (i - d) * np.float32(0.1)])[None]
+    k = np.stack([(i - d) * np.float32(0.05), (i + d) * np.float32(0.05)])[None]
+    v = np.stack([(i * 2 + d) * np.float32(0.1), (d - i) * np.float32(0.1)])[None]
+
+    def sdpa(q, k, v, mask=None):
+        if k.shape[1] != q.shape[1]:
+            g = q.shape[1] // k.shape[1]
+            k, v = np.repeat(k, g, axis=1), np.repeat(v, g, axis=1)
+        s = q.astype(np.float64) @ np.swapaxes(k.astype(np.float64), -1, -2) / np.sqrt(q.shape[-1])
+        if mask is not None:
+            s = s + mask
+        m = s.max(-1, keepdims=True)
+        p = np.where(np.isneginf(s), 0.0, np.exp(s - np.where(np.isneginf(m), 0.0, m)))
+        den = p.sum(-1, keepdims=True)
+        return np.where(den > 0, p / np.where(den > 0, den, 1.0), 0.0) @ v.astype(np.float64)
+
+    assert np.max(np.abs(O.flash_attention(q, k, v) - sdpa(q, k, v))) < 1e-4
+    h = np.arange(4, dtype=np.float64)[:, None, None]
+    s = np.arange(8, dtype=np.float64)[None, :, None]
+    dd = np.arange(16, dtype=np.float64)[None, None, :]
+    qg = np.sin(h * 10 + s + dd * 0.1).astype(np.float32)[None]
+    hk = np.arange(2, dtype=np.float64)[:, None, None]
+    kg = np.cos(hk * 5 + s * 0.5 + dd * 0.2).astype(np.float32)[None]
+    vg = np.sin(hk * 3 + s * 0.2 + dd * 0.3).astype(np.float32)[None]
+    assert np.max(np.abs(O.flash_attention(qg, kg, vg) - sdpa(qg, kg, vg))) < 1e-4
+    causal = np.triu(np.full((8, 8), -np.inf, np.float32), 1)
+    causal[0, 0] = -np.inf                                     # row 0 attends to nothing
+    got = O.flash_attention(qg, kg, vg, mask=causal)
+    assert np.all(got[:, :, 0] == 0.0)
+    assert np.max(np.abs(got - sdpa(qg, kg, vg, causal))) < 1e-4

@@ -462,10 +462,94 @@ int32_t zc_gemm_f32(size_t m, size_t n, size_t k, float alpha, const float* a, i
   return kOk;
 }
 
-int32_t zc_flash_attention_f32(size_t, size_t, size_t, size_t, size_t, float, int32_t, size_t, size_t, size_t,
-                               const float*, const float*, const float*, const float*, float*) {
-  t_last_error = "zc_flash_attention_f32: prefill attention is not provided by this library";
-  return kNotHandled;
+// TensorOps.FlashAttentionCpu's native dispatch (TensorOps.Neural.cs:1062-1080): q [batch][sq][d], k [kv batch][sk][d],
+// v [kv batch][sk][dv], out [batch][sq][dv], kv batch of b = is_gqa ? (b / hq) * hkv + (b % hq) / group : b.  The ABI
+// carries no mask extent, so the managed code's mask broadcast (batch b reads mask block b % (mask length / sq*sk))
+// cannot be reproduced here: a call with a mask, or with a shape outside the kernel's (dv != d, d not 16 / 32 / 64 /
+// 128, a grouped batch that is not a multiple of hq), returns -1 and the managed FlashAttention runs.
+int32_t zc_flash_attention_f32(size_t batch, size_t sq, size_t sk, size_t d, size_t dv, float scale, int32_t is_gqa,
+                               size_t hq, size_t hkv, size_t group, const float* q, const float* k, const float* v,
+                               const float* mask, float* out) {
+  t_last_error.clear();
+  if (mask) {
+    t_last_error = "zc_flash_attention_f32: an additive mask is not handled (the ABI carries no mask extent)";
+    return kNotHandled;
+  }
+  if (!q || !k || !v || !out) return fail(kBadArgument, "null pointer");
+  if (batch == 0 || sq == 0) return kOk;
+  if (dv != d || (d != 16 && d != 32 && d != 64 && d != 128)) {
+    t_last_error = "zc_flash_attention_f32: head sizes outside 16 / 32 / 64 / 128 (or dv != d) are not handled";
+    return kNotHandled;
+  }
+  size_t seqs = batch, heads = 1, groups = 1, kv_heads = 1;
+  if (is_gqa) {
+    if (hq == 0 || hkv == 0 || group == 0 || hq != hkv * group || batch % hq) {
+      t_last_error = "zc_flash_attention_f32: grouped batch does not split into hq heads";
+      return kNotHandled;
+    }
+    seqs = batch / hq;
+    heads = hq;
+    groups = group;
+    kv_heads = hkv;
+  }
+  if (seqs > 65535 || heads > 65535 || sq > 0x7fffffffu || sk > 0x7fffffffu || sq * d > (1ull << 40)) {
+    t_last_error = "zc_flash_attention_f32: dimensions beyond the launch grid are not handled";
+    return kNotHandled;
+  }
+  const size_t q_floats = batch * sq * d;
+  const size_t kv_floats = seqs * kv_heads * sk * d;
+  if (sk == 0) {  // no keys: every row's sum is 0 and the output is zeros (FlashAttentionComputeRow)
+    std::memset(out, 0, q_floats * sizeof(float));
+    return kOk;
+  }
+  HostCtx* c = nullptr;
+  ZC_RC(host_ctx(&c));
+  void *dq, *dk, *dv_, *dctx, *dpt, *dout;
+  ZC_RC(staging(c, 0, q_floats * 4, &dq));
+  ZC_RC(staging(c, 1, kv_floats * 4, &dk));
+  ZC_RC(staging(c, 2, kv_floats * 4, &dv_));
+  ZC_RC(staging(c, 3, sq * 4, &dctx));
+  ZC_RC(staging(c, 4, 16, &dpt));
+  ZC_RC(staging(c, 5, q_floats * 4, &dout));
+  const std::vector<int32_t> ctx(sq, (int32_t)sk);
+  const int32_t page0 = 0;
+  ZC_CUDA(cudaMemcpyAsync(dq, q, q_floats * 4, cudaMemcpyHostToDevice, c->stream));
+  ZC_CUDA(cudaMemcpyAsync(dk, k, kv_floats * 4, cudaMemcpyHostToDevice, c->stream));
+  ZC_CUDA(cudaMemcpyAsync(dv_, v, kv_floats * 4, cudaMemcpyHostToDevice, c->stream));
+  ZC_CUDA(cudaMemcpyAsync(dctx, ctx.data(), sq * 4, cudaMemcpyHostToDevice, c->stream));
+  ZC_CUDA(cudaMemcpyAsync(dpt, &page0, 4, cudaMemcpyHostToDevice, c->stream));
+  PrefillAttnArgs a{};
+  a.q = (const float*)dq;
+  a.k = dk;
+  a.v = dv_;
+  a.page_table = (const int32_t*)dpt;
+  a.ctx_len = (const int32_t*)dctx;
+  a.out = (float*)dout;
+  a.rows = (int)sq;
+  a.seqs = (int)seqs;
+  a.hq = (int)heads;
+  a.group = (int)groups;
+  a.hd = (int)d;
+  a.page_size = (int)sk;  // one page holds a kv batch's sk keys
+  a.max_pages = 1;
+  a.num_pages = 1;
+  a.page_stride = 0;
+  a.slot_stride = (long long)d;
+  a.head_stride = (long long)(sk * d);
+  a.kv_seq_stride = (long long)(kv_heads * sk * d);
+  a.q_row_stride = (long long)d;
+  a.q_head_stride = (long long)(sq * d);
+  a.q_seq_stride = (long long)(heads * sq * d);
+  a.pt_seq_stride = 0;
+  a.ctx_seq_stride = 0;
+  a.out_row_stride = a.q_row_stride;
+  a.out_head_stride = a.q_head_stride;
+  a.out_seq_stride = a.q_seq_stride;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.kv_half = 0;
+  ZC_RC(prefill_attention(a, c->stream));
+  ZC_CUDA(cudaMemcpyAsync(out, dout, q_floats * 4, cudaMemcpyDeviceToHost, c->stream));
+  return finish(c);
 }
 
 int32_t zc_rmsnorm_f32(size_t n, const float* x, const float* w, float* dst, float eps) {

@@ -37,6 +37,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <limits>
 #include <map>
 #include <string>
 #include <vector>
@@ -117,6 +118,8 @@ struct Engine {
   int timeout_ms = 120000;
   int hq = 0, hkv = 0, ffn = 0, vocab = 0, vocab_chunk = 0;
   int hd = 0, q_dim = 0, kv_dim = 0, qkv_dim = 0;
+  int prefill_row = -1;  // page-table row of the prompt in flight through forward(), else -1
+  int prefill_attn_min_rows = 64;
   int device = 0;
   cudaStream_t stream = nullptr;
   bool own_stream = false;
@@ -238,7 +241,46 @@ int linear_h(Engine* E, const DevW& w, const __half* xh, float* y, int rows, int
                         E->gemm_ws_bytes, E->status, E->stream);
 }
 
+// Rows of one sequence's prompt (E->prefill_row >= 0) at least E->prefill_attn_min_rows (64; the environment
+// variable ZCU_PREFILL_ATTN_MIN_ROWS overrides it at engine creation, 0 = never): the tiled prefill kernel, which
+// reads each key once per 32 query rows; otherwise the decode kernel, which splits each row's context across CTAs.
+int prefill_attn_min_rows_from_env() {
+  const char* env = std::getenv("ZCU_PREFILL_ATTN_MIN_ROWS");
+  if (!env || !*env) return 64;
+  const int v = std::atoi(env);
+  return v <= 0 ? std::numeric_limits<int>::max() : v;
+}
+
 int attention(Engine* E, int layer, int T, const int32_t* ctx, bool half_out) {
+  if (E->prefill_row >= 0 && T >= E->prefill_attn_min_rows) {
+    PrefillAttnArgs p{};
+    p.q = E->qkv;
+    p.k = E->kpool + (size_t)layer * E->layer_pool_elems;
+    p.v = E->vpool + (size_t)layer * E->layer_pool_elems;
+    p.page_table = E->page_table + (size_t)E->prefill_row * E->cfg.max_pages_per_seq;
+    p.ctx_len = ctx;
+    p.out = half_out ? reinterpret_cast<float*>(E->xh) : E->attn;
+    p.rows = T;
+    p.seqs = 1;
+    p.hq = E->hq;
+    p.group = E->hq / E->hkv;
+    p.hd = E->hd;
+    p.page_size = E->cfg.page_size;
+    p.max_pages = E->cfg.max_pages_per_seq;
+    p.num_pages = E->cfg.total_pages;
+    p.page_stride = (long long)E->hkv * E->cfg.page_size * E->hd;
+    p.slot_stride = E->hd;
+    p.head_stride = (long long)E->cfg.page_size * E->hd;
+    p.q_row_stride = E->qkv_dim;
+    p.q_head_stride = E->hd;
+    p.out_row_stride = half_out ? 2 * E->q_dim : E->q_dim;  // fp16 rows are [hi q_dim | lo q_dim]
+    p.out_head_stride = E->hd;
+    p.out_half = half_out ? 1 : 0;
+    p.out_lo_offset = E->q_dim;
+    p.scale_log2 = (1.0f / (float)std::sqrt((double)E->hd)) * 1.4426950408889634f;  // GqaAttention.cs:45
+    p.kv_half = 1;
+    return prefill_attention(p, E->stream);
+  }
   PagedAttnArgs a{};
   a.out_half = half_out ? 1 : 0;
   a.q = E->qkv;
@@ -689,6 +731,7 @@ int32_t zcu_engine_create_tp(const zcu_engine_config* cfg, int32_t tp_size, int3
   }
   Engine* E = new Engine();
   E->cfg = c;
+  E->prefill_attn_min_rows = prefill_attn_min_rows_from_env();
   E->tp_size = tp_size;
   E->tp_rank = tp_rank;
   E->shard = sh;
@@ -952,7 +995,10 @@ int32_t zcu_engine_prefill(void* engine, int32_t seq_id, const int32_t* tokens, 
   E_CUDA(cudaMemcpyAsync(E->pos, pos.data(), n * 4, cudaMemcpyHostToDevice, E->stream));
   E_CUDA(cudaMemcpyAsync(E->rows, rows.data(), n * 4, cudaMemcpyHostToDevice, E->stream));
   E_RC(embed_q8_0(E->tok_emb.qs, E->tok_emb.d, E->tokens, n, E->cfg.vocab, E->cfg.dim, E->x, E->stream));
-  E_RC(forward(E, n, false));
+  E->prefill_row = s->row;
+  const int frc = forward(E, n, false);
+  E->prefill_row = -1;
+  E_RC(frc);
   if (logits) E_RC(logits_to_host(E, 1, logits));
   E_RC(wait(E));
   s->len = std::max(s->len, start_pos + n);  // AppendTokenAt at the last layer (PagedKvCache.cs:311-314)

@@ -90,6 +90,32 @@ size_t paged_attention_workspace_floats(int batch, int hq, int hd, int splits);
 int paged_attention_choose_splits(int batch, int hkv, int max_ctx, int page_size);
 int paged_attention(const PagedAttnArgs& a, cudaStream_t s);
 
+// Attention for many query rows at once (attention_prefill.cu).  Query row r of sequence z, head h reads
+// q[z*q_seq_stride + h*q_head_stride + r*q_row_stride + 0..hd) and attends to key tokens [0, ctx_len[z*ctx_seq_stride
+// + r]) of kv head h / group; key token t lives at page page_table[z*pt_seq_stride + t / page_size], slot
+// t % page_size: element z*kv_seq_stride + kvh*head_stride + page*page_stride + slot*slot_stride + dim of k / v.
+// out[z*out_seq_stride + h*out_head_stride + r*out_row_stride + dim] = softmax(q.k * scale) . v (zeros for a row
+// with no key).  hd 16, 32, 64 or 128; k / v fp16 (kv_half) or fp32.
+struct PrefillAttnArgs {
+  const float* q;
+  const void* k;
+  const void* v;
+  const int32_t* page_table;
+  const int32_t* ctx_len;
+  float* out;
+  int rows, seqs, hq, group, hd;
+  int page_size, max_pages, num_pages;
+  long long page_stride, slot_stride, head_stride, kv_seq_stride;
+  long long q_row_stride, q_head_stride, q_seq_stride;
+  long long pt_seq_stride, ctx_seq_stride;
+  long long out_row_stride, out_head_stride, out_seq_stride;
+  int out_half = 0;            // 1: out is __half hi / lo pairs, lo out_lo_offset elements after hi
+  long long out_lo_offset = 0;
+  float scale_log2;            // scale * log2(e)
+  int kv_half;
+};
+int prefill_attention(const PrefillAttnArgs& a, cudaStream_t s);
+
 // ---- small decode-step operators (ops.cu) ----
 // dst = src, `bytes` a multiple of 4, both 16-byte aligned; either side may be mapped pinned host memory.
 int copy_words(const void* src, void* dst, size_t bytes, cudaStream_t s);
