@@ -250,6 +250,44 @@ ZC_API int32_t zcu_engine_generate_sampled(void* engine, int32_t seq_id, const i
  * is sequence b's i-th sampled token.  timing_ms[0] = device ms of the n_new steps.  Returns n_new or < 0. */
 ZC_API int32_t zcu_engine_generate_batch(void* engine, int32_t batch, const int32_t* seq_ids, const int32_t* tokens,
                                          int32_t n_new, int32_t* out_tokens, float* timing_ms);
+/* Continuous batching (no counterpart in the reference, whose LlmEngine.GenerateStreamAsync, LlmEngine.cs:71-152,
+ * runs each call's prefill and decode loop on its own over the shared PagedKvCache).  Concurrent requests share
+ * every decode step: zcu_engine_submit queues one GenerateStreamAsync call (prompt tokens, SamplingConfig's numeric
+ * fields, MaxTokens = max_new, EosTokenId = eos_token (-1: none) plus StopTokens); zcu_engine_serve_step admits
+ * queued requests first come first served while a page-table row and the pages of prompt + max_new tokens are free
+ * (PrefillPrompt, then the first token is sampled), then runs one ForwardToken + Sample for every running request
+ * as one batched step (one captured graph per batch size) and reports what happened as events.  A request's i-th
+ * token uses the draw zcu_sample_uniform(seed, i), so its tokens do not depend on what it was batched with beyond
+ * the last bits of the logits.  One GPU (tp_size 1).  Sequences of running requests must not be freed or driven
+ * through the other entry points meanwhile. */
+typedef struct zcu_serve_event {
+  int32_t seq_id;
+  int32_t token;     /* the sampled token (ZCU_SERVE_STOP_TOKEN: the stop token, which is not part of the output;
+                        cancelled / refused: -1) */
+  int32_t finished;  /* 1 when the request is over and its sequence freed */
+  int32_t reason;    /* ZCU_SERVE_* */
+} zcu_serve_event;
+enum {
+  ZCU_SERVE_RUNNING = 0,
+  ZCU_SERVE_STOP_TOKEN = 1,  /* eos_token or a stop token was sampled (GenerateStreamAsync breaks without yielding) */
+  ZCU_SERVE_MAX_TOKENS = 2,  /* max_new tokens emitted (this event carries the last one) */
+  ZCU_SERVE_CANCELLED = 3,
+  ZCU_SERVE_REFUSED = 4      /* more than 4096 sampling candidates after Top-K */
+};
+/* Queues a request.  -2 for a live or queued seq_id or bad arguments, -6 when prompt + max_new cannot fit a
+ * sequence (max_pages_per_seq, context length, total pages) or the prompt exceeds max_prefill_tokens, -4 when
+ * tp_size > 1.  Host only: nothing runs until the next serve step. */
+ZC_API int32_t zcu_engine_submit(void* engine, int32_t seq_id, const int32_t* prompt, int32_t n_prompt,
+                                 int32_t max_new, const zcu_sampling_config* cfg, uint64_t seed, int32_t eos_token,
+                                 const int32_t* stop_tokens, int32_t n_stop);
+/* One scheduler iteration (blocking): cancellations, admissions, one batched decode step.  Writes the events to
+ * events (cap >= 2 * max_batch + cancellations of queued requests) and returns their count, or < 0. */
+ZC_API int32_t zcu_engine_serve_step(void* engine, zcu_serve_event* events, int32_t cap);
+/* Cancels a queued or running request; its CANCELLED event comes with the next serve step.  -2 if unknown. */
+ZC_API int32_t zcu_engine_cancel(void* engine, int32_t seq_id);
+/* Running and queued request counts. */
+ZC_API int32_t zcu_engine_serve_counts(void* engine, int32_t* active, int32_t* queued);
+
 /* PagedKvCache.AppendTokenAt (Memory/PagedKvCache.cs:149-183) for tokens [start_pos, start_pos + n) of one layer:
  * k, v are [n][kv_heads][hd] (host or device; kv_dtype 0 = fp32, 1 = fp16).  Appending the last layer sets the
  * sequence length, as the reference counts a token once its last layer is stored.  Like set_weight, the call

@@ -132,6 +132,22 @@ SIGNATURES.update({
 })
 
 
+class ServeEvent(C.Structure):
+    """zcu_serve_event (include/zero_tensor_cuda.h)."""
+
+    _fields_ = [(n, C.c_int32) for n in ("seq_id", "token", "finished", "reason")]
+
+
+SERVE_RUNNING, SERVE_STOP_TOKEN, SERVE_MAX_TOKENS, SERVE_CANCELLED, SERVE_REFUSED = range(5)
+
+SIGNATURES.update({
+    "zcu_engine_submit": (i32, [vp, i32, vp, i32, i32, C.POINTER(SamplingConfig), C.c_uint64, i32, vp, i32]),
+    "zcu_engine_serve_step": (i32, [vp, C.POINTER(ServeEvent), i32]),
+    "zcu_engine_cancel": (i32, [vp, i32]),
+    "zcu_engine_serve_counts": (i32, [vp, C.POINTER(i32), C.POINTER(i32)]),
+})
+
+
 class ZcError(RuntimeError):
     pass
 

@@ -37,6 +37,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <deque>
 #include <limits>
 #include <map>
 #include <string>
@@ -107,6 +108,37 @@ struct Seq {
   int len = 0;                 // tokens whose K/V are complete in every layer
 };
 
+// One request of the continuous batcher: GenerateStreamAsync's per-call state (LlmEngine.cs:71-152).
+struct ServeReq {
+  int seq_id = 0;
+  std::vector<int32_t> prompt;
+  int max_new = 0;
+  SampleConfig sc{};
+  uint64_t seed = 0;
+  int eos = -1;
+  std::vector<int32_t> stop;
+  int generated = 0;   // tokens emitted
+  int pending = -1;    // last sampled token, emitted and not yet run through the model
+  int pos = 0;         // its position
+  bool cancel = false;
+};
+
+// Continuous batching state: requests wait in `queue` (FIFO) until a page-table row and the pages for prompt +
+// max_new tokens are free, then are prefilled and join every following decode step until they finish.
+struct Serve {
+  std::deque<ServeReq> queue;
+  std::vector<ServeReq> active;
+  std::vector<int> cancelled_queued;  // seq ids removed from the queue, reported at the next step
+  int32_t* past = nullptr;            // device [max_batch][past_cap]: each page-table row's token history
+  int32_t* past_len = nullptr;        // device [max_batch]
+  int past_cap = 0;
+  SampleConfig* cfg_dev = nullptr;    // device [max_batch]: the step's per-row sampling configurations
+  float* u_dev = nullptr;             // device [max_batch]: the step's per-row draws
+  int32_t* out_dev = nullptr;         // device [max_batch]: sampled tokens
+  void* host = nullptr;               // pinned: tokens, pos, rows, out [max_batch] int32; u [max_batch]; cfg [max_batch]
+  std::map<int, cudaGraphExec_t> graphs;  // decode step (embed, forward, sample, history) by batch size
+};
+
 struct Engine {
   zcu_engine_config cfg{};
   // tensor-parallel shard; hq / hkv / ffn / vocab are this rank's (the whole model's when tp_size == 1)
@@ -175,6 +207,7 @@ struct Engine {
   std::string fused_why;
   std::map<int, cudaGraphExec_t> step_graphs;   // decode step graphs (B = 1 generation)
   std::map<int, cudaGraphExec_t> batch_graphs;  // batched generation step graphs, by batch size
+  Serve* serve = nullptr;                       // continuous batching (zcu_engine_submit / serve_step)
   std::string err;
 };
 
@@ -691,6 +724,98 @@ int capture_batch_step(Engine* E, int B, cudaGraphExec_t* out) {
   return kOk;
 }
 
+// Continuous batching: one decode step of B running requests, rows [0, B) of E->tokens / pos / rows (uploaded
+// before each launch), each sampled with its own configuration and draw and its token appended to its history.
+int capture_serve_step(Engine* E, int B, cudaGraphExec_t* out) {
+  Serve* S = E->serve;
+  cudaGraph_t g;
+  E_CUDA(cudaStreamBeginCapture(E->stream, cudaStreamCaptureModeThreadLocal));
+  int rc = embed_q8_0(E->tok_emb.qs, E->tok_emb.d, E->tokens, B, E->cfg.vocab, E->cfg.dim, E->x, E->stream);
+  if (rc == kOk) rc = forward(E, B, B > 1);
+  if (rc == kOk)
+    rc = sample_rows_each(E->logits, B, E->vocab, S->past, S->past_len, S->past_cap, E->rows, S->cfg_dev, S->u_dev,
+                          S->out_dev, E->stream);
+  if (rc == kOk) rc = append_history(S->out_dev, E->rows, B, S->past, S->past_len, S->past_cap, E->stream);
+  cudaError_t ce = cudaStreamEndCapture(E->stream, &g);
+  if (rc != kOk) return rc;
+  E_CUDA(ce);
+  ce = cudaGraphInstantiate(out, g, 0);
+  cudaGraphDestroy(g);
+  E_CUDA(ce);
+  return kOk;
+}
+
+int serve_init(Engine* E) {
+  if (E->serve) return kOk;
+  const int B = E->cfg.max_batch;
+  Serve* S = new Serve();
+  S->past_cap = E->cfg.max_pages_per_seq * E->cfg.page_size;
+  int rc = dalloc(E, &S->past, (size_t)B * S->past_cap);
+  if (rc == kOk) rc = dalloc(E, &S->past_len, B);
+  if (rc == kOk) rc = dalloc(E, &S->cfg_dev, B);
+  if (rc == kOk) rc = dalloc(E, &S->u_dev, B);
+  if (rc == kOk) rc = dalloc(E, &S->out_dev, B);
+  if (rc == kOk && cudaMallocHost(&S->host, (size_t)B * (5 * 4 + sizeof(SampleConfig))) != cudaSuccess) {
+    cudaGetLastError();
+    S->host = nullptr;
+    E->err = "pinned host allocation failed";
+    rc = kOutOfMemory;
+  }
+  if (rc != kOk) {
+    delete S;
+    return rc;
+  }
+  E->serve = S;
+  return kOk;
+}
+
+// The draw of a request's i-th token: the one sampled generation uses (zcu_sample_uniform).
+inline float serve_uniform(uint64_t seed, uint64_t i) { return splitmix_uniform(seed + i); }
+
+// Pinned host views: [tokens | pos | rows | out] int32 [max_batch] each, u float [max_batch], cfg [max_batch].
+struct ServeHost {
+  int32_t *tokens, *pos, *rows, *out;
+  float* u;
+  SampleConfig* cfg;
+};
+ServeHost serve_host(Engine* E) {
+  const int B = E->cfg.max_batch;
+  char* h = static_cast<char*>(E->serve->host);
+  ServeHost v;
+  v.tokens = reinterpret_cast<int32_t*>(h);
+  v.pos = v.tokens + B;
+  v.rows = v.pos + B;
+  v.out = v.rows + B;
+  v.u = reinterpret_cast<float*>(v.out + B);
+  v.cfg = reinterpret_cast<SampleConfig*>(v.u + B);
+  return v;
+}
+
+// A token sampled for request r: decides whether it ends the request (GenerateStreamAsync's loop: a stop token
+// ends it unemitted; MaxTokens ends it after the token) and records the event.
+void serve_take(ServeReq& r, int tok, std::vector<zcu_serve_event>* ev, bool* done) {
+  zcu_serve_event e{r.seq_id, tok, 0, ZCU_SERVE_RUNNING};
+  *done = false;
+  if (tok < 0) {
+    e.finished = 1;
+    e.reason = ZCU_SERVE_REFUSED;
+    *done = true;
+  } else if (tok == r.eos || std::find(r.stop.begin(), r.stop.end(), tok) != r.stop.end()) {
+    e.finished = 1;
+    e.reason = ZCU_SERVE_STOP_TOKEN;
+    *done = true;
+  } else {
+    ++r.generated;
+    r.pending = tok;
+    if (r.generated >= r.max_new) {
+      e.finished = 1;
+      e.reason = ZCU_SERVE_MAX_TOKENS;
+      *done = true;
+    }
+  }
+  ev->push_back(e);
+}
+
 }  // namespace
 
 }  // namespace zc
@@ -906,6 +1031,11 @@ int32_t zcu_engine_destroy(void* engine) {
   // graphs that hold collectives go before the communicator
   for (auto& kv : E->step_graphs) cudaGraphExecDestroy(kv.second);
   for (auto& kv : E->batch_graphs) cudaGraphExecDestroy(kv.second);
+  if (E->serve) {
+    for (auto& kv : E->serve->graphs) cudaGraphExecDestroy(kv.second);
+    if (E->serve->host) cudaFreeHost(E->serve->host);
+    delete E->serve;
+  }
   zc::arp_destroy(E->arp);
   zc::comm_destroy(E->comm);
   for (void* p : E->allocs) cudaFree(p);
@@ -1354,6 +1484,202 @@ int32_t zcu_engine_generate_batch(void* engine, int32_t batch, const int32_t* se
     return kCudaError;
   }
   return n_new;
+}
+
+// ---- continuous batching ----
+
+int32_t zcu_engine_submit(void* engine, int32_t seq_id, const int32_t* prompt, int32_t n_prompt, int32_t max_new,
+                          const zcu_sampling_config* cfg, uint64_t seed, int32_t eos_token, const int32_t* stop_tokens,
+                          int32_t n_stop) {
+  using namespace zc;
+  Engine* E = static_cast<Engine*>(engine);
+  if (!E || !prompt || !cfg || n_prompt <= 0 || max_new < 0 || n_stop < 0 || (n_stop > 0 && !stop_tokens) ||
+      cfg->top_k < 0)
+    return kBadArgument;
+  E->err.clear();
+  if (E->tp_size != 1) {
+    E->err = "continuous batching runs on one GPU (each tensor-parallel rank holds a vocabulary slice)";
+    return kUnsupported;
+  }
+  if (n_prompt > E->max_rows) {
+    E->err = "prompt longer than max_prefill_tokens";
+    return kTooLarge;
+  }
+  const long long need = (long long)n_prompt + max_new;
+  const int P = E->cfg.page_size;
+  if (need > (long long)E->cfg.max_pages_per_seq * P || need > E->max_pos ||
+      (need + P - 1) / P > E->cfg.total_pages) {
+    E->err = "prompt + max_new exceed the sequence capacity (pages, max_pages_per_seq or context length)";
+    return kTooLarge;
+  }
+  if (E->seqs.count(seq_id)) {
+    E->err = "sequence id already live";
+    return kBadArgument;
+  }
+  E_RC(serve_init(E));
+  Serve* S = E->serve;
+  for (const ServeReq& r : S->queue)
+    if (r.seq_id == seq_id) {
+      E->err = "sequence id already submitted";
+      return kBadArgument;
+    }
+  ServeReq r;
+  r.seq_id = seq_id;
+  r.prompt.assign(prompt, prompt + n_prompt);
+  r.max_new = max_new;
+  r.sc = SampleConfig{cfg->temperature, cfg->top_p, cfg->min_p, cfg->top_k, cfg->repetition_penalty};
+  r.seed = seed;
+  r.eos = eos_token;
+  if (n_stop > 0) r.stop.assign(stop_tokens, stop_tokens + n_stop);
+  S->queue.push_back(std::move(r));
+  return kOk;
+}
+
+int32_t zcu_engine_cancel(void* engine, int32_t seq_id) {
+  using namespace zc;
+  Engine* E = static_cast<Engine*>(engine);
+  if (!E || !E->serve) return kBadArgument;
+  Serve* S = E->serve;
+  for (auto it = S->queue.begin(); it != S->queue.end(); ++it)
+    if (it->seq_id == seq_id) {
+      S->queue.erase(it);
+      S->cancelled_queued.push_back(seq_id);
+      return kOk;
+    }
+  for (ServeReq& r : S->active)
+    if (r.seq_id == seq_id) {
+      r.cancel = true;
+      return kOk;
+    }
+  return kBadArgument;
+}
+
+int32_t zcu_engine_serve_counts(void* engine, int32_t* active, int32_t* queued) {
+  Engine* E = static_cast<Engine*>(engine);
+  if (!E) return zc::kBadArgument;
+  if (active) *active = E->serve ? (int32_t)E->serve->active.size() : 0;
+  if (queued) *queued = E->serve ? (int32_t)E->serve->queue.size() : 0;
+  return zc::kOk;
+}
+
+int32_t zcu_engine_serve_step(void* engine, zcu_serve_event* events, int32_t cap) {
+  using namespace zc;
+  Engine* E = static_cast<Engine*>(engine);
+  if (!E || !events) return kBadArgument;
+  E->err.clear();
+  if (!E->serve) return 0;
+  Serve* S = E->serve;
+  if (cap < 2 * E->cfg.max_batch + (int)S->cancelled_queued.size()) {
+    E->err = "event capacity below 2 * max_batch + pending cancellations";
+    return kBadArgument;
+  }
+  std::vector<zcu_serve_event> ev;
+  for (int id : S->cancelled_queued) ev.push_back({id, -1, 1, ZCU_SERVE_CANCELLED});
+  S->cancelled_queued.clear();
+  auto finish = [&](size_t i) {
+    zcu_engine_free_sequence(engine, S->active[i].seq_id);
+    S->active.erase(S->active.begin() + (long)i);
+  };
+  for (size_t i = 0; i < S->active.size();) {
+    if (S->active[i].cancel) {
+      ev.push_back({S->active[i].seq_id, -1, 1, ZCU_SERVE_CANCELLED});
+      finish(i);
+    } else {
+      ++i;
+    }
+  }
+  const ServeHost h = serve_host(E);
+  const int P = E->cfg.page_size;
+  // 1. admission, first come first served: a page-table row and the pages of prompt + max_new tokens
+  while (!S->queue.empty() && (int)S->active.size() < E->cfg.max_batch && !E->free_rows.empty()) {
+    ServeReq& q = S->queue.front();
+    const int n = (int)q.prompt.size();
+    const int pages = (n + q.max_new + P - 1) / P;
+    if ((int)E->free_stack.size() < pages) break;
+    ServeReq r = std::move(q);
+    S->queue.pop_front();
+    Seq* sq = nullptr;
+    E_RC(get_seq(E, r.seq_id, &sq));
+    E_RC(ensure_pages(E, *sq, n + r.max_new));
+    const int row = sq->row;
+    E_RC(zcu_engine_prefill(engine, r.seq_id, r.prompt.data(), n, 0, nullptr));  // PrefillPrompt
+    if (r.max_new == 0) {  // the reference's loop does not run: nothing is sampled
+      ev.push_back({r.seq_id, -1, 1, ZCU_SERVE_MAX_TOKENS});
+      zcu_engine_free_sequence(engine, r.seq_id);
+      continue;
+    }
+    // history = the prompt; sample the first token from the prefill's logits
+    h.u[0] = serve_uniform(r.seed, 0);
+    h.cfg[0] = r.sc;
+    const int32_t nn = n;
+    E_CUDA(cudaMemcpyAsync(S->past + (size_t)row * S->past_cap, r.prompt.data(), (size_t)n * 4,
+                           cudaMemcpyHostToDevice, E->stream));
+    E_CUDA(cudaMemcpyAsync(S->past_len + row, &nn, 4, cudaMemcpyHostToDevice, E->stream));
+    E_CUDA(cudaMemcpyAsync(S->u_dev, h.u, 4, cudaMemcpyHostToDevice, E->stream));
+    E_CUDA(cudaMemcpyAsync(S->cfg_dev, h.cfg, sizeof(SampleConfig), cudaMemcpyHostToDevice, E->stream));
+    E_RC(sample_rows_each(E->logits, 1, E->vocab, S->past, S->past_len, S->past_cap, E->rows, S->cfg_dev, S->u_dev,
+                          S->out_dev, E->stream));
+    E_RC(append_history(S->out_dev, E->rows, 1, S->past, S->past_len, S->past_cap, E->stream));
+    E_CUDA(cudaMemcpyAsync(h.out, S->out_dev, 4, cudaMemcpyDeviceToHost, E->stream));
+    E_RC(wait(E));
+    r.pos = n;
+    bool done = false;
+    serve_take(r, h.out[0], &ev, &done);
+    if (done) {
+      zcu_engine_free_sequence(engine, r.seq_id);
+      continue;
+    }
+    S->active.push_back(std::move(r));
+  }
+  // 2. one decode step of every running request: ForwardToken(pending, pos), then sample
+  const int B = (int)S->active.size();
+  if (B > 0) {
+    for (int b = 0; b < B; ++b) {
+      ServeReq& r = S->active[b];
+      h.tokens[b] = r.pending;
+      h.pos[b] = r.pos;
+      h.rows[b] = E->seqs.at(r.seq_id).row;
+      h.u[b] = serve_uniform(r.seed, (uint64_t)r.generated);
+      h.cfg[b] = r.sc;
+    }
+    auto it = S->graphs.find(B);
+    if (it == S->graphs.end()) {
+      cudaGraphExec_t ge;
+      E_RC(capture_serve_step(E, B, &ge));
+      it = S->graphs.emplace(B, ge).first;
+    }
+    E_CUDA(cudaMemcpyAsync(E->tokens, h.tokens, (size_t)B * 4, cudaMemcpyHostToDevice, E->stream));
+    E_CUDA(cudaMemcpyAsync(E->pos, h.pos, (size_t)B * 4, cudaMemcpyHostToDevice, E->stream));
+    E_CUDA(cudaMemcpyAsync(E->rows, h.rows, (size_t)B * 4, cudaMemcpyHostToDevice, E->stream));
+    E_CUDA(cudaMemcpyAsync(S->u_dev, h.u, (size_t)B * 4, cudaMemcpyHostToDevice, E->stream));
+    E_CUDA(cudaMemcpyAsync(S->cfg_dev, h.cfg, (size_t)B * sizeof(SampleConfig), cudaMemcpyHostToDevice, E->stream));
+    E_CUDA(cudaGraphLaunch(it->second, E->stream));
+    E_CUDA(cudaMemcpyAsync(h.out, S->out_dev, (size_t)B * 4, cudaMemcpyDeviceToHost, E->stream));
+    E_RC(wait(E));
+    int st = 0;
+    E_CUDA(cudaMemcpy(&st, E->status, 4, cudaMemcpyDeviceToHost));
+    if (st) {
+      E->err = "a kernel's bounded wait expired (status " + std::to_string(st) + ")";
+      return kCudaError;
+    }
+    std::vector<char> done(B, 0);
+    for (int b = 0; b < B; ++b) {
+      ServeReq& r = S->active[b];
+      E->seqs.at(r.seq_id).len = r.pos + 1;  // the forwarded token's K/V are in every layer
+      r.pos += 1;
+      bool d = false;
+      serve_take(r, h.out[b], &ev, &d);
+      done[b] = d;
+    }
+    for (int b = B - 1; b >= 0; --b)
+      if (done[b]) finish((size_t)b);
+  }
+  if ((int)ev.size() > cap) {  // cannot happen with cap >= 2 * max_batch + cancellations
+    E->err = "event buffer overflow";
+    return kTooLarge;
+  }
+  std::copy(ev.begin(), ev.end(), events);
+  return (int32_t)ev.size();
 }
 
 }  // extern "C"

@@ -177,6 +177,14 @@ struct SampleConfig {
 int sample_rows(float* logits, int rows, int vocab, const int32_t* past, const int32_t* past_len, int past_cap,
                 const SampleConfig& cfg, const float* uniforms, int32_t* out, int32_t* cand_idx, float* cand_p,
                 int32_t* n_cand, int cand_cap, cudaStream_t s);
+// The same with a configuration and a draw per row (row_cfg[r], uniforms[r]) and row r's history in row
+// past_rows[r] of past / past_len (null: row r).  Candidates are not reported.
+int sample_rows_each(float* logits, int rows, int vocab, const int32_t* past, const int32_t* past_len, int past_cap,
+                     const int32_t* past_rows, const SampleConfig* row_cfg, const float* uniforms, int32_t* out,
+                     cudaStream_t s);
+// Appends tok[r] to history row past_rows[r] (past [.][past_cap], past_len [.]) while it has room.
+int append_history(const int32_t* tok, const int32_t* past_rows, int rows, int32_t* past, int32_t* past_len,
+                   int past_cap, cudaStream_t s);
 // u[r] = splitmix_uniform(seed + *counter + r) for r < rows (<= 1024); *counter += rows.
 int draw_uniforms(uint64_t seed, int32_t* counter, int rows, float* u, cudaStream_t s);
 

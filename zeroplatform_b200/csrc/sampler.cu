@@ -54,11 +54,16 @@ __device__ __forceinline__ T block_reduce(T v, T* red, Op op) {
 __global__ void __launch_bounds__(SAMPLE_THREADS) sample_kernel(float* __restrict__ logits, int vocab,
                                                                   const int32_t* __restrict__ past,
                                                                   const int32_t* __restrict__ past_len, int past_cap,
-                                                                  SampleConfig cfg, const float* __restrict__ uniforms,
+                                                                  const int32_t* __restrict__ past_rows,
+                                                                  SampleConfig cfg0,
+                                                                  const SampleConfig* __restrict__ row_cfg,
+                                                                  const float* __restrict__ uniforms,
                                                                   int32_t* __restrict__ out, int32_t* cand_idx,
                                                                   float* cand_p, int32_t* n_cand, int cand_cap) {
   pdl_trigger();
   pdl_wait();
+  const SampleConfig cfg = row_cfg ? row_cfg[blockIdx.x] : cfg0;
+  const int prow = past_rows ? past_rows[blockIdx.x] : (int)blockIdx.x;  // this row's history
   __shared__ float redf[32];
   __shared__ int redi[32];
   __shared__ unsigned hist[256];
@@ -72,8 +77,8 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) sample_kernel(float* __restric
   float* lg = logits + (size_t)row * vocab;
   // 1. repetition penalty (thread 0, the reference's order)
   if (cfg.penalty > 1.0f && past && past_len && tid == 0) {
-    const int n = min(past_len[row], past_cap);
-    const int32_t* pt = past + (size_t)row * past_cap;
+    const int n = min(past_len[prow], past_cap);
+    const int32_t* pt = past + (size_t)prow * past_cap;
     for (int i = 0; i < n; ++i) {
       const unsigned t = (unsigned)pt[i];
       if (t < (unsigned)vocab) lg[t] = lg[t] > 0 ? lg[t] / cfg.penalty : lg[t] * cfg.penalty;
@@ -319,7 +324,45 @@ int sample_rows(float* logits, int rows, int vocab, const int32_t* past, const i
   if (!greedy && !uniforms) return kBadArgument;
   if (cfg.top_k < 0) return kBadArgument;
   return launch_pdl(sample_kernel, dim3(rows), dim3(SAMPLE_THREADS), 0, s, logits, vocab, past, past_len, past_cap,
-                    cfg, uniforms, out, cand_idx, cand_p, n_cand, cand_cap) == cudaSuccess
+                    (const int32_t*)nullptr, cfg, (const SampleConfig*)nullptr, uniforms, out, cand_idx, cand_p,
+                    n_cand, cand_cap) == cudaSuccess
+             ? kOk
+             : kCudaError;
+}
+
+int sample_rows_each(float* logits, int rows, int vocab, const int32_t* past, const int32_t* past_len, int past_cap,
+                     const int32_t* past_rows, const SampleConfig* row_cfg, const float* uniforms, int32_t* out,
+                     cudaStream_t s) {
+  if (!logits || !out || !row_cfg || !uniforms || rows <= 0 || vocab <= 0) return kBadArgument;
+  return launch_pdl(sample_kernel, dim3(rows), dim3(SAMPLE_THREADS), 0, s, logits, vocab, past, past_len, past_cap,
+                    past_rows, SampleConfig{}, row_cfg, uniforms, out, (int32_t*)nullptr, (float*)nullptr,
+                    (int32_t*)nullptr, 0) == cudaSuccess
+             ? kOk
+             : kCudaError;
+}
+
+namespace {
+// past[past_rows[r]][past_len[past_rows[r]]++] = tok[r] while the row has room (past_cap).
+__global__ void append_history_kernel(const int32_t* tok, const int32_t* past_rows, int rows, int32_t* past,
+                                      int32_t* past_len, int past_cap) {
+  pdl_trigger();
+  pdl_wait();
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  const int p = past_rows[r];
+  const int n = past_len[p];
+  if (n < past_cap) {
+    past[(size_t)p * past_cap + n] = tok[r];
+    past_len[p] = n + 1;
+  }
+}
+}  // namespace
+
+int append_history(const int32_t* tok, const int32_t* past_rows, int rows, int32_t* past, int32_t* past_len,
+                   int past_cap, cudaStream_t s) {
+  if (!tok || !past_rows || !past || !past_len || rows <= 0 || past_cap <= 0) return kBadArgument;
+  return launch_pdl(append_history_kernel, dim3((rows + 127) / 128), dim3(128), 0, s, tok, past_rows, rows, past,
+                    past_len, past_cap) == cudaSuccess
              ? kOk
              : kCudaError;
 }

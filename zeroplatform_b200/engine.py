@@ -151,6 +151,36 @@ class LlmEngine:
                                                           seed, eos_token, out.ctypes.data, timing), "generate_sampled")
         return out[:n].copy(), float(timing[0]), float(timing[1])
 
+    # ---- continuous batching (zcu_engine_submit / zcu_engine_serve_step) ----
+
+    def submit(self, seq_id: int, prompt, max_new: int, temperature=0.7, top_p=0.9, min_p=0.0, top_k=40,
+               repetition_penalty=1.1, seed=0, eos_token: int = -1, stop_tokens=()):
+        """Queues one GenerateStreamAsync request (SamplingConfig's fields; MaxTokens = max_new); it runs in the
+        following serve_step calls together with every other running request."""
+        from ._lib import SamplingConfig
+        cfg = SamplingConfig(temperature, top_p, min_p, top_k, repetition_penalty)
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        st = np.ascontiguousarray(sorted(set(int(t) for t in stop_tokens)), dtype=np.int32)
+        self._check(lib().zcu_engine_submit(self._h, seq_id, p.ctypes.data, p.size, max_new, C.byref(cfg), seed,
+                                            eos_token, st.ctypes.data if st.size else None, st.size), "submit")
+
+    def serve_step(self):
+        """One scheduler iteration; returns [(seq_id, token, finished, reason)] (reason: _lib.SERVE_*)."""
+        from ._lib import ServeEvent
+        if not hasattr(self, "_events"):
+            self._events = (ServeEvent * (2 * self.cfg.max_batch + 4096))()
+        n = self._check(lib().zcu_engine_serve_step(self._h, self._events, len(self._events)), "serve_step")
+        return [(e.seq_id, e.token, e.finished, e.reason) for e in self._events[:n]]
+
+    def cancel(self, seq_id: int):
+        self._check(lib().zcu_engine_cancel(self._h, seq_id), "cancel")
+
+    def serve_counts(self):
+        """(running, queued) requests."""
+        a, q = C.c_int32(), C.c_int32()
+        lib().zcu_engine_serve_counts(self._h, C.byref(a), C.byref(q))
+        return a.value, q.value
+
     def step_kind(self):
         """(1, "") when generation runs one cooperative kernel per token, (0, reason) for the per-operator graph,
         (-1, "") before the first generate call."""
