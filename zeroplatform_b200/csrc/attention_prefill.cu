@@ -15,12 +15,21 @@
 // token t sits at page page_table[t / page_size], slot t % page_size, so the same kernel reads the engine's fp16
 // page pools and a dense [kv batch][sk][d] fp32 tensor (one page of sk slots).  Tokens at or past a row's context
 // length, and pages outside [0, num_pages), contribute nothing.  fp32 arithmetic throughout.
+//
+// Tensor-core form (fp16 K/V, head size 64 or 128: the engine's pools).  One CTA of 4 warps per 64 query rows of a
+// head, each warp 16 rows, keys staged 64 at a time by cp.async into a double-buffered shared-memory ring.  Scores
+// S = q . K come from mma.sync m16n8k16 with q carried as an fp16 pair (q_hi = fp16(q), q_lo = fp16(q - q_hi)) and
+// K exact in fp16, so S = q_hi K + q_lo K is q . K to ~2^-22; the online softmax runs on the S fragments in fp32
+// (exp2 domain), and P . V again takes P as an fp16 pair against exact fp16 V.  Every product is exact and
+// accumulates in fp32, so the result matches the fp32 form to summation order.  Warps whose rows have no key in a
+// block skip its arithmetic; tiles are issued longest first.
 
 #include <cuda_fp16.h>
 #include <math.h>
 
 #include "common.cuh"
 #include "kernels.h"
+#include "sync.cuh"
 
 namespace zc {
 
@@ -172,6 +181,263 @@ __global__ void __launch_bounds__(PF_THREADS) prefill_attn_kernel(PrefillAttnArg
   }
 }
 
+// ---- tensor-core form ----
+constexpr int MQ = 64;   // query rows per CTA (16 per warp)
+constexpr int MKEYS = 64;  // keys per stage
+
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// (x, y) -> fp16 pair (low half = x) and the pair of residuals x - fp16(x), y - fp16(y)
+__device__ __forceinline__ void split_pair(float x, float y, uint32_t& hi, uint32_t& lo) {
+  const __half2 h = __floats2half2_rn(x, y);
+  const float2 f = __half22float2(h);
+  const __half2 l = __floats2half2_rn(x - f.x, y - f.y);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(128) prefill_attn_mma_kernel(PrefillAttnArgs a) {
+  constexpr int KSTR = HD + 8;   // halves per staged key row (16-byte pad: ldmatrix rows in distinct banks)
+  constexpr int KC = HD / 16;    // 16-wide k-chunks of q . K
+  constexpr int DN = HD / 8;     // 8-wide dim tiles of the output
+  constexpr int STAGE = MKEYS * KSTR;  // halves per stage of K (and of V)
+  constexpr int CHUNKS = MKEYS * HD / 8;  // 16-byte pieces per stage of K (and of V)
+  extern __shared__ __align__(128) __half pf_smem[];
+  __half* sK = pf_smem;              // [2][MKEYS][KSTR]
+  __half* sV = pf_smem + 2 * STAGE;  // [2][MKEYS][KSTR]
+  __shared__ int s_wmax[4];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int tile = gridDim.x - 1 - blockIdx.x;  // longest (latest) tiles first
+  const int h = blockIdx.y, z = blockIdx.z;
+  const int rw = tile * MQ + warp * 16;  // the warp's first row
+  const int ra = rw + g, rb = rw + g + 8;
+  const int kvh = h / a.group;
+  const int cap = a.max_pages * a.page_size;
+  const int ctx_a = ra < a.rows ? min(max(a.ctx_len[(size_t)z * a.ctx_seq_stride + ra], 0), cap) : 0;
+  const int ctx_b = rb < a.rows ? min(max(a.ctx_len[(size_t)z * a.ctx_seq_stride + rb], 0), cap) : 0;
+  int wmax = max(ctx_a, ctx_b);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) wmax = max(wmax, __shfl_xor_sync(0xffffffffu, wmax, o));
+  if (lane == 0) s_wmax[warp] = wmax;
+  // q rows as fp16 pairs in A-fragment order (pre-scaled into the exp2 domain)
+  uint32_t qh[KC][4], ql[KC][4];
+  {
+    const float* qz = a.q + (size_t)z * a.q_seq_stride + (size_t)h * a.q_head_stride;
+    const float* qa = qz + (size_t)ra * a.q_row_stride;
+    const float* qb = qz + (size_t)rb * a.q_row_stride;
+#pragma unroll
+    for (int kc = 0; kc < KC; ++kc) {
+      const int d0 = 16 * kc + 2 * t4;
+      float2 v[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      if (ra < a.rows) {
+        v[0] = *reinterpret_cast<const float2*>(qa + d0);
+        v[2] = *reinterpret_cast<const float2*>(qa + d0 + 8);
+      }
+      if (rb < a.rows) {
+        v[1] = *reinterpret_cast<const float2*>(qb + d0);
+        v[3] = *reinterpret_cast<const float2*>(qb + d0 + 8);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) split_pair(v[i].x * a.scale_log2, v[i].y * a.scale_log2, qh[kc][i], ql[kc][i]);
+    }
+  }
+  __syncthreads();
+  const int max_ctx = max(max(s_wmax[0], s_wmax[1]), max(s_wmax[2], s_wmax[3]));
+  const int nb = (max_ctx + MKEYS - 1) / MKEYS;
+  const __half* kz = reinterpret_cast<const __half*>(a.k) + (size_t)z * a.kv_seq_stride + (size_t)kvh * a.head_stride;
+  const __half* vz = reinterpret_cast<const __half*>(a.v) + (size_t)z * a.kv_seq_stride + (size_t)kvh * a.head_stride;
+  const int32_t* pt = a.page_table + (size_t)z * a.pt_seq_stride;
+  // stage b of K and V into ring slot b & 1: token 64 b + key, 16-byte piece `part` of its row; tokens at or past
+  // the CTA's longest context, or on pages outside [0, num_pages), arrive as zeros
+  auto load_stage = [&](int b) {
+    const int slot = b & 1;
+#pragma unroll
+    for (int c = tid; c < CHUNKS; c += 128) {
+      const int key = c / (HD / 8), part = c % (HD / 8);
+      const int tok = b * MKEYS + key;
+      const int page = tok < max_ctx ? pt[tok / a.page_size] : -1;
+      const bool ok = page >= 0 && page < a.num_pages;
+      const size_t off =
+          (size_t)(ok ? page : 0) * a.page_stride + (size_t)(ok ? tok % a.page_size : 0) * a.slot_stride + 8 * part;
+      const int so = slot * STAGE + key * KSTR + 8 * part;
+      cp_async16(smem_u32(sK + so), kz + off, ok);
+      cp_async16(smem_u32(sV + so), vz + off, ok);
+    }
+  };
+  float o[DN][4];
+#pragma unroll
+  for (int i = 0; i < DN; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
+  if (nb > 0) load_stage(0);
+  cp_async_commit();
+  for (int b = 0; b < nb; ++b) {
+    if (b + 1 < nb) load_stage(b + 1);  // its slot was last read in block b - 1 (released by that block's barrier)
+    cp_async_commit();
+    cp_async_wait<1>();  // stage b has landed (this thread's copies); the barrier makes it every thread's
+    __syncthreads();
+    if (wmax > b * MKEYS) {  // the warp has at least one key in this block
+      const __half* kb = sK + (b & 1) * STAGE;
+      const __half* vb = sV + (b & 1) * STAGE;
+      float sc[8][4];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+#pragma unroll
+        for (int kc = 0; kc < KC; kc += 2) {
+          uint32_t b0, b1, b2, b3;  // K rows 8 j .. 8 j + 7: dims 16 kc .. 16 kc + 31 as two k-chunks
+          ldsm_x4(smem_u32(kb + (8 * j + (lane & 7)) * KSTR + 16 * kc + 8 * (lane >> 3)), b0, b1, b2, b3);
+          mma16816(sc[j], qh[kc], b0, b1);
+          mma16816(sc[j], ql[kc], b0, b1);
+          mma16816(sc[j], qh[kc + 1], b2, b3);
+          mma16816(sc[j], ql[kc + 1], b2, b3);
+        }
+      }
+      // mask, block maxima of rows a (values 0, 1) and b (values 2, 3) over the quad's 64 columns
+      float mxa = -INFINITY, mxb = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int k0 = b * MKEYS + 8 * j + 2 * t4;
+        if (k0 >= ctx_a) sc[j][0] = -INFINITY;
+        if (k0 + 1 >= ctx_a) sc[j][1] = -INFINITY;
+        if (k0 >= ctx_b) sc[j][2] = -INFINITY;
+        if (k0 + 1 >= ctx_b) sc[j][3] = -INFINITY;
+        mxa = fmaxf(mxa, fmaxf(sc[j][0], sc[j][1]));
+        mxb = fmaxf(mxb, fmaxf(sc[j][2], sc[j][3]));
+      }
+#pragma unroll
+      for (int off = 1; off <= 2; off <<= 1) {
+        mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, off));
+        mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, off));
+      }
+      const float na = fmaxf(m_a, mxa), nbm = fmaxf(m_b, mxb);
+      const float al_a = m_a == -INFINITY ? 0.f : exp2f(m_a - na);
+      const float al_b = m_b == -INFINITY ? 0.f : exp2f(m_b - nbm);
+      m_a = na;
+      m_b = nbm;
+      float sa = 0.f, sb = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        sc[j][0] = sc[j][0] == -INFINITY ? 0.f : exp2f(sc[j][0] - na);
+        sc[j][1] = sc[j][1] == -INFINITY ? 0.f : exp2f(sc[j][1] - na);
+        sc[j][2] = sc[j][2] == -INFINITY ? 0.f : exp2f(sc[j][2] - nbm);
+        sc[j][3] = sc[j][3] == -INFINITY ? 0.f : exp2f(sc[j][3] - nbm);
+        sa += sc[j][0] + sc[j][1];
+        sb += sc[j][2] + sc[j][3];
+      }
+      l_a = l_a * al_a + sa;
+      l_b = l_b * al_b + sb;
+#pragma unroll
+      for (int i = 0; i < DN; ++i) {
+        o[i][0] *= al_a;
+        o[i][1] *= al_a;
+        o[i][2] *= al_b;
+        o[i][3] *= al_b;
+      }
+      // O += P . V, 16 keys at a time; P's A fragment is the S fragment of two key tiles
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t ph[4], pl[4];
+        split_pair(sc[2 * kk][0], sc[2 * kk][1], ph[0], pl[0]);
+        split_pair(sc[2 * kk][2], sc[2 * kk][3], ph[1], pl[1]);
+        split_pair(sc[2 * kk + 1][0], sc[2 * kk + 1][1], ph[2], pl[2]);
+        split_pair(sc[2 * kk + 1][2], sc[2 * kk + 1][3], ph[3], pl[3]);
+#pragma unroll
+        for (int dn = 0; dn < DN; dn += 2) {
+          uint32_t b0, b1, b2, b3;  // V rows 16 kk .. 16 kk + 15, dims 8 dn .. 8 dn + 15, transposed
+          ldsm_x4_t(smem_u32(vb + (16 * kk + 8 * ((lane >> 3) & 1) + (lane & 7)) * KSTR + 8 * (dn + (lane >> 4))), b0,
+                    b1, b2, b3);
+          mma16816(o[dn], ph, b0, b1);
+          mma16816(o[dn], pl, b0, b1);
+          mma16816(o[dn + 1], ph, b2, b3);
+          mma16816(o[dn + 1], pl, b2, b3);
+        }
+      }
+    }
+    __syncthreads();  // this slot is read by every warp before the next iteration's copy overwrites it
+  }
+  cp_async_wait<0>();
+#pragma unroll
+  for (int off = 1; off <= 2; off <<= 1) {
+    l_a += __shfl_xor_sync(0xffffffffu, l_a, off);
+    l_b += __shfl_xor_sync(0xffffffffu, l_b, off);
+  }
+  const float ia = l_a > 0.f ? 1.0f / l_a : 0.f, ib = l_b > 0.f ? 1.0f / l_b : 0.f;  // no key: zeros
+  const size_t ob = (size_t)z * a.out_seq_stride + (size_t)h * a.out_head_stride;
+#pragma unroll
+  for (int dn = 0; dn < DN; ++dn) {
+    const int d = 8 * dn + 2 * t4;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int row = half ? rb : ra;
+      if (row >= a.rows) continue;
+      const float inv = half ? ib : ia;
+      const float v0 = o[dn][2 * half] * inv, v1 = o[dn][2 * half + 1] * inv;
+      const size_t off = ob + (size_t)row * a.out_row_stride + d;
+      if (a.out_half) {
+        __half* oh = reinterpret_cast<__half*>(a.out) + off;
+        store_hl(oh, (size_t)a.out_lo_offset, v0);
+        store_hl(oh + 1, (size_t)a.out_lo_offset, v1);
+      } else {
+        a.out[off] = v0;
+        a.out[off + 1] = v1;
+      }
+    }
+  }
+}
+
+template <int HD>
+int launch_pf_mma(const PrefillAttnArgs& a, cudaStream_t s) {
+  constexpr int smem = 4 * MKEYS * (HD + 8) * 2;  // K and V, two stages each
+  static unsigned long long attr_set = 0;          // devices on which the shared-memory limit was raised
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return kCudaError;
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(attr_set & bit)) {
+    if (cudaFuncSetAttribute(prefill_attn_mma_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+        cudaSuccess)
+      return kCudaError;
+    attr_set |= bit;
+  }
+  const dim3 grid((a.rows + MQ - 1) / MQ, a.hq, a.seqs);
+  prefill_attn_mma_kernel<HD><<<grid, 128, smem, s>>>(a);
+  return cudaPeekAtLastError() == cudaSuccess ? kOk : kCudaError;
+}
+
+// The tensor-core form needs fp16 K/V whose rows start on 16-byte boundaries and a q row layout that allows
+// 8-byte loads.
+bool mma_form_ok(const PrefillAttnArgs& a) {
+  if (!a.kv_half || (a.hd != 64 && a.hd != 128)) return false;
+  if ((reinterpret_cast<uintptr_t>(a.k) | reinterpret_cast<uintptr_t>(a.v)) & 15) return false;
+  if ((a.page_stride | a.slot_stride | a.head_stride | a.kv_seq_stride) & 7) return false;
+  if ((reinterpret_cast<uintptr_t>(a.q) & 7) || ((a.q_row_stride | a.q_head_stride | a.q_seq_stride) & 1)) return false;
+  if ((a.out_row_stride | a.out_head_stride | a.out_seq_stride) & 1) return false;
+  return true;
+}
+
 template <typename KV>
 int launch_pf(const PrefillAttnArgs& a, cudaStream_t s) {
   const dim3 grid((a.rows + PF_BQ - 1) / PF_BQ, a.hq, a.seqs);
@@ -195,6 +461,7 @@ int prefill_attention(const PrefillAttnArgs& a, cudaStream_t s) {
   if ((long long)a.max_pages * a.page_size > 0x7fffffffLL) return kUnsupported;
   if (a.hd != 16 && a.hd != 32 && a.hd != 64 && a.hd != 128) return kUnsupported;
   if (a.seqs > 65535 || a.hq > 65535) return kUnsupported;
+  if (mma_form_ok(a)) return a.hd == 64 ? launch_pf_mma<64>(a, s) : launch_pf_mma<128>(a, s);
   return a.kv_half ? launch_pf<__half>(a, s) : launch_pf<float>(a, s);
 }
 
