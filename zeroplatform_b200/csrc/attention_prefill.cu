@@ -16,8 +16,10 @@
 // page pools and a dense [kv batch][sk][d] fp32 tensor (one page of sk slots).  Tokens at or past a row's context
 // length, and pages outside [0, num_pages), contribute nothing.  fp32 arithmetic throughout.
 //
-// Tensor-core form (fp16 K/V, head size 64 or 128: the engine's pools).  One CTA of 4 warps per 64 query rows of a
-// head, each warp 16 rows, keys staged 64 at a time by cp.async into a double-buffered shared-memory ring.  Scores
+// Tensor-core form (fp16 K/V, head size 64 or 128: the engine's pools).  One CTA of 8 warps per 64 query rows of a
+// head: warps 0-3 take 16 rows each over the even 64-key blocks, warps 4-7 the same rows over the odd blocks (the
+// two partial softmaxes merge at the end), keys staged two blocks at a time by cp.async into a double-buffered
+// shared-memory ring.  Scores
 // S = q . K come from mma.sync m16n8k16 with q carried as an fp16 pair (q_hi = fp16(q), q_lo = fp16(q - q_hi)) and
 // K exact in fp16, so S = q_hi K + q_lo K is q . K to ~2^-22; the online softmax runs on the S fragments in fp32
 // (exp2 domain), and P . V again takes P as an fp16 pair against exact fp16 V.  Every product is exact and
@@ -219,21 +221,23 @@ __device__ __forceinline__ void split_pair(float x, float y, uint32_t& hi, uint3
 }
 
 template <int HD>
-__global__ void __launch_bounds__(128) prefill_attn_mma_kernel(PrefillAttnArgs a) {
+__global__ void __launch_bounds__(256) prefill_attn_mma_kernel(PrefillAttnArgs a) {
   constexpr int KSTR = HD + 8;   // halves per staged key row (16-byte pad: ldmatrix rows in distinct banks)
   constexpr int KC = HD / 16;    // 16-wide k-chunks of q . K
   constexpr int DN = HD / 8;     // 8-wide dim tiles of the output
-  constexpr int STAGE = MKEYS * KSTR;  // halves per stage of K (and of V)
-  constexpr int CHUNKS = MKEYS * HD / 8;  // 16-byte pieces per stage of K (and of V)
+  constexpr int STAGE = MKEYS * KSTR;  // halves per block of K (and of V)
+  constexpr int CHUNKS = MKEYS * HD / 8;  // 16-byte pieces per block of K (and of V)
+  constexpr int MERGE = DN * 4 + 4;       // floats a thread of the second key group hands over
   extern __shared__ __align__(128) __half pf_smem[];
-  __half* sK = pf_smem;              // [2][MKEYS][KSTR]
-  __half* sV = pf_smem + 2 * STAGE;  // [2][MKEYS][KSTR]
-  __shared__ int s_wmax[4];
+  __half* sK = pf_smem;              // [2 stages][2 blocks][MKEYS][KSTR]
+  __half* sV = pf_smem + 4 * STAGE;  // the same for V
+  __shared__ int s_wmax[8];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int rg = warp & 3, kp = warp >> 2;  // row group (16 rows), key group (even / odd blocks)
   const int g = lane >> 2, t4 = lane & 3;
   const int tile = gridDim.x - 1 - blockIdx.x;  // longest (latest) tiles first
   const int h = blockIdx.y, z = blockIdx.z;
-  const int rw = tile * MQ + warp * 16;  // the warp's first row
+  const int rw = tile * MQ + rg * 16;  // the warp's first row
   const int ra = rw + g, rb = rw + g + 8;
   const int kvh = h / a.group;
   const int cap = a.max_pages * a.page_size;
@@ -266,24 +270,27 @@ __global__ void __launch_bounds__(128) prefill_attn_mma_kernel(PrefillAttnArgs a
     }
   }
   __syncthreads();
-  const int max_ctx = max(max(s_wmax[0], s_wmax[1]), max(s_wmax[2], s_wmax[3]));
+  int max_ctx = 0;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) max_ctx = max(max_ctx, s_wmax[w]);
   const int nb = (max_ctx + MKEYS - 1) / MKEYS;
+  const int n_it = (nb + 1) / 2;  // iterations: blocks 2 i (key group 0) and 2 i + 1 (key group 1)
   const __half* kz = reinterpret_cast<const __half*>(a.k) + (size_t)z * a.kv_seq_stride + (size_t)kvh * a.head_stride;
   const __half* vz = reinterpret_cast<const __half*>(a.v) + (size_t)z * a.kv_seq_stride + (size_t)kvh * a.head_stride;
   const int32_t* pt = a.page_table + (size_t)z * a.pt_seq_stride;
-  // stage b of K and V into ring slot b & 1: token 64 b + key, 16-byte piece `part` of its row; tokens at or past
-  // the CTA's longest context, or on pages outside [0, num_pages), arrive as zeros
-  auto load_stage = [&](int b) {
-    const int slot = b & 1;
+  // blocks 2 i and 2 i + 1 of K and V into stage i & 1: token 64 b + key, 16-byte piece `part` of its row; tokens at
+  // or past the CTA's longest context, or on pages outside [0, num_pages), arrive as zeros
+  auto load_stage = [&](int i) {
 #pragma unroll
-    for (int c = tid; c < CHUNKS; c += 128) {
-      const int key = c / (HD / 8), part = c % (HD / 8);
-      const int tok = b * MKEYS + key;
+    for (int c = tid; c < 2 * CHUNKS; c += 256) {
+      const int blk = c / CHUNKS, cc = c % CHUNKS;
+      const int key = cc / (HD / 8), part = cc % (HD / 8);
+      const int tok = (2 * i + blk) * MKEYS + key;
       const int page = tok < max_ctx ? pt[tok / a.page_size] : -1;
       const bool ok = page >= 0 && page < a.num_pages;
       const size_t off =
           (size_t)(ok ? page : 0) * a.page_stride + (size_t)(ok ? tok % a.page_size : 0) * a.slot_stride + 8 * part;
-      const int so = slot * STAGE + key * KSTR + 8 * part;
+      const int so = ((i & 1) * 2 + blk) * STAGE + key * KSTR + 8 * part;
       cp_async16(smem_u32(sK + so), kz + off, ok);
       cp_async16(smem_u32(sV + so), vz + off, ok);
     }
@@ -292,16 +299,17 @@ __global__ void __launch_bounds__(128) prefill_attn_mma_kernel(PrefillAttnArgs a
 #pragma unroll
   for (int i = 0; i < DN; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
-  if (nb > 0) load_stage(0);
+  if (n_it > 0) load_stage(0);
   cp_async_commit();
-  for (int b = 0; b < nb; ++b) {
-    if (b + 1 < nb) load_stage(b + 1);  // its slot was last read in block b - 1 (released by that block's barrier)
+  for (int it = 0; it < n_it; ++it) {
+    if (it + 1 < n_it) load_stage(it + 1);  // its slots were last read in iteration it - 1 (released by its barrier)
     cp_async_commit();
-    cp_async_wait<1>();  // stage b has landed (this thread's copies); the barrier makes it every thread's
+    cp_async_wait<1>();  // stage it has landed (this thread's copies); the barrier makes it every thread's
     __syncthreads();
-    if (wmax > b * MKEYS) {  // the warp has at least one key in this block
-      const __half* kb = sK + (b & 1) * STAGE;
-      const __half* vb = sV + (b & 1) * STAGE;
+    const int b = 2 * it + kp;
+    if (b < nb && wmax > b * MKEYS) {  // the warp has at least one key in its block
+      const __half* kb = sK + ((it & 1) * 2 + kp) * STAGE;
+      const __half* vb = sV + ((it & 1) * 2 + kp) * STAGE;
       float sc[8][4];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
@@ -377,13 +385,47 @@ __global__ void __launch_bounds__(128) prefill_attn_mma_kernel(PrefillAttnArgs a
         }
       }
     }
-    __syncthreads();  // this slot is read by every warp before the next iteration's copy overwrites it
+    __syncthreads();  // this stage is read by every warp before a later iteration's copy overwrites it
   }
   cp_async_wait<0>();
 #pragma unroll
   for (int off = 1; off <= 2; off <<= 1) {
     l_a += __shfl_xor_sync(0xffffffffu, l_a, off);
     l_b += __shfl_xor_sync(0xffffffffu, l_b, off);
+  }
+  // the two key groups of a row group merge: group 1 hands (m, l, O) over through shared memory (the key stages
+  // are free: every copy has landed and every warp passed the loop's last barrier)
+  __syncthreads();
+  float* xch = reinterpret_cast<float*>(pf_smem) + (size_t)(rg * 32 + lane) * MERGE;
+  if (kp == 1) {
+    xch[0] = m_a;
+    xch[1] = m_b;
+    xch[2] = l_a;
+    xch[3] = l_b;
+#pragma unroll
+    for (int i = 0; i < DN; ++i) {
+      xch[4 + 4 * i] = o[i][0];
+      xch[5 + 4 * i] = o[i][1];
+      xch[6 + 4 * i] = o[i][2];
+      xch[7 + 4 * i] = o[i][3];
+    }
+  }
+  __syncthreads();
+  if (kp == 1) return;
+  {
+    const float m1a = xch[0], m1b = xch[1], l1a = xch[2], l1b = xch[3];
+    const float Ma = fmaxf(m_a, m1a), Mb = fmaxf(m_b, m1b);
+    const float f0a = m_a == -INFINITY ? 0.f : exp2f(m_a - Ma), f1a = m1a == -INFINITY ? 0.f : exp2f(m1a - Ma);
+    const float f0b = m_b == -INFINITY ? 0.f : exp2f(m_b - Mb), f1b = m1b == -INFINITY ? 0.f : exp2f(m1b - Mb);
+    l_a = l_a * f0a + l1a * f1a;
+    l_b = l_b * f0b + l1b * f1b;
+#pragma unroll
+    for (int i = 0; i < DN; ++i) {
+      o[i][0] = o[i][0] * f0a + xch[4 + 4 * i] * f1a;
+      o[i][1] = o[i][1] * f0a + xch[5 + 4 * i] * f1a;
+      o[i][2] = o[i][2] * f0b + xch[6 + 4 * i] * f1b;
+      o[i][3] = o[i][3] * f0b + xch[7 + 4 * i] * f1b;
+    }
   }
   const float ia = l_a > 0.f ? 1.0f / l_a : 0.f, ib = l_b > 0.f ? 1.0f / l_b : 0.f;  // no key: zeros
   const size_t ob = (size_t)z * a.out_seq_stride + (size_t)h * a.out_head_stride;
@@ -411,7 +453,7 @@ __global__ void __launch_bounds__(128) prefill_attn_mma_kernel(PrefillAttnArgs a
 
 template <int HD>
 int launch_pf_mma(const PrefillAttnArgs& a, cudaStream_t s) {
-  constexpr int smem = 4 * MKEYS * (HD + 8) * 2;  // K and V, two stages each
+  constexpr int smem = 8 * MKEYS * (HD + 8) * 2;  // K and V, two stages of two blocks each
   static unsigned long long attr_set = 0;          // devices on which the shared-memory limit was raised
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return kCudaError;
@@ -423,7 +465,7 @@ int launch_pf_mma(const PrefillAttnArgs& a, cudaStream_t s) {
     attr_set |= bit;
   }
   const dim3 grid((a.rows + MQ - 1) / MQ, a.hq, a.seqs);
-  prefill_attn_mma_kernel<HD><<<grid, 128, smem, s>>>(a);
+  prefill_attn_mma_kernel<HD><<<grid, 256, smem, s>>>(a);
   return cudaPeekAtLastError() == cudaSuccess ? kOk : kCudaError;
 }
 
