@@ -294,12 +294,10 @@ def prefill_gemm_leg(dev, L, iters=20, with_cpu=False, cpu_tokens=64, cpu_s=5.0)
     return out
 
 
-def decode_12l_leg(dev, with_cpu, n_prompt=512, n_new=128):
-    """Small Llama decode workload: 12 layers, d 768, 12 heads x 64, SwiGLU 2048, vocab 32000, Q8_0 from N(0,0.02);
-    512 random prompt ids then 128 greedy tokens (repetition penalty 1.0), 16-token fp16 KV pages."""
+def _model_12l(dev):
+    """The 12-layer d768 model (12 heads x 64, SwiGLU 2048, vocab 32000), Q8_0 from seeded N(0,0.02)."""
     import numpy as np
     import torch
-    from zeroplatform_b200.engine import LlmEngine
     from zeroplatform_b200.ops import quantize
     vocab, dim, layers, heads, ffn = 32000, 768, 12, 12, 2048
     g = torch.Generator(device=dev)
@@ -309,12 +307,71 @@ def decode_12l_leg(dev, with_cpu, n_prompt=512, n_new=128):
         shape = (rows, cols) if n is None else (n, rows, cols)
         return quantize(8, torch.randn(shape, generator=g, device=dev) * 0.02).cpu().numpy()
 
-    m = dict(vocab=vocab, dim=dim, layers=layers, heads=heads, kv_heads=heads, ffn=ffn, context_length=2048, eps=1e-5,
-             rope_base=10000.0, tok_emb=q8(vocab, dim), lm_head=q8(vocab, dim), wq=q8(dim, dim, layers),
-             wk=q8(dim, dim, layers), wv=q8(dim, dim, layers), wo=q8(dim, dim, layers), wgate=q8(ffn, dim, layers),
-             wup=q8(ffn, dim, layers), wdown=q8(dim, ffn, layers),
-             attn_norm=np.ones((layers, dim), np.float32), ffn_norm=np.ones((layers, dim), np.float32),
-             final_norm=np.ones(dim, np.float32))
+    return dict(vocab=vocab, dim=dim, layers=layers, heads=heads, kv_heads=heads, ffn=ffn, context_length=2048,
+                eps=1e-5, rope_base=10000.0, tok_emb=q8(vocab, dim), lm_head=q8(vocab, dim), wq=q8(dim, dim, layers),
+                wk=q8(dim, dim, layers), wv=q8(dim, dim, layers), wo=q8(dim, dim, layers), wgate=q8(ffn, dim, layers),
+                wup=q8(ffn, dim, layers), wdown=q8(dim, ffn, layers),
+                attn_norm=np.ones((layers, dim), np.float32), ffn_norm=np.ones((layers, dim), np.float32),
+                final_norm=np.ones(dim, np.float32))
+
+
+def serve_leg(dev, n_req=32, max_batch=16, n_new=64, seed=21):
+    """Continuous batching on the 12-layer d768 model: n_req requests (prompts of 64-192 random ids, greedy, n_new
+    tokens each) submitted at once to the engine's scheduler (zcu_engine_submit / zcu_engine_serve_step, max_batch
+    rows): requests are admitted as rows free up and every step is one batched decode of all running requests.
+    Against it, the same requests generated one after another (zcu_engine_generate: one kernel per token).  Both
+    timed by the host clock around the whole run (each serve step synchronises), after a warm-up run of the same
+    mix that captures the step graphs of every batch size."""
+    import time
+    import numpy as np
+    from zeroplatform_b200.engine import LlmEngine
+    m = _model_12l(dev)
+    rng = np.random.default_rng(seed)
+    prompts = [rng.integers(0, m["vocab"], int(n)).astype(np.int32) for n in rng.integers(64, 193, n_req)]
+    per_seq = (192 + n_new) // 16 + 2
+    e = LlmEngine(m, total_pages=max_batch * per_seq, page_size=16, max_batch=max_batch, max_pages_per_seq=per_seq,
+                  max_prefill_tokens=192)
+
+    def batched(id0):
+        for i, p in enumerate(prompts):
+            e.submit(id0 + i, p, n_new, temperature=0.0, top_k=1, top_p=1.0, repetition_penalty=1.0)
+        done = toks = steps = 0
+        t0 = time.perf_counter()
+        while done < n_req:
+            steps += 1
+            for _, tok, fin, reason in e.serve_step():
+                toks += int(tok >= 0 and reason != 1)
+                done += int(fin)
+        return toks, steps, time.perf_counter() - t0
+
+    batched(1000)
+    toks_b, steps_b, t_b = batched(2000)
+    for i, p in enumerate(prompts[:2]):  # warm-up of the one-sequence path
+        e.generate_greedy(5000 + i, p, n_new)
+        e.free_sequence(5000 + i)
+    toks_s = 0
+    t0 = time.perf_counter()
+    for i, p in enumerate(prompts):
+        out, _, _ = e.generate_greedy(6000 + i, p, n_new)
+        toks_s += len(out)
+        e.free_sequence(6000 + i)
+    t_s = time.perf_counter() - t0
+    e.close()
+    return {"requests": n_req, "max_batch": max_batch, "new_tokens_per_request": n_new,
+            "prompt_tokens": int(sum(len(p) for p in prompts)), "generated_tokens": toks_b, "serve_steps": steps_b,
+            "tok_s_batched": round(toks_b / t_b, 1), "tok_s_sequential": round(toks_s / t_s, 1),
+            "speedup": round((toks_b / t_b) / (toks_s / t_s), 2), "batched_s": round(t_b, 3),
+            "sequential_s": round(t_s, 3),
+            "timing": "host wall clock around each whole run (prefills included), after a warm-up run"}
+
+
+def decode_12l_leg(dev, with_cpu, n_prompt=512, n_new=128):
+    """Small Llama decode workload: 12 layers, d 768, 12 heads x 64, SwiGLU 2048, vocab 32000, Q8_0 from N(0,0.02);
+    512 random prompt ids then 128 greedy tokens (repetition penalty 1.0), 16-token fp16 KV pages."""
+    import numpy as np
+    from zeroplatform_b200.engine import LlmEngine
+    m = _model_12l(dev)
+    vocab, dim, layers, heads = m["vocab"], m["dim"], m["layers"], m["heads"]
     prompt = np.random.default_rng(5).integers(0, vocab, n_prompt).astype(np.int32)
     e = LlmEngine(m, total_pages=64, page_size=16, max_batch=1, max_pages_per_seq=64, max_prefill_tokens=n_prompt)
     e.generate_greedy(0, prompt, 8)            # warm-up: captures the decode-step graph
@@ -718,6 +775,10 @@ def run_ours(args):
         except Exception as ex:
             extra["decode_12l_d768"] = {"error": str(ex)[:200]}
         try:
+            extra["serve_12l_d768_32req"] = serve_leg(dev)
+        except Exception as ex:
+            extra["serve_12l_d768_32req"] = {"error": str(ex)[:200]}
+        try:
             extra[f"decode_7b_b32_tp{world}"] = decode_7b_leg(dev, rank, world, layers=args.layers,
                                                               n_new=args.new_tokens, with_cpu=with_cpu)
         except Exception as ex:
@@ -800,6 +861,9 @@ def run_leg(args):
     elif args.leg == "decode_12l":
         res = decode_12l_leg(dev, False)
         name = "decode_12l_d768"
+    elif args.leg == "serve":
+        res = serve_leg(dev)
+        name = "serve_12l_d768_32req"
     elif args.leg == "gemm":
         m, n, k = (int(v) for v in args.shape.split(","))
         res = gemm_leg(dev, m, n, k)
@@ -816,8 +880,9 @@ def run_leg(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--leg", choices=["all", "decode_7b", "decode_12l", "moe", "gemm"], default="all",
-                    help="all: the headline and every extra leg; decode_7b: only the 7B tensor-parallel decode; "
+    ap.add_argument("--leg", choices=["all", "decode_7b", "decode_12l", "moe", "gemm", "serve"], default="all",
+                    help="all: the headline and every extra leg; decode_7b: only the 7B tensor-parallel decode; serve: "
+                         "continuous batching on the 12-layer model; "
                          "moe: only the expert-parallel MoE layer; gemm: one GEMM shape (--shape)")
     ap.add_argument("--shape", default="512,11008,4096", help="gemm: M,N,K")
     ap.add_argument("--layers", type=int, default=32, help="decode_7b: decoder layers (32 = the 7B shape)")
@@ -837,7 +902,7 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
-    elif args.leg in ("decode_7b", "decode_12l", "moe", "gemm"):
+    elif args.leg in ("decode_7b", "decode_12l", "moe", "gemm", "serve"):
         run_leg(args)
     else:
         run_ours(args)
