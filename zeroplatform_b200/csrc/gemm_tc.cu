@@ -20,8 +20,8 @@
 //   warp 2      TMA producer: activation tiles (fp16, pre-converted) [BN tokens x 64 k], 128B swizzle
 //   warps 4-11  dequantizers: int8 W tile (shared memory) x fp16 block scales -> fp16 hi / lo planes of q*d,
 //               either in shared memory in the UMMA K-major 128B-swizzled layout (fence.proxy.async before
-//               signalling the MMA warp) or, for tiles of at most 64 tokens, in TMEM (tcgen05.st, one weight row
-//               per lane; the MMA then reads A from TMEM)
+//               signalling the MMA warp) or, for tiles of at most 64 tokens and Q8_0 tiles of 128, in TMEM
+//               (tcgen05.st, one weight row per lane; the MMA then reads A from TMEM)
 //   warps 12-15 epilogue: tcgen05.ld 32 TMEM columns at a time, coalesced fp32 stores of Y (or of the
 //               split-K partials, summed afterwards in split order by splitk_reduce_kernel)
 // The accumulator is double-buffered in TMEM (2 x 2 BN columns: the x_hi and x_lo halves) so the epilogue of
@@ -57,9 +57,9 @@ __host__ __device__ constexpr int w_tile_bytes(int qt) { return qt == 8 ? BM * B
 __host__ __device__ constexpr int w_stage_bytes(int qt) { return w_tile_bytes(qt) + S_TILE_BYTES; }
 __host__ __device__ constexpr int w_row_bytes(int qt) { return w_tile_bytes(qt) / BM; }  // 256 or 128
 constexpr int MAX_SPLITS = 8;               // split-K ranges per output tile at most
-// Tensor-memory A (tile widths BN <= 64 with TMA'd scales): the dequantizers store the fp16 hi / lo planes of
-// each k-stage into TMEM columns after the accumulators (64 columns a stage: 32 hi, 32 lo), so A never
-// occupies shared memory or its bandwidth.  The weight tile then arrives 128B-swizzled (128-byte boxes) so that
+// Tensor-memory A (tile widths BN <= 64, and Q8_0 tiles of BN = 128 with a single accumulator; TMA'd scales):
+// the dequantizers store the fp16 hi / lo planes of each k-stage into TMEM columns after the accumulators (64
+// columns a stage: 32 hi, 32 lo), so A never occupies shared memory or its bandwidth.  The weight tile then arrives 128B-swizzled (128-byte boxes) so that
 // one-row-per-lane reads are conflict free.
 constexpr int TMEM_COLS = 512;
 constexpr int A_TMEM_STAGE_COLS = 64;
@@ -80,6 +80,8 @@ struct GemmParams {
   int splits;       // K ranges per tile (split-K); work units = n_tiles * splits
   int kb_per_split;  // a multiple of W_SUB
   int scale_tma;     // 1: block scales arrive by TMA with their weight tile (K % 256 == 0), 0: loaded per item
+  int acc_bufs;      // TMEM accumulators: 2 (the epilogue of a tile overlaps the next tile's MMAs), or 1 for
+                     // 128-token tiles with A in TMEM (their 2 x 128 accumulator columns leave room for 4 A stages)
 };
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint32_t bar) {
@@ -346,8 +348,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       uint32_t ph = 0;
       int it = 0;
       for (int u = blockIdx.x; u < n_units && !*abort_flag; u += gridDim.x, ++it) {
-        const int acc = it & 1;
-        const uint32_t acc_ph = (uint32_t)(it >> 1) & 1;
+        const int acc = it % p.acc_bufs;
+        const uint32_t acc_ph = (uint32_t)(it / p.acc_bufs) & 1;
         if (!mbar_wait(smem_u32(&tempty[acc]), acc_ph ^ 1, abort_flag, p.status, 2)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * 2 * bn);
@@ -360,8 +362,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           }
           tc_fence_after();
           const uint64_t bd = bdesc0 + (uint64_t)(s * (b_stage_bytes >> 4));
-          if constexpr (AT) {  // A stage s: TMEM columns [4 bn + 64 s, +32) hi, [+32, +64) lo; 8 columns per k16
-            const uint32_t at = tmem_base + (uint32_t)(4 * bn + s * A_TMEM_STAGE_COLS);
+          if constexpr (AT) {  // A stage s: TMEM columns [2 acc_bufs bn + 64 s, +32) hi, [+32, +64) lo; 8 per k16
+            const uint32_t at = tmem_base + (uint32_t)(2 * p.acc_bufs * bn + s * A_TMEM_STAGE_COLS);
 #pragma unroll
             for (int kk = 0; kk < BK / 16; ++kk) {
               umma_f16_ta(d_tmem, at + 8 * kk, bd + 2 * kk, idesc2, (kb != kb0 || kk != 0) ? 1u : 0u);
@@ -454,7 +456,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             }
           }
           const uint32_t ta = tmem_base + ((uint32_t)(32 * (warp & 3)) << 16) +
-                              (uint32_t)(4 * bn + as * A_TMEM_STAGE_COLS + 16 * g);
+                              (uint32_t)(2 * p.acc_bufs * bn + as * A_TMEM_STAGE_COLS + 16 * g);
           tmem_st16(ta, hv);
           tmem_st16(ta + 32, lv);
           tmem_st_wait();
@@ -544,8 +546,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int row_in_tile = quad * 32 + lane;
     int it = 0;
     for (int u = blockIdx.x; u < n_units && !*abort_flag; u += gridDim.x, ++it) {
-      const int acc = it & 1;
-      const uint32_t acc_ph = (uint32_t)(it >> 1) & 1;
+      const int acc = it % p.acc_bufs;
+      const uint32_t acc_ph = (uint32_t)(it / p.acc_bufs) & 1;
       if (!mbar_wait(smem_u32(&tfull[acc]), acc_ph, abort_flag, p.status, 7)) break;
       tc_fence_after();
       const int t = unit_tile(u);
@@ -664,8 +666,9 @@ static void ring_depths(int qt, int bn, int& ab, int& w) {
 
 // Ring depths with A in tensor memory: as many A stages as TMEM holds after the accumulators (at most
 // MAX_STAGES), the weight ring as deep as shared memory allows (2 .. 4 tiles, 6 for the half-size Q4_0 tiles).
+static int acc_bufs_at(int bn) { return bn <= AT_MAX_BN ? 2 : 1; }
 static void ring_depths_at(int qt, int bn, int& ab, int& w) {
-  ab = std::min(MAX_STAGES, (TMEM_COLS - 4 * bn) / A_TMEM_STAGE_COLS);
+  ab = std::min(MAX_STAGES, (TMEM_COLS - 2 * acc_bufs_at(bn) * bn) / A_TMEM_STAGE_COLS);
   w = qt == 8 ? 4 : 6;
   while (w > 2 && SMEM_FIXED + ab * 2 * bn * BK * 2 + w * w_stage_bytes(qt) > SMEM_LIMIT) --w;
 }
@@ -746,7 +749,9 @@ static int launch_gemm(const void* qs, const uint16_t* d, const __half* x_hi, co
   GemmConfig c = choose_config(m, n, k, QT);
   // Block scales [N][K/32] fp16 by TMA, 8 per row per weight tile (needs a 16-byte row pitch: K % 256 == 0).
   const int scale_tma = (k % 256 == 0) ? 1 : 0;
-  const bool at = c.bn <= AT_MAX_BN && scale_tma;  // A in tensor memory
+  // A in tensor memory: tiles of up to 64 tokens (double-buffered accumulators), and 128-token Q8_0 tiles with a
+  // single accumulator (measured: 512 x 11008 x 4096 140.7 -> 123.9 us; Q4_0 tiles of 128 ran 6 % slower)
+  const bool at = (c.bn <= AT_MAX_BN || (c.bn == 128 && QT == 8)) && scale_tma;
   if (at) ring_depths_at(QT, c.bn, c.ab_stages, c.w_stages);
   float* part = reinterpret_cast<float*>(ws + align256((size_t)m * k * 4));
   if (partials) {
@@ -798,6 +803,7 @@ static int launch_gemm(const void* qs, const uint16_t* d, const __half* x_hi, co
   GemmParams p;
   p.d = d;
   p.scale_tma = scale_tma;
+  p.acc_bufs = at ? acc_bufs_at(c.bn) : 2;
   p.y = y;
   p.part = part;
   p.status = status;
