@@ -73,11 +73,11 @@ ZC_API int32_t zcu_gemm_q4_0(const uint8_t* qs, const uint16_t* d, const float* 
 ZC_API int32_t zcu_device_status(int32_t reset);
 
 /* Failure-detection self-test on one GPU (no counterpart in the reference): runs the tensor-parallel all-reduce's
- * reduce kernel against a local receive area of `ranks` (2 .. 8) ranks in which only rank 0 ever publishes its
- * flag, with the kernel's bounded wait shortened to wait_ms (1 .. 5000).  The wait runs out, the kernel records
- * code 21 in its status word and returns, and the context stays usable.  Returns that code (0 would mean the wait
- * never ran out) or a negative status when the test could not run; seen (16 words, may be NULL) receives the
- * kernel's state: [4] the epoch it waited for, [5 ..] the flags it saw. */
+ * reduce kernel against a local receive area of `ranks` (2 .. 8) ranks in which only rank 0 has pushed (its
+ * words carry epoch 1), with the kernel's bounded wait shortened to wait_ms (1 .. 5000).  The wait runs out, the
+ * kernel records code 21 in its status word and returns, and the context stays usable.  Returns that code (0 would
+ * mean the wait never ran out) or a negative status when the test could not run; seen (16 words, may be NULL)
+ * receives the kernel's state: [4] the epoch it waited for, [5 + r] the epoch of rank r's first word. */
 ZC_API int32_t zcu_peer_wait_selftest(int32_t ranks, int32_t wait_ms, uint32_t* seen);
 
 /* Paged decode attention on device buffers -- GqaAttention.Forward (ZeroLlm/src/ZeroLlm.Core/Layers/

@@ -142,10 +142,10 @@ def test_flash_attention_declines_what_it_does_not_run():
 
 
 def test_bounded_peer_wait_runs_out_and_reports():
-    """The tensor-parallel all-reduce's reduce kernel waits (bounded) for every peer's epoch flag.  Here it runs on
-    one GPU against a receive area of 2 (and 8) ranks where no peer ever publishes: the wait must give up after
-    the shortened limit, record code 21 with what it saw (it needed epoch 1; rank 0's flag is 1, the others 0),
-    and return -- and the context must stay usable for the next kernel."""
+    """The tensor-parallel all-reduce's reduce kernel waits (bounded) until every peer's words carry the current
+    epoch.  Here it runs on one GPU against a receive area of 2 (and 8) ranks where no peer ever pushes: the wait
+    must give up after the shortened limit, record code 21 with what it saw (it needed epoch 1; rank 0's words
+    carry 1, the others 0), and return -- and the context must stay usable for the next kernel."""
     import time
     from zeroplatform_b200 import _lib
     from zeroplatform_b200.ops import QuantizedWeight

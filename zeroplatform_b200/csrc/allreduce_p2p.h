@@ -23,9 +23,10 @@ size_t arp_capacity(const P2pAllReduce* a);
 // The epoch and, after a timed-out wait, what it waited for and saw (for error messages).
 std::string arp_describe(const P2pAllReduce* a);
 // Runs the reduce kernel of this all-reduce on one GPU against a local receive area of W ranks in which only rank
-// 0 ever publishes its flag, with a wait limit of wait_ms: the kernel's bounded wait runs out, it records its code
-// (21) and returns.  Returns that code (0 would mean the wait did not run out), or < 0 when the test could not
-// run; seen[0..15] receives the kernel's state words ([4] = the epoch it waited for, [5 ..] the flags it saw).
+// 0 has pushed (its words carry epoch 1), with a wait limit of wait_ms: the kernel's bounded wait runs out, it
+// records its code (21) and returns.  Returns that code (0 would mean the wait did not run out), or < 0 when the
+// test could not run; seen[0..15] receives the kernel's state words ([4] = the epoch it waited for, [5 + r] = the
+// epoch of rank r's first word).
 int arp_wait_selftest(int W, int wait_ms, unsigned int* seen, std::string* err);
 // In-place sum of x[0, n) over all ranks (n <= capacity); two kernels on stream s, graph-capturable.
 int arp_allreduce_sum(P2pAllReduce* a, float* x, size_t n, cudaStream_t s);
