@@ -365,6 +365,21 @@ int linear_push(Engine* E, const DevW& w, int rows) {
   return arp_push_partials(E->arp, part, splits, (size_t)rows * w.n, residual_mode(E) ? E->x : nullptr, E->stream);
 }
 
+// Wgate|Wup on the tensor cores and SwiGLU into E->xh (fp16 hi / lo), with the split-K sum folded into the
+// SwiGLU kernel when `parts`.
+int gate_up_swiglu(Engine* E, int l, int T, bool parts) {
+  if (!parts) {
+    E_RC(linear_h(E, E->wgu[l], E->xh, E->gu, T, 0));
+    return swiglu_rows_h(E->gu, E->xh, T, E->ffn, E->stream);
+  }
+  const DevW& w = E->wgu[l];
+  float* part = nullptr;
+  int splits = 0;
+  E_RC(gemm_q8_0_tc_h_partials(w.qs, w.d, E->xh, E->xh + w.k, 2 * w.k, T, w.n, w.k, E->gemm_ws, E->gemm_ws_bytes,
+                               E->status, E->stream, &part, &splits));
+  return swiglu_rows_h_parts(part, splits, E->xh, T, E->ffn, E->stream);
+}
+
 // The forward pass over T activation rows already embedded in E->x, with tokens' positions in E->pos and
 // page-table rows in E->rows.  Leaves the last row's logits (or every row's when all_logits) of this rank's
 // vocabulary slice in E->logits.
@@ -381,6 +396,9 @@ int forward(Engine* E, int T, bool all_logits) {
   // fused into the kernels around them (linear_push, then arp_reduce_rmsnorm_h, which also writes the next
   // RmsNorm's fp16 operand)
   const bool fused = tc && E->arp && (size_t)T * c.dim <= arp_capacity(E->arp);
+  // decode batches (at most 128 rows, where the GEMM's split-K partials have room in its workspace): the
+  // Wqkv and Wgate|Wup partials go straight into the RoPE / K-V append and SwiGLU kernels
+  const bool parts = tc && T <= 128;
   bool normed = false;  // E->xh already holds the next RmsNorm's output (written by arp_reduce_rmsnorm_h)
   for (int l = 0; l < L; ++l) {
     const float* an = E->attn_norm + (size_t)l * c.dim;
@@ -389,21 +407,33 @@ int forward(Engine* E, int T, bool all_logits) {
       E_RC(gemv_q8_0_rmsnorm(E->wqkv[l].qs, E->wqkv[l].d, E->x, an, c.eps, E->qkv, E->qkv_dim, c.dim, 0, E->stream));
     } else if (tc) {
       if (!normed) E_RC(rmsnorm_h(E->x, an, E->xh, T, c.dim, c.eps, E->stream));
-      E_RC(linear_h(E, E->wqkv[l], E->xh, E->qkv, T, 0));
+      if (parts) {  // the split-K sum is folded into the RoPE / K-V append kernel
+        float* part = nullptr;
+        int splits = 0;
+        const DevW& w = E->wqkv[l];
+        E_RC(gemm_q8_0_tc_h_partials(w.qs, w.d, E->xh, E->xh + w.k, 2 * w.k, T, w.n, w.k, E->gemm_ws,
+                                     E->gemm_ws_bytes, E->status, E->stream, &part, &splits));
+        E_RC(rope_append_kv_parts(part, splits, E->qkv, T, E->hq, E->hkv, E->hd, E->pos, E->rows, E->page_table,
+                                  c.max_pages_per_seq, c.page_size, E->cos_t, E->sin_t, E->max_pos,
+                                  E->kpool + (size_t)l * E->layer_pool_elems,
+                                  E->vpool + (size_t)l * E->layer_pool_elems, E->stream));
+      } else {
+        E_RC(linear_h(E, E->wqkv[l], E->xh, E->qkv, T, 0));
+      }
     } else {
       E_RC(rmsnorm(E->x, an, E->xn, T, c.dim, c.eps, E->stream));
       E_RC(linear(E, E->wqkv[l], E->xn, E->qkv, T, 0));
     }
-    E_RC(rope_append_kv(E->qkv, T, E->hq, E->hkv, E->hd, E->pos, E->rows, E->page_table, c.max_pages_per_seq,
-                        c.page_size, E->cos_t, E->sin_t, E->max_pos, E->kpool + (size_t)l * E->layer_pool_elems,
-                        E->vpool + (size_t)l * E->layer_pool_elems, E->stream));
+    if (!(tc && parts))
+      E_RC(rope_append_kv(E->qkv, T, E->hq, E->hkv, E->hd, E->pos, E->rows, E->page_table, c.max_pages_per_seq,
+                          c.page_size, E->cos_t, E->sin_t, E->max_pos, E->kpool + (size_t)l * E->layer_pool_elems,
+                          E->vpool + (size_t)l * E->layer_pool_elems, E->stream));
     const int32_t* ctx = (c.reference_causal_quirk && l != L - 1) ? E->ctx_ex : E->ctx_in;
     E_RC(attention(E, l, T, ctx, tc));
     if (fused) {
       E_RC(linear_push(E, E->wo[l], T));  // x += Wo . attn, summed over ranks
       E_RC(arp_reduce_rmsnorm_h(E->arp, E->x, fn, c.eps, E->xh, T, c.dim, E->stream));
-      E_RC(linear_h(E, E->wgu[l], E->xh, E->gu, T, 0));
-      E_RC(swiglu_rows_h(E->gu, E->xh, T, E->ffn, E->stream));
+      E_RC(gate_up_swiglu(E, l, T, parts));
       E_RC(linear_push(E, E->wdown[l], T));  // x += Wdown . s, summed over ranks
       const float* next_norm = l + 1 < L ? E->attn_norm + (size_t)(l + 1) * c.dim : E->final_norm;
       E_RC(arp_reduce_rmsnorm_h(E->arp, E->x, next_norm, c.eps, E->xh, T, c.dim, E->stream));
@@ -420,8 +450,7 @@ int forward(Engine* E, int T, bool all_logits) {
       E_RC(gemv_q8_0_swiglu(E->wdown[l].qs, E->wdown[l].d, E->gu, E->x, c.dim, E->ffn, acc, E->stream));
     } else if (tc) {
       E_RC(rmsnorm_h(E->x, fn, E->xh, T, c.dim, c.eps, E->stream));
-      E_RC(linear_h(E, E->wgu[l], E->xh, E->gu, T, 0));
-      E_RC(swiglu_rows_h(E->gu, E->xh, T, E->ffn, E->stream));
+      E_RC(gate_up_swiglu(E, l, T, parts));
       E_RC(linear_h(E, E->wdown[l], E->xh, E->x, T, acc));
     } else {
       E_RC(rmsnorm(E->x, fn, E->xn, T, c.dim, c.eps, E->stream));

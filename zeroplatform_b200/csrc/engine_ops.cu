@@ -14,7 +14,18 @@ namespace zc {
 
 namespace {
 
-__global__ void rope_append_kernel(float* __restrict__ qkv, int T, int hq, int hkv, int hd,
+// Element e of a projection's output: qkv[e] itself, or (part != nullptr) the sum of the GEMM's split-K partials
+// part[s * stride + e] in split order -- the order splitk_reduce_kernel adds them in, so the values are the same.
+__device__ __forceinline__ float split_sum(const float* __restrict__ y, const float* __restrict__ part, int splits,
+                                           size_t stride, size_t e) {
+  if (!part) return y[e];
+  float v = part[e];
+  for (int s = 1; s < splits; ++s) v += part[(size_t)s * stride + e];
+  return v;
+}
+
+__global__ void rope_append_kernel(float* __restrict__ qkv, const float* __restrict__ part, int splits, size_t stride,
+                                   int T, int hq, int hkv, int hd,
                                    const int32_t* __restrict__ pos, const int32_t* __restrict__ rows,
                                    const int32_t* __restrict__ page_table, int max_pages, int page_size,
                                    const float* __restrict__ cos_t, const float* __restrict__ sin_t, int max_pos,
@@ -33,7 +44,8 @@ __global__ void rope_append_kernel(float* __restrict__ qkv, int T, int hq, int h
     const int ps = pos[t];
     float* row = qkv + (size_t)t * row_len;
     float* v = row + (size_t)h * hd + 2 * p;  // q, k and v heads are consecutive in the row
-    float x0 = v[0], x1 = v[1];
+    const size_t e = (size_t)(v - qkv);
+    float x0 = split_sum(qkv, part, splits, stride, e), x1 = split_sum(qkv, part, splits, stride, e + 1);
     if (h < hq + hkv) {  // rotate q and k
       const int pc = min(max(ps, 0), max_pos - 1);
       const float c = cos_t[(size_t)pc * half + p], s = sin_t[(size_t)pc * half + p];
@@ -46,6 +58,10 @@ __global__ void rope_append_kernel(float* __restrict__ qkv, int T, int hq, int h
         v[1] = x1;
         continue;
       }
+    }
+    if (part) {  // the row holds the projection (v unrotated) as the separate reduction would have left it
+      v[0] = x0;
+      v[1] = x1;
     }
     // k or v head: append to the page pool
     const int lp = ps / page_size;
@@ -64,14 +80,15 @@ __global__ void rope_append_kernel(float* __restrict__ qkv, int T, int hq, int h
 }
 
 template <typename OutT>
-__global__ void swiglu_rows_kernel(const float* __restrict__ gu, OutT* __restrict__ out, int T, int ffn) {
+__global__ void swiglu_rows_kernel(const float* __restrict__ gu, const float* __restrict__ part, int splits,
+                                   size_t stride, OutT* __restrict__ out, int T, int ffn) {
   pdl_trigger();
   pdl_wait();
   const size_t total = (size_t)T * ffn;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const int t = (int)(i / ffn), j = (int)(i % ffn);
-    const float g = gu[(size_t)t * 2 * ffn + j];
-    const float u = gu[(size_t)t * 2 * ffn + ffn + j];
+    const float g = split_sum(gu, part, splits, stride, (size_t)t * 2 * ffn + j);
+    const float u = split_sum(gu, part, splits, stride, (size_t)t * 2 * ffn + ffn + j);
     const float sg = 1.0f / (1.0f + expf(-g));
     constexpr int kPlanes = sizeof(OutT) == 2 ? 2 : 1;  // __half: rows [hi ffn | lo ffn]
     store_act(out + (size_t)t * ffn * kPlanes + j, (size_t)ffn, __fmul_rn(__fmul_rn(g, sg), u));
@@ -245,8 +262,26 @@ int rope_append_kv(float* qkv, int T, int hq, int hkv, int hd, const int32_t* po
   if (!qkv || !pos || !rows || !page_table || !cos_t || !sin_t || !k_pool || !v_pool || (hd & 1)) return kBadArgument;
   if (T <= 0) return kOk;
   const size_t n = (size_t)T * (hq + 2 * hkv) * (hd / 2);
-  return launch_pdl(rope_append_kernel, dim3(grid_for(n, 256)), dim3(256), 0, s, qkv, T, hq, hkv, hd, pos, rows,
-                    page_table, max_pages, page_size, cos_t, sin_t, max_pos, k_pool, v_pool) == cudaSuccess
+  return launch_pdl(rope_append_kernel, dim3(grid_for(n, 256)), dim3(256), 0, s, qkv, (const float*)nullptr, 1,
+                    (size_t)0, T, hq, hkv, hd, pos, rows, page_table, max_pages, page_size, cos_t, sin_t, max_pos,
+                    k_pool, v_pool) == cudaSuccess
+             ? kOk
+             : kCudaError;
+}
+
+int rope_append_kv_parts(const float* part, int splits, float* qkv, int T, int hq, int hkv, int hd,
+                         const int32_t* pos, const int32_t* rows, const int32_t* page_table, int max_pages,
+                         int page_size, const float* cos_t, const float* sin_t, int max_pos, __half* k_pool,
+                         __half* v_pool, cudaStream_t s) {
+  if (!part || splits < 1 || !qkv || !pos || !rows || !page_table || !cos_t || !sin_t || !k_pool || !v_pool ||
+      (hd & 1))
+    return kBadArgument;
+  if (T <= 0) return kOk;
+  const size_t n = (size_t)T * (hq + 2 * hkv) * (hd / 2);
+  const size_t stride = (size_t)T * (hq + 2 * hkv) * hd;
+  return launch_pdl(rope_append_kernel, dim3(grid_for(n, 256)), dim3(256), 0, s, qkv, part, splits, stride, T, hq,
+                    hkv, hd, pos, rows, page_table, max_pages, page_size, cos_t, sin_t, max_pos, k_pool,
+                    v_pool) == cudaSuccess
              ? kOk
              : kCudaError;
 }
@@ -254,8 +289,8 @@ int rope_append_kv(float* qkv, int T, int hq, int hkv, int hd, const int32_t* po
 int swiglu_rows(const float* gu, float* out, int T, int ffn, cudaStream_t s) {
   if (!gu || !out) return kBadArgument;
   if (T <= 0) return kOk;
-  return launch_pdl(swiglu_rows_kernel<float>, dim3(grid_for((size_t)T * ffn, 256)), dim3(256), 0, s, gu, out, T,
-                    ffn) == cudaSuccess
+  return launch_pdl(swiglu_rows_kernel<float>, dim3(grid_for((size_t)T * ffn, 256)), dim3(256), 0, s, gu,
+                    (const float*)nullptr, 1, (size_t)0, out, T, ffn) == cudaSuccess
              ? kOk
              : kCudaError;
 }
@@ -263,8 +298,17 @@ int swiglu_rows(const float* gu, float* out, int T, int ffn, cudaStream_t s) {
 int swiglu_rows_h(const float* gu, __half* out, int T, int ffn, cudaStream_t s) {
   if (!gu || !out) return kBadArgument;
   if (T <= 0) return kOk;
-  return launch_pdl(swiglu_rows_kernel<__half>, dim3(grid_for((size_t)T * ffn, 256)), dim3(256), 0, s, gu, out, T,
-                    ffn) == cudaSuccess
+  return launch_pdl(swiglu_rows_kernel<__half>, dim3(grid_for((size_t)T * ffn, 256)), dim3(256), 0, s, gu,
+                    (const float*)nullptr, 1, (size_t)0, out, T, ffn) == cudaSuccess
+             ? kOk
+             : kCudaError;
+}
+
+int swiglu_rows_h_parts(const float* part, int splits, __half* out, int T, int ffn, cudaStream_t s) {
+  if (!part || splits < 1 || !out) return kBadArgument;
+  if (T <= 0) return kOk;
+  return launch_pdl(swiglu_rows_kernel<__half>, dim3(grid_for((size_t)T * ffn, 256)), dim3(256), 0, s, part, part,
+                    splits, (size_t)T * 2 * ffn, out, T, ffn) == cudaSuccess
              ? kOk
              : kCudaError;
 }

@@ -140,6 +140,14 @@ int rope_append_kv(float* qkv, int T, int hq, int hkv, int hd, const int32_t* po
 // out[t][i] = SwiGLU(gu[t][i], gu[t][ffn + i])
 int swiglu_rows(const float* gu, float* out, int T, int ffn, cudaStream_t s);
 int swiglu_rows_h(const float* gu, __half* out, int T, int ffn, cudaStream_t s);  // out [T][hi ffn | lo ffn]
+// The same two steps fed by a GEMM's split-K partials part[splits][T][row] (summed in split order, as the
+// separate reduction does) instead of its reduced output: one kernel instead of two.  rope_append_kv_parts also
+// leaves the reduced rows (q and k rotated) in qkv.
+int rope_append_kv_parts(const float* part, int splits, float* qkv, int T, int hq, int hkv, int hd,
+                         const int32_t* pos, const int32_t* rows, const int32_t* page_table, int max_pages,
+                         int page_size, const float* cos_t, const float* sin_t, int max_pos, __half* k_pool,
+                         __half* v_pool, cudaStream_t s);
+int swiglu_rows_h_parts(const float* part, int splits, __half* out, int T, int ffn, cudaStream_t s);
 // LlmSampler greedy branch per row: repetition penalty over past[row][0:past_len[row]] then argmax
 // (first index wins ties).  penalty <= 1 disables the penalty.  out[row] = token.
 int greedy_sample(float* logits, int rows, int vocab, const int32_t* past, const int32_t* past_len, int past_cap,
