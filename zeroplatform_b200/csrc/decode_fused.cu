@@ -63,17 +63,23 @@ __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
 }
 
 __device__ __forceinline__ int4 ldcg4(const void* p) { return __ldcg(reinterpret_cast<const int4*>(p)); }
+
+// One arrival with release semantics at GPU scope: after the CTA's __syncthreads, every write the CTA made
+// before it is visible to a thread that observes the count with ld.acquire.gpu (no separate full fence).
+__device__ __forceinline__ void red_release_gpu(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ float ldcg(const float* p) { return __ldcg(p); }
 
-// Grid barrier number k (1, 2, ...): ctl[0] counts arrivals; one thread per CTA adds its arrival and polls the
-// count (acquire) until it reaches k * grid.  Returns false when the wait ran out or another CTA gave up (ctl[1]).
+// Grid barrier number k (1, 2, ...): ctl[0] counts arrivals; one thread per CTA adds its arrival (release, after
+// the CTA's __syncthreads) and polls the count (acquire) until it reaches k * grid; the closing __syncthreads
+// passes the acquired view on to the CTA.  Returns false when the wait ran out or another CTA gave up (ctl[1]).
 __device__ __forceinline__ bool grid_sync(unsigned* ctl, unsigned& k, int* status, volatile int* sh_ok) {
   __syncthreads();
   ++k;
   if (threadIdx.x == 0) {
     int ok = 1;
-    __threadfence();
-    atomicAdd(ctl, 1u);
+    red_release_gpu(ctl, 1u);
     const unsigned target = k * gridDim.x;
     const uint64_t t0 = global_ns();
     uint32_t polls = 0;
@@ -91,7 +97,6 @@ __device__ __forceinline__ bool grid_sync(unsigned* ctl, unsigned& k, int* statu
         }
       }
     }
-    __threadfence();
     *sh_ok = ok;
   }
   __syncthreads();
@@ -612,12 +617,29 @@ __global__ void __launch_bounds__(FS_THREADS, 1) fused_step_kernel(FusedStepArgs
         part[0] = m;
         part[1] = lsum;
       }
+      // this split's Wo items (row, 16-column chunk of head h): the first batch's loads go out before the wait,
+      // since the weights do not depend on the attention
+      const int cpr = a.hd / 16, kb = a.q_dim / QK;
+      const int rw0 = (int)((long long)a.dim * s / S), rw1 = (int)((long long)a.dim * (s + 1) / S);
+      const int items = (rw1 - rw0) * cpr;
+      int4 w[8];
+      float sc[8];
+      auto load_wo = [&](int it0) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int it = it0 + j * FS_THREADS + tid;
+          const int row = rw0 + it / cpr, c = it % cpr;
+          const bool ok = it < items;
+          w[j] = ok ? ld_stream_v4(W.o_qs + (size_t)row * a.q_dim + (size_t)h * a.hd + c * 16) : make_int4(0, 0, 0, 0);
+          sc[j] = ok ? h2f(__ldg(W.o_d + (size_t)row * kb + (size_t)h * (a.hd / QK) + (c >> 1))) : 0.f;
+        }
+      };
+      load_wo(0);
       // every split of head h waits (bounded) for the head's S partials -- all CTAs of a cooperative launch are
       // resident, so the wait ends -- then merges them and computes its share of the head's Wo rows
-      __threadfence();
       __syncthreads();
       if (tid == 0) {
-        atomicAdd(a.ctl + 3 + h, 1u);
+        red_release_gpu(a.ctl + 3 + h, 1u);
         const unsigned want = (unsigned)S * (unsigned)(l + 1);
         const uint64_t tw0 = global_ns();
         uint32_t polls = 0;
@@ -631,7 +653,6 @@ __global__ void __launch_bounds__(FS_THREADS, 1) fused_step_kernel(FusedStepArgs
             break;
           }
         }
-        __threadfence();
         sh_last = ok;
       }
       __syncthreads();
@@ -658,20 +679,8 @@ __global__ void __launch_bounds__(FS_THREADS, 1) fused_step_kernel(FusedStepArgs
       __syncthreads();
       // P[h][row] = Wo[row, head h's hd columns] . attn_h for this split's rows: items (row, 16-column chunk), a
       // batch's loads all in flight; the cpr chunks of a row are adjacent lanes and meet in a shuffle reduction
-      const int cpr = a.hd / 16, kb = a.q_dim / QK;
-      const int rw0 = (int)((long long)a.dim * s / S), rw1 = (int)((long long)a.dim * (s + 1) / S);
-      const int items = (rw1 - rw0) * cpr;
       for (int it0 = 0; it0 < items; it0 += 8 * FS_THREADS) {
-        int4 w[8];
-        float sc[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int it = it0 + j * FS_THREADS + tid;
-          const int row = rw0 + it / cpr, c = it % cpr;
-          const bool ok = it < items;
-          w[j] = ok ? ld_stream_v4(W.o_qs + (size_t)row * a.q_dim + (size_t)h * a.hd + c * 16) : make_int4(0, 0, 0, 0);
-          sc[j] = ok ? h2f(__ldg(W.o_d + (size_t)row * kb + (size_t)h * (a.hd / QK) + (c >> 1))) : 0.f;
-        }
+        if (it0 > 0) load_wo(it0);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const int it = it0 + j * FS_THREADS + tid;
