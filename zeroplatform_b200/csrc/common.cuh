@@ -19,7 +19,7 @@ enum Status : int {
   kNotHandled = -1,      // caller should run its own (managed) path
   kBadArgument = -2,     // sizes / alignment / null pointers
   kCudaError = -3,       // a CUDA runtime call failed; details in zc_cuda_last_error()
-  kUnsupported = -4,     // a shape this build does not cover
+  kUnsupported = -4,     // a shape this library does not cover
   kOutOfMemory = -5,     // device allocation failed
   kTooLarge = -6,        // exceeds a fixed-capacity buffer
 };
