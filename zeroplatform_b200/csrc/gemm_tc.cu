@@ -80,9 +80,19 @@ struct GemmParams {
   int splits;       // K ranges per tile (split-K); work units = n_tiles * splits
   int kb_per_split;  // a multiple of W_SUB
   int scale_tma;     // 1: block scales arrive by TMA with their weight tile (K % 256 == 0), 0: loaded per item
+  int x_merged;      // 1: x_map is 3-D (k, token, hi / lo plane): one TMA box brings both activation tiles
   int acc_bufs;      // TMEM accumulators: 2 (the epilogue of a tile overlaps the next tile's MMAs), or 1 for
                      // 128-token tiles with A in TMEM (their 2 x 128 accumulator columns leave room for 4 A stages)
 };
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::
+          "r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
+      : "memory");
+}
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint32_t bar) {
   asm volatile(
@@ -332,9 +342,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         for (int kb = unit_kb0(u); kb < unit_kb1(u); ++kb) {
           if (!mbar_wait(smem_u32(&ab_empty[s]), ph ^ 1, abort_flag, p.status, 6)) break;
           mbar_arrive_tx(smem_u32(&ab_full[s]), (uint32_t)b_stage_bytes);
-          tma_load_2d(smem_u32(b_st + s * b_stage_bytes), &x_map, kb * BK, tok0, smem_u32(&ab_full[s]));
-          tma_load_2d(smem_u32(b_st + s * b_stage_bytes + b_tile_bytes), &xl_map, kb * BK, tok0,
-                      smem_u32(&ab_full[s]));
+          if (p.x_merged) {  // [plane][token][64 k]: the hi tile, then the lo tile, in one instruction
+            tma_load_3d(smem_u32(b_st + s * b_stage_bytes), &x_map, kb * BK, tok0, 0, smem_u32(&ab_full[s]));
+          } else {
+            tma_load_2d(smem_u32(b_st + s * b_stage_bytes), &x_map, kb * BK, tok0, smem_u32(&ab_full[s]));
+            tma_load_2d(smem_u32(b_st + s * b_stage_bytes + b_tile_bytes), &xl_map, kb * BK, tok0,
+                        smem_u32(&ab_full[s]));
+          }
           if (++s == AST) {
             s = 0;
             ph ^= 1;
@@ -782,6 +796,27 @@ static int launch_gemm(const void* qs, const uint16_t* d, const __half* x_hi, co
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return kCudaError;
   }
+  // The hi and lo tiles of a stage as one 3-D box (k, token, plane) when the lo values sit a whole number of
+  // 16-byte units after the hi ones: one TMA instruction per stage instead of two (each instruction costs the
+  // issuing SM a few hundred cycles whatever its size).  Shared memory receives [plane][token][64 k], the layout
+  // of the two separate tiles.
+  int x_merged = 0;
+  CUtensorMap xmap3;
+  {
+    const long long off = (long long)(x_lo - x_hi);  // elements from a hi value to its lo value
+    if (off > 0 && (off * 2) % 16 == 0) {
+      cuuint64_t gdim[3] = {(cuuint64_t)k, (cuuint64_t)m, 2};
+      cuuint64_t gstride[2] = {(cuuint64_t)ldx * 2, (cuuint64_t)off * 2};
+      cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)c.bn, 2};
+      cuuint32_t estride[3] = {1, 1, 1};
+      if (enc(&xmap3, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half*>(x_hi), gdim, gstride, box, estride,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS) {
+        xmap = xmap3;
+        x_merged = 1;
+      }
+    }
+  }
   {
     // weight tiles: whole 256- (Q8_0) or 128-byte (Q4_0) rows unswizzled, or with A in TMEM 128-byte boxes
     // with the 128B swizzle (a Q8_0 tile is then two boxes)
@@ -811,6 +846,7 @@ static int launch_gemm(const void* qs, const uint16_t* d, const __half* x_hi, co
   GemmParams p;
   p.d = d;
   p.scale_tma = scale_tma;
+  p.x_merged = x_merged;
   p.acc_bufs = at ? acc_bufs_at(c.bn) : 2;
   p.y = y;
   p.part = part;
