@@ -106,8 +106,8 @@ ZC_API int32_t zcu_paged_attention(const float* q, const void* k_pool, const voi
  * the split-K scratch is a fixed 1 MiB array inside the library (held by every GPU that loads it until the
  * process exits), so shapes needing more than 8,192 arrival counters (batch * hq) or 253,952 partial floats
  * (batch * hq * splits * (hd + 2)) return -6 with a message in zc_cuda_last_error().  It never calls
- * cudaMalloc or cudaFree.  The first call on a device looks the array up (cudaGetSymbolAddress): make it
- * before any stream capture.  All calls on a device share the array: calls whose kernels overlap on the GPU
+ * cudaMalloc or cudaFree.  The first call on a device looks the array's address up (cudaGetSymbolAddress) and
+ * caches it.  All calls on a device share the array: calls whose kernels overlap on the GPU
  * race (calls on one stream are ordered); each call clears the counters it uses before launching. */
 ZC_API int32_t zcu_paged_attention_noalloc(const float* q, const void* k_pool, const void* v_pool, int32_t kv_dtype,
                                            const int32_t* page_table, const int32_t* ctx_len, float* out,

@@ -18,7 +18,7 @@
 //   * the array keeps what the last call left; the counters must start at zero, so each call clears them
 //     (cudaMemsetAsync on the same stream) before its launch.
 // Set-up: the first call on each device looks the array's device address up with cudaGetSymbolAddress
-// (with that device current) and caches it; make that first call before capturing a stream into a graph.
+// (with that device current) and caches it.
 // Nothing in this file calls cudaMalloc, cudaFree or an allocating library routine.
 
 #include <cuda_runtime.h>
